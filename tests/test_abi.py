@@ -1,0 +1,64 @@
+"""The C ABI surface without a GPU: the library loads, exports every function
+include/xpu_cuda.h declares, and rejects bad arguments on the host with a
+status code and a message (no device work is queued for those calls)."""
+
+import ctypes
+import subprocess
+
+import pytest
+
+from xpu_playground_b200 import _lib
+
+
+def test_library_loads_and_reports_abi_version():
+    lib = _lib.load()
+    assert lib.xpu_abi_version() >= 1
+
+
+def test_every_declared_function_is_exported():
+    declared = _lib.declared_functions()
+    assert "xpu_gemv" in declared and "xpu_qwen_attention" in declared
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    missing = [name for name in declared if name not in exported]
+    assert not missing, f"declared but not exported: {missing}"
+    # and the Python binding knows every declared function's signature
+    assert not [n for n in declared if n not in _lib.SIGNATURES]
+
+
+def test_signatures_cover_only_declared_functions():
+    declared = set(_lib.declared_functions())
+    assert set(_lib.SIGNATURES) <= declared
+
+
+@pytest.mark.parametrize("call", [
+    lambda L: L.xpu_gemv(0, None, None, None, 4, 4, None),
+    lambda L: L.xpu_gemv(7, 1, 1, 1, 4, 4, None),
+    lambda L: L.xpu_gemv(0, 1, 1, 1, 0, 4, None),
+    lambda L: L.xpu_qwen_rms_norm(None, None, None, 8, 1e-6, None),
+    lambda L: L.xpu_qwen_qkv_rope_cache(*([1] * 9), 0, 1, 30, 8, None),
+    lambda L: L.xpu_qwen_attention(1, 1, 1, 1, 10, 32, 8, 16, 8, None),
+    lambda L: L.xpu_qwen_attention(1, 1, 1, 1, 0, 32, 8, None, 0, None),
+    lambda L: L.xpu_qwen_argmax(None, None, 5, None),
+])
+def test_invalid_arguments_fail_on_host(call):
+    L = _lib.load()
+    status = call(L)
+    assert status in (_lib.XPU_ERR_INVALID, _lib.XPU_ERR_UNSUPPORTED)
+    assert _lib.last_error()
+
+
+def test_attention_group_sizes():
+    L = _lib.load()
+    # 12 query heads over 8 kv heads is not a whole group -> invalid
+    assert L.xpu_qwen_attention(16, 16, 16, 16, 0, 12, 8, 16, 1 << 20, None) == _lib.XPU_ERR_INVALID
+    # group of 3 is rejected as unsupported before any launch
+    assert L.xpu_qwen_attention(16, 16, 16, 16, 0, 24, 8, 16, 1 << 20, None) == _lib.XPU_ERR_UNSUPPORTED
+    assert L.xpu_qwen_attention_workspace_size(32, 128) == 32 * 1 * 130 * 4
+    assert L.xpu_qwen_attention_workspace_size(32, 129) == 32 * 2 * 130 * 4
+
+
+def test_check_raises_with_message():
+    with pytest.raises(_lib.XpuError, match="XPU_ERR_INVALID"):
+        _lib.call("xpu_gemv", 0, None, None, None, 1, 1, None)

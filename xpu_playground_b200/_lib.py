@@ -1,0 +1,93 @@
+"""ctypes binding of libxpu_cuda.so (the C ABI declared in include/xpu_cuda.h).
+
+The library is loaded from this package's lib/ directory, where
+``python -m xpu_playground_b200.build`` puts it. There is no fallback: if the
+library is missing, importing a kernel wrapper raises ``XpuLibraryMissing``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "lib" / "libxpu_cuda.so"
+HEADER = PKG.parent / "include" / "xpu_cuda.h"
+
+XPU_OK, XPU_ERR_INVALID, XPU_ERR_CUDA, XPU_ERR_UNSUPPORTED = 0, 1, 2, 3
+XPU_ERR_TIMEOUT, XPU_ERR_NONFINITE, XPU_ERR_NO_MEMORY = 4, 5, 6
+XPU_BF16, XPU_FP16 = 0, 1
+
+STATUS_NAMES = {0: "XPU_OK", 1: "XPU_ERR_INVALID", 2: "XPU_ERR_CUDA", 3: "XPU_ERR_UNSUPPORTED",
+                4: "XPU_ERR_TIMEOUT", 5: "XPU_ERR_NONFINITE", 6: "XPU_ERR_NO_MEMORY"}
+
+
+class XpuLibraryMissing(ImportError):
+    pass
+
+
+class XpuError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+vp, sz = ctypes.c_void_p, ctypes.c_size_t
+u32, u64, i32, f32, f64 = ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int, ctypes.c_float, ctypes.c_double
+
+# name -> (restype, argtypes). Keep in step with include/xpu_cuda.h.
+SIGNATURES: dict[str, tuple] = {
+    "xpu_last_error": (ctypes.c_char_p, []),
+    "xpu_abi_version": (i32, []),
+    "xpu_gemv": (i32, [i32, vp, vp, vp, u32, u32, vp]),
+    "xpu_qwen_embedding": (i32, [vp, vp, u32, u32, vp]),
+    "xpu_qwen_rms_norm": (i32, [vp, vp, vp, u32, f32, vp]),
+    "xpu_qwen_gemv": (i32, [vp, vp, vp, u32, u32, vp]),
+    "xpu_qwen_qkv_rope_cache": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, vp]),
+    "xpu_qwen_attention_workspace_size": (sz, [u32, u32]),
+    "xpu_qwen_attention": (i32, [vp, vp, vp, vp, u32, u32, u32, vp, sz, vp]),
+    "xpu_qwen_add": (i32, [vp, vp, u32, vp]),
+    "xpu_qwen_silu_multiply": (i32, [vp, vp, u32, vp]),
+    "xpu_qwen_argmax": (i32, [vp, vp, u32, vp]),
+}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load libxpu_cuda.so once and attach the C signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise XpuLibraryMissing(
+            f"{LIB_PATH} is missing: build it with `python -m xpu_playground_b200.build` "
+            "(there is no CPU fallback)")
+    lib = ctypes.CDLL(str(LIB_PATH), mode=ctypes.RTLD_GLOBAL)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype, fn.argtypes = res, args
+    _lib = lib
+    return lib
+
+
+def last_error() -> str:
+    return load().xpu_last_error().decode()
+
+
+def check(status: int) -> None:
+    if status != XPU_OK:
+        raise XpuError(status, last_error())
+
+
+def call(name: str, *args) -> None:
+    """Call a status-returning entry point and raise XpuError on failure."""
+    check(getattr(load(), name)(*args))
+
+
+def declared_functions(header: Path = HEADER) -> list[str]:
+    """Names of the functions include/xpu_cuda.h declares."""
+    text = header.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(xpu_\w+|run_\w+)\s*\(", text)))

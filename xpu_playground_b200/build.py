@@ -1,0 +1,124 @@
+"""Build recipe for libxpu_cuda.so and the C++ host binaries (in-tree).
+
+Everything is compiled for sm_100a only:
+    nvcc -gencode arch=compute_100a,code=sm_100a -lineinfo -O3 ...
+Objects go to xpu_playground_b200/_build/, the shared library to
+xpu_playground_b200/lib/ and the CLI/test binaries to xpu_playground_b200/bin/.
+A target is rebuilt when any source or header it may include is newer.
+
+    python -m xpu_playground_b200.build          # build everything
+    python -m xpu_playground_b200.build --clean  # remove the outputs first
+"""
+
+from __future__ import annotations
+
+import argparse
+import concurrent.futures
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+HOST = PKG / "host"
+INCLUDE = ROOT / "include"
+BUILD = PKG / "_build"
+LIB_DIR = PKG / "lib"
+BIN_DIR = PKG / "bin"
+LIB = LIB_DIR / "libxpu_cuda.so"
+
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+CXX = os.environ.get("CXX", "g++")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + [
+    "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
+    "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
+    f"-I{INCLUDE}", f"-I{CSRC}",
+]
+CXX_FLAGS = ["-O2", "-std=c++17", "-Wall", "-Wextra", "-Werror", f"-I{INCLUDE}", f"-I{HOST}"]
+
+# C++ host programs: name -> sources under host/ (all link libxpu_cuda.so).
+HOST_PROGRAMS: dict[str, list[str]] = {}
+
+
+def _headers() -> list[Path]:
+    return sorted(list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h")) +
+                  list(HOST.glob("*.hpp")))
+
+
+def _stale(target: Path, sources: list[Path]) -> bool:
+    if not target.exists():
+        return True
+    t = target.stat().st_mtime
+    return any(s.stat().st_mtime > t for s in sources)
+
+
+def _run(cmd: list[str]) -> None:
+    proc = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+    if proc.returncode != 0:
+        sys.stderr.write(" ".join(cmd) + "\n" + proc.stdout)
+        raise RuntimeError(f"build step failed: {cmd[0]} {cmd[-1]}")
+
+
+def build_library(jobs: int | None = None) -> Path:
+    """Compile csrc/*.cu and csrc/*.cpp into lib/libxpu_cuda.so."""
+    BUILD.mkdir(parents=True, exist_ok=True)
+    LIB_DIR.mkdir(parents=True, exist_ok=True)
+    headers = _headers()
+    sources = sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
+    objects, todo = [], []
+    for src in sources:
+        obj = BUILD / (src.name + ".o")
+        objects.append(obj)
+        if _stale(obj, [src, Path(__file__), *headers]):
+            todo.append([NVCC, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)])
+    with concurrent.futures.ThreadPoolExecutor(max_workers=jobs or os.cpu_count() or 4) as pool:
+        for fut in [pool.submit(_run, cmd) for cmd in todo]:
+            fut.result()
+    if todo or _stale(LIB, objects):
+        _run([NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objects), "-ldl"])
+    return LIB
+
+
+def build_programs() -> list[Path]:
+    """Link the C++ host programs against libxpu_cuda.so."""
+    BIN_DIR.mkdir(parents=True, exist_ok=True)
+    headers = _headers()
+    outputs = []
+    for name, files in HOST_PROGRAMS.items():
+        srcs = [HOST / f for f in files]
+        out = BIN_DIR / name
+        outputs.append(out)
+        if _stale(out, [*srcs, LIB, Path(__file__), *headers]):
+            _run([CXX, *CXX_FLAGS, *map(str, srcs), "-o", str(out), f"-L{LIB_DIR}", "-lxpu_cuda",
+                  f"-Wl,-rpath,$ORIGIN/../lib"])
+    return outputs
+
+
+def build_all(jobs: int | None = None) -> None:
+    build_library(jobs)
+    build_programs()
+
+
+def clean() -> None:
+    for d in (BUILD, LIB_DIR, BIN_DIR):
+        if d.exists():
+            shutil.rmtree(d)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--clean", action="store_true")
+    ap.add_argument("-j", "--jobs", type=int, default=None)
+    args = ap.parse_args()
+    if args.clean:
+        clean()
+    build_all(args.jobs)
+    print(LIB)
+
+
+if __name__ == "__main__":
+    main()

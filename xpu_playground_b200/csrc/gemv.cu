@@ -1,0 +1,123 @@
+// Row-major GEMV y = A.x with FP32 accumulation (bf16 or fp16 in and out).
+//
+// Replaces gemv::Kernel<T>::run (gemv_kernel.hpp:21-63), which gives one
+// eSIMD work-item per row and walks K 32 columns at a time. Here:
+//   * the vector x is staged once per CTA into shared memory (16-byte chunks);
+//   * every warp owns ROWS rows and streams them with 16-byte
+//     ld.global.nc.L1::no_allocate loads, UNROLL chunks in flight per row;
+//   * lane l accumulates chunks l, l+32, l+64, ... in order, 8 products per
+//     chunk, then a butterfly shuffle sum folds the 32 lanes (fixed order).
+// Rows whose K is not a multiple of 8, or whose base is not 16-byte aligned,
+// take the scalar kernel below (same FP32 math, one element per lane step).
+#include "common.cuh"
+#include "xpu_internal.h"
+
+namespace xpu {
+
+constexpr int kGemvThreads = 256;
+constexpr int kGemvWarps = kGemvThreads / 32;
+
+template <typename T, int ROWS, int UNROLL>
+__global__ void __launch_bounds__(kGemvThreads)
+gemv_vec_kernel(const T *__restrict__ A, const T *__restrict__ x, T *__restrict__ y,
+                uint32_t m, uint32_t k) {
+  extern __shared__ uint4 xs[];  // k / 8 chunks of x
+  const uint32_t chunks = k >> 3;
+  const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
+  for (uint32_t i = threadIdx.x; i < chunks; i += kGemvThreads) xs[i] = ld_ro16(x4 + i);
+  __syncthreads();
+
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t row0 = (blockIdx.x * kGemvWarps + warp) * ROWS;
+  if (row0 >= m) return;
+  const uint4 *rows[ROWS];
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) {
+    const uint32_t row = min(row0 + r, m - 1);  // clamp: duplicate rows are dropped below
+    rows[r] = reinterpret_cast<const uint4 *>(A + static_cast<size_t>(row) * k);
+  }
+  float acc[ROWS];
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) acc[r] = 0.f;
+
+  uint32_t c = lane;
+  for (; c + 32 * (UNROLL - 1) < chunks; c += 32 * UNROLL) {
+    uint4 a[ROWS][UNROLL];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) a[r][u] = ld_stream16(rows[r] + c + 32 * u);
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const uint4 xv = xs[c + 32 * u];
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r) acc[r] = dot8<T>(a[r][u], xv, acc[r]);
+    }
+  }
+  for (; c < chunks; c += 32) {
+    const uint4 xv = xs[c];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) acc[r] = dot8<T>(ld_stream16(rows[r] + c), xv, acc[r]);
+  }
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) acc[r] = warp_sum(acc[r]);
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r)
+      if (row0 + r < m) y[row0 + r] = Elem<T>::from_float(acc[r]);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kGemvThreads)
+gemv_scalar_kernel(const T *__restrict__ A, const T *__restrict__ x, T *__restrict__ y,
+                   uint32_t m, uint32_t k) {
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t row = blockIdx.x * kGemvWarps + warp;
+  if (row >= m) return;
+  const T *a = A + static_cast<size_t>(row) * k;
+  float acc = 0.f;
+  for (uint32_t c = lane; c < k; c += 32)
+    acc = fmaf(Elem<T>::to_float(a[c]), Elem<T>::to_float(x[c]), acc);
+  acc = warp_sum(acc);
+  if (lane == 0) y[row] = Elem<T>::from_float(acc);
+}
+
+template <typename T, int ROWS, int UNROLL>
+static cudaError_t launch_vec(const T *A, const T *x, T *y, uint32_t m, uint32_t k,
+                              cudaStream_t stream) {
+  const size_t smem = static_cast<size_t>(k / 8) * sizeof(uint4);
+  auto kernel = gemv_vec_kernel<T, ROWS, UNROLL>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  const uint32_t rows_per_cta = kGemvWarps * ROWS;
+  const uint32_t grid = (m + rows_per_cta - 1) / rows_per_cta;
+  kernel<<<grid, kGemvThreads, smem, stream>>>(A, x, y, m, k);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t gemv_launch(const T *A, const T *x, T *y, uint32_t m, uint32_t k,
+                        cudaStream_t stream) {
+  const bool vector_path = (k % 8 == 0) && aligned16(A) && aligned16(x) &&
+                           static_cast<size_t>(k / 8) * sizeof(uint4) <= kMaxGemvVectorBytes;
+  if (!vector_path) {
+    const uint32_t grid = (m + kGemvWarps - 1) / kGemvWarps;
+    gemv_scalar_kernel<T><<<grid, kGemvThreads, 0, stream>>>(A, x, y, m, k);
+    return cudaGetLastError();
+  }
+  // Two rows per warp once there are enough rows to fill every SM several
+  // times over; one row per warp keeps small matrices spread across SMs.
+  if (m >= 8192) return launch_vec<T, 2, 4>(A, x, y, m, k, stream);
+  return launch_vec<T, 1, 8>(A, x, y, m, k, stream);
+}
+
+template cudaError_t gemv_launch<__nv_bfloat16>(const __nv_bfloat16 *, const __nv_bfloat16 *,
+                                                __nv_bfloat16 *, uint32_t, uint32_t, cudaStream_t);
+template cudaError_t gemv_launch<__half>(const __half *, const __half *, __half *, uint32_t,
+                                         uint32_t, cudaStream_t);
+
+}  // namespace xpu

@@ -1,0 +1,54 @@
+// Internal declarations shared by the translation units of libxpu_cuda.
+// Nothing here is part of the C ABI (include/xpu_cuda.h is).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/xpu_cuda.h"
+
+namespace xpu {
+
+// Largest vector (in bytes) the GEMV stages whole into shared memory.
+constexpr size_t kMaxGemvVectorBytes = 200 * 1024;
+
+__host__ __device__ inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Thread-local "last error" text behind xpu_last_error().
+void set_error(const std::string &message);
+int fail(int status, const std::string &message);
+int cuda_status(cudaError_t error, const char *what);
+
+// ---- GEMV ----
+template <typename T>
+cudaError_t gemv_launch(const T *A, const T *x, T *y, uint32_t m, uint32_t k,
+                        cudaStream_t stream);
+
+// ---- Qwen3 operators with the reference kernels' semantics ----
+cudaError_t qwen_embedding_launch(const uint16_t *table, uint16_t *out, uint32_t token,
+                                  uint32_t width, cudaStream_t stream);
+cudaError_t qwen_rms_norm_launch(const uint16_t *in, const uint16_t *w, uint16_t *out,
+                                 uint32_t width, float eps, cudaStream_t stream);
+cudaError_t qwen_qkv_rope_cache_launch(uint16_t *q, uint16_t *k, const uint16_t *v,
+                                       const uint16_t *qn, const uint16_t *kn,
+                                       const uint16_t *cos_table, const uint16_t *sin_table,
+                                       uint16_t *kc, uint16_t *vc, uint32_t position,
+                                       uint32_t max_seq, uint32_t q_heads, uint32_t kv_heads,
+                                       cudaStream_t stream);
+size_t qwen_attention_workspace(uint32_t q_heads, uint32_t max_positions);
+cudaError_t qwen_attention_launch(const uint16_t *q, const uint16_t *kc, const uint16_t *vc,
+                                  uint16_t *out, uint32_t position, uint32_t q_heads,
+                                  uint32_t kv_heads, float *workspace, cudaStream_t stream);
+cudaError_t qwen_add_launch(uint16_t *left, const uint16_t *right, uint32_t width,
+                            cudaStream_t stream);
+cudaError_t qwen_silu_multiply_launch(uint16_t *gate, const uint16_t *up, uint32_t width,
+                                      cudaStream_t stream);
+cudaError_t qwen_argmax_launch(const uint16_t *values, uint32_t *token, uint32_t width,
+                               cudaStream_t stream);
+
+}  // namespace xpu
