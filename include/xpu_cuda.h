@@ -109,6 +109,88 @@ int xpu_qwen_silu_multiply(uint16_t *gate, const uint16_t *up, uint32_t width, v
  * index of the maximum, 0xffffffff if any value is NaN or +-Inf. */
 int xpu_qwen_argmax(const uint16_t *values, uint32_t *token, uint32_t width, void *stream);
 
+/* ------------------------------------------------------- synthetic data --
+ * Seeded, irregular inputs generated on the device (the reference generates
+ * its benchmark inputs on the device too: gemv.cpp:156-167). Each element is
+ * a pure function of (seed, tag, index); the CPU oracle reproduces it bit
+ * for bit. */
+
+/* out[i] = uniform[-1, 1) rounded to dtype (XPU_BF16 / XPU_FP16). */
+int xpu_fill_uniform16(int dtype, void *out, uint64_t count, uint64_t seed, uint64_t tag,
+                       void *stream);
+/* out[i] ~ N(0, stddev^2) (Irwin-Hall sum of twelve 10-bit uniforms), bf16. */
+int xpu_fill_normal_bf16(uint16_t *out, uint64_t count, uint64_t seed, uint64_t tag, float stddev,
+                         void *stream);
+
+/* ------------------------------------------------------ Qwen3 decoder --
+ * The decode engine of qwen3/main.cpp:118-329 (Engine): weights in one
+ * device arena, bf16 KV caches [layer][position][kv_head][128], RoPE tables,
+ * and one decode step captured as a CUDA graph. Shape-generic (the
+ * reference pins Qwen3-8B in qwen3/model.hpp:11-22): head_dim 128,
+ * query/key-value head ratio 1, 2, 4 or 8, tied or untied lm_head.
+ * tp_size > 1 builds rank tp_rank of a tensor-parallel group. */
+typedef struct xpu_qwen3_engine xpu_qwen3_engine;
+
+typedef struct {
+  uint32_t hidden_size;
+  uint32_t intermediate_size;
+  uint32_t num_hidden_layers;
+  uint32_t num_attention_heads;
+  uint32_t num_key_value_heads;
+  uint32_t vocab_size;
+  uint32_t tie_word_embeddings; /* 0 or 1 */
+  float rms_norm_eps;
+  double rope_theta;
+} xpu_qwen3_shape;
+
+typedef struct {
+  uint64_t weight_bytes;     /* bytes of this rank's weight arena */
+  uint32_t kernels_per_step; /* kernel launches in one decode step */
+  uint32_t vocab_rows;       /* lm_head rows held by this rank */
+  uint32_t vocab_offset;     /* first vocabulary id of this rank */
+  void *stream;              /* the engine's CUDA stream */
+} xpu_qwen3_info_t;
+
+/* Engine ctor + Engine::reserve (qwen3/main.cpp:120-157): allocates the
+ * weight arena, caches for maximum_sequence positions and the activations on
+ * `device`. */
+int xpu_qwen3_create(const xpu_qwen3_shape *shape, uint32_t maximum_sequence, int device,
+                     uint32_t tp_rank, uint32_t tp_size, xpu_qwen3_engine **out);
+int xpu_qwen3_destroy(xpu_qwen3_engine *engine);
+/* Seeded synthetic checkpoint: norm weights 1, all other tensors N(0, stddev)
+ * drawn per tensor (xpu_fill_normal_bf16 stream = tensor tag: 0 embed, 1 final
+ * norm, 2 lm_head, 3 + 11*layer + index in the layer's tensor list). */
+int xpu_qwen3_init_synthetic(xpu_qwen3_engine *engine, uint64_t seed, float stddev);
+/* Engine::upload_weights (qwen3/main.cpp:265-298) for one tensor: `elements`
+ * bf16 values of the full, unsharded checkpoint tensor `name` (safetensors
+ * naming, qwen3/model.cpp:412-425) from host memory; this rank keeps its shard. */
+int xpu_qwen3_set_tensor(xpu_qwen3_engine *engine, const char *name, const uint16_t *host_bf16,
+                         uint64_t elements);
+/* Engine::decode (qwen3/main.cpp:159-226): one synchronous step; returns the
+ * greedy next token. XPU_ERR_NONFINITE (and 0xffffffff) on NaN/Inf logits. */
+int xpu_qwen3_decode(xpu_qwen3_engine *engine, uint32_t token, uint32_t position,
+                     uint32_t *next_token);
+/* qwen3/main.cpp:342-352 on the device: the prompt fed token by token, then up
+ * to max_new_tokens greedy tokens (stopping after EOS 151645 / 151643 when
+ * stop_at_eos), with one host synchronisation. */
+int xpu_qwen3_generate(xpu_qwen3_engine *engine, const uint32_t *prompt, uint32_t prompt_len,
+                       uint32_t max_new_tokens, int stop_at_eos, uint32_t *out_tokens,
+                       uint32_t *out_count);
+/* Device-resident stepping: set the next step's input, enqueue steps without
+ * synchronising (each step feeds its greedy token to the next), read back. */
+int xpu_qwen3_set_state(xpu_qwen3_engine *engine, uint32_t token, uint32_t position,
+                        uint32_t prompt_len);
+int xpu_qwen3_enqueue_steps(xpu_qwen3_engine *engine, uint32_t steps, void *stream);
+int xpu_qwen3_get_state(xpu_qwen3_engine *engine, uint32_t *last_token, uint32_t *next_position,
+                        uint32_t *error);
+int xpu_qwen3_synchronize(xpu_qwen3_engine *engine);
+/* bf16 logits of the last step (this rank's vocab_rows rows). */
+int xpu_qwen3_logits(xpu_qwen3_engine *engine, uint16_t *host_out, uint32_t count);
+int xpu_qwen3_info(xpu_qwen3_engine *engine, xpu_qwen3_info_t *info);
+/* Algorithmic HBM bytes of one decode step at `context` cached positions:
+ * every weight streamed once (one embedding row) plus K/V reads. */
+uint64_t xpu_qwen3_bytes_per_token(xpu_qwen3_engine *engine, uint32_t context);
+
 #ifdef __cplusplus
 }
 #endif

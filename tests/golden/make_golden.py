@@ -40,6 +40,7 @@ MODEL_CASES = {
     "tiny": ("tiny", 1234, 7, 8, 24),
     "tiny-tied": ("tiny-tied", 99, 11, 12, 20),
     "qwen3-0.6b": ("qwen3-0.6b", 2026, 3, 128, 128),
+    "qwen3-8b-l2": ("qwen3-8b-l2", 8, 5, 16, 16),
 }
 
 

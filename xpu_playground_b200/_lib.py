@@ -50,7 +50,35 @@ SIGNATURES: dict[str, tuple] = {
     "xpu_qwen_add": (i32, [vp, vp, u32, vp]),
     "xpu_qwen_silu_multiply": (i32, [vp, vp, u32, vp]),
     "xpu_qwen_argmax": (i32, [vp, vp, u32, vp]),
+    "xpu_fill_uniform16": (i32, [i32, vp, u64, u64, u64, vp]),
+    "xpu_fill_normal_bf16": (i32, [vp, u64, u64, u64, f32, vp]),
+    "xpu_qwen3_create": (i32, [vp, u32, i32, u32, u32, vp]),
+    "xpu_qwen3_destroy": (i32, [vp]),
+    "xpu_qwen3_init_synthetic": (i32, [vp, u64, f32]),
+    "xpu_qwen3_set_tensor": (i32, [vp, ctypes.c_char_p, vp, u64]),
+    "xpu_qwen3_decode": (i32, [vp, u32, u32, vp]),
+    "xpu_qwen3_generate": (i32, [vp, vp, u32, u32, i32, vp, vp]),
+    "xpu_qwen3_set_state": (i32, [vp, u32, u32, u32]),
+    "xpu_qwen3_enqueue_steps": (i32, [vp, u32, vp]),
+    "xpu_qwen3_get_state": (i32, [vp, vp, vp, vp]),
+    "xpu_qwen3_synchronize": (i32, [vp]),
+    "xpu_qwen3_logits": (i32, [vp, vp, u32]),
+    "xpu_qwen3_info": (i32, [vp, vp]),
+    "xpu_qwen3_bytes_per_token": (u64, [vp, u32]),
 }
+
+
+class Qwen3ShapeC(ctypes.Structure):
+    """xpu_qwen3_shape."""
+    _fields_ = [("hidden_size", u32), ("intermediate_size", u32), ("num_hidden_layers", u32),
+                ("num_attention_heads", u32), ("num_key_value_heads", u32), ("vocab_size", u32),
+                ("tie_word_embeddings", u32), ("rms_norm_eps", f32), ("rope_theta", f64)]
+
+
+class Qwen3InfoC(ctypes.Structure):
+    """xpu_qwen3_info_t."""
+    _fields_ = [("weight_bytes", u64), ("kernels_per_step", u32), ("vocab_rows", u32),
+                ("vocab_offset", u32), ("stream", vp)]
 
 _lib = None
 

@@ -1,0 +1,118 @@
+// Data layout and kernel interface of the fused Qwen3 decode step.
+//
+// One decode step of one tensor-parallel rank is this launch sequence
+// (captured once into a CUDA graph and replayed per token):
+//   embed                      x = embed[token]
+//   per layer:
+//     qkv      RMSNorm(x) -> [Wq;Wk;Wv] GEMV (split-K), last CTA per head:
+//              q/k RMSNorm + RoPE, q -> q buffer, k/v -> cache[position]
+//     scores   per (kv head, 128-position chunk): s = bf16(bf16(q.k) * scale),
+//              chunk max and sum of exp
+//     pv       softmax probabilities bf16(exp(s - M) / S), partial sum p*v per
+//              chunk, last CTA per kv head sums the chunks -> attn buffer
+//     oproj    Wo GEMV over canonical K chunks, last CTA per row tile:
+//              x = bf16(x + bf16(sum of chunks))        [TP: exchange first]
+//     gateup   RMSNorm(x) -> [gate;up] GEMV, h = bf16(bf16(silu(g)) * u)
+//     down     Wd GEMV over canonical K chunks, residual add as oproj
+//   lmhead     RMSNorm(x) -> lm_head GEMV, bf16 logits, argmax (lowest index
+//              on ties, NaN/Inf -> 0xffffffff), state update
+// The rounding points are those of the transformers Qwen3 eager/bf16 forward
+// that qwen3/reference.py runs.
+#pragma once
+
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace xpu {
+
+constexpr uint32_t kHD = 128;            // head_dim
+constexpr uint32_t kCanonChunks = 8;     // K chunks of the row-parallel GEMVs
+constexpr uint32_t kPosChunk = 128;      // positions per attention chunk
+constexpr uint32_t kDecThreads = 256;    // threads per decode-GEMV CTA
+constexpr uint32_t kTileRows = 16;       // rows per decode-GEMV tile (8 warps x 2)
+constexpr float kAttnScale = 0.08838834764831845f;  // 1/sqrt(128)
+
+typedef __nv_bfloat16 bf16;
+
+// Device-resident step state. Host writes it for synchronous decode calls;
+// the lm_head kernel advances it for device-resident generation.
+struct DecodeState {
+  uint32_t token;       // input token of the next step (unless position < prompt_len)
+  uint32_t position;    // position of the next step
+  uint32_t prompt_len;  // positions below this read their token from prompt[]
+  uint32_t next;        // greedy token of the last step (0xffffffff on NaN/Inf)
+  uint32_t error;       // sticky: 1 = NaN/Inf logits, 2 = exchange timeout
+  uint32_t steps;       // completed steps since the last reset
+  uint32_t pad[2];
+};
+
+struct DecodeDims {
+  uint32_t H;           // hidden size
+  uint32_t I_l;         // intermediate rows held by this rank
+  uint32_t QH_l, KVH_l; // heads held by this rank
+  uint32_t vocab;       // full vocabulary (embedding rows)
+  uint32_t V_l;         // vocabulary rows held by this rank
+  uint32_t v_offset;    // first global vocabulary row of this rank
+  uint32_t max_seq;
+  uint32_t qkv_splits;  // K splits of the QKV GEMV (fixed per shape)
+  uint32_t chunks_l;    // canonical chunks held by this rank (8 / tp_size)
+  uint32_t chunk0;      // first canonical chunk of this rank
+  uint32_t tp_size, tp_rank;
+  float eps;
+};
+
+struct LayerWeights {
+  const bf16 *in_norm, *post_norm, *q_norm, *k_norm;
+  const bf16 *wqkv;  // [(QH_l + 2 KVH_l) * 128][H]
+  const bf16 *wo;    // [H][QH_l * 128]
+  const bf16 *wgu;   // [2 I_l][H], row 2i = gate i, 2i+1 = up i
+  const bf16 *wd;    // [H][I_l]
+  bf16 *kcache, *vcache;  // [max_seq][KVH_l][128]
+};
+
+struct DecodeBuffers {
+  bf16 *x;           // residual stream [H]
+  bf16 *q;           // [QH_l * 128]
+  bf16 *attn;        // attention output [QH_l * 128]
+  bf16 *h;           // SwiGLU output [I_l]
+  float *part_qkv;   // [qkv_splits][rows_qkv]
+  float *part;       // [8][H] canonical-chunk partials (oproj and down share it)
+  float *scores;     // [QH_l][max_seq]
+  float *stats;      // [QH_l][n_pos_chunks][2]
+  float *attn_part;  // [QH_l][n_pos_chunks][128]
+  ArgBest *lm_best;  // [lm CTAs]
+  uint32_t *lm_bad;  // [lm CTAs]
+  uint16_t *logits;  // [V_l] bf16 bits
+  unsigned *cnt_qkv; // [heads_qkv]
+  unsigned *cnt_attn;// [KVH_l]
+  unsigned *cnt_tile;// [H / 16]
+  unsigned *cnt_lm;  // [1]
+  DecodeState *state;
+  const uint32_t *prompt;  // [max_seq]
+  uint32_t *log;           // [max_seq] greedy token per position
+  const bf16 *cos_t, *sin_t;  // [max_seq][128]
+  const bf16 *embed;       // [vocab][H]
+  const bf16 *final_norm;
+  const bf16 *lm_head;     // [V_l][H]
+};
+
+// Launchers (decode_kernels.cu). Each returns the launch error.
+cudaError_t launch_embed(const DecodeDims &d, const DecodeBuffers &b, cudaStream_t s);
+cudaError_t launch_qkv(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w,
+                       cudaStream_t s);
+cudaError_t launch_attention(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w,
+                             cudaStream_t s);
+cudaError_t launch_oproj(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w,
+                         cudaStream_t s);
+cudaError_t launch_gateup(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w,
+                          cudaStream_t s);
+cudaError_t launch_down(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w,
+                        cudaStream_t s);
+cudaError_t launch_lmhead(const DecodeDims &d, const DecodeBuffers &b, cudaStream_t s);
+
+// Number of CTAs the lm_head kernel launches (sizes lm_best / lm_bad).
+uint32_t lmhead_ctas(const DecodeDims &d);
+uint32_t pos_chunks(uint32_t max_seq);
+
+}  // namespace xpu

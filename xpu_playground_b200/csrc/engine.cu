@@ -1,0 +1,660 @@
+// Qwen3 decode engine: weights, KV cache and the per-token CUDA graph.
+//
+// Replaces the reference's Engine (qwen3/main.cpp:118-329) and the Level Zero
+// runtime it drives (qwen3/level_zero_runtime.cpp): instead of 508 launches
+// each followed by a host synchronisation, one decode step is a captured
+// CUDA graph of 2 + 6 * layers fused kernels (decode.cuh) that reads its
+// input token and position from device memory, so prompt processing and
+// greedy generation run back to back on the GPU without host round trips.
+//
+// Tensor parallelism (tp_size > 1) shards q/k/v and gate/up by rows (heads,
+// intermediate units), o_proj/down by columns in canonical chunks, and the
+// lm_head by vocabulary rows.
+#include <algorithm>
+#include <cmath>
+#include <stdexcept>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "decode.cuh"
+#include "xpu_internal.h"
+
+namespace xpu {
+
+cudaError_t fill_normal_window(uint16_t *dst, uint64_t dst_ld, uint32_t row_step, uint64_t nrows,
+                               uint64_t ncols, uint64_t src_cols, uint64_t r0, uint64_t c0,
+                               uint64_t seed, uint64_t tag, float stddev, cudaStream_t s);
+cudaError_t fill_value16(uint16_t *dst, uint64_t n, uint16_t bits, cudaStream_t s);
+
+namespace {
+
+struct CudaError : std::runtime_error {
+  cudaError_t code;
+  CudaError(cudaError_t c, const std::string &what)
+      : std::runtime_error(what + ": " + cudaGetErrorName(c) + " (" + cudaGetErrorString(c) + ")"), code(c) {}
+};
+
+#define CK(expr)                                               \
+  do {                                                         \
+    cudaError_t e_ = (expr);                                   \
+    if (e_ != cudaSuccess) throw CudaError(e_, #expr);         \
+  } while (0)
+
+struct InvalidArg : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+uint16_t host_bf16(float v) {  // RNE, finite inputs only (constants)
+  uint32_t bits;
+  std::memcpy(&bits, &v, 4);
+  bits += 0x7fffu + ((bits >> 16) & 1u);
+  return static_cast<uint16_t>(bits >> 16);
+}
+
+// Where (part of) one checkpoint tensor lives on this rank: rows
+// [r0, r0 + nr) and columns [c0, c0 + nc) of the global [rows x cols] tensor
+// go to dst, row i of the window at dst + i * pitch elements.
+struct Placement {
+  uint16_t *dst;
+  uint64_t pitch;
+  uint64_t r0, nr, c0, nc, cols;
+};
+
+}  // namespace
+
+class Qwen3Engine {
+ public:
+  Qwen3Engine(const xpu_qwen3_shape &shape, uint32_t max_seq, int device, uint32_t tp_rank,
+              uint32_t tp_size)
+      : shape_(shape), max_seq_(max_seq), device_(device), rank_(tp_rank), tp_(tp_size) {
+    validate();
+    CK(cudaSetDevice(device_));
+    CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    plan();
+    allocate();
+    upload_rope();
+  }
+
+  ~Qwen3Engine() {
+    cudaSetDevice(device_);
+    if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    for (void *p : allocations_) cudaFree(p);
+    if (host_state_) cudaFreeHost(host_state_);
+    if (stream_) cudaStreamDestroy(stream_);
+  }
+
+  Qwen3Engine(const Qwen3Engine &) = delete;
+  Qwen3Engine &operator=(const Qwen3Engine &) = delete;
+
+  // ---------------------------------------------------------- weights ----
+  std::vector<std::string> tensor_names() const {
+    std::vector<std::string> names{"model.embed_tokens.weight", "model.norm.weight"};
+    if (!shape_.tie_word_embeddings) names.push_back("lm_head.weight");
+    static const char *suffix[] = {
+        "input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_proj.weight",
+        "self_attn.k_proj.weight", "self_attn.v_proj.weight", "self_attn.o_proj.weight",
+        "self_attn.q_norm.weight", "self_attn.k_norm.weight", "mlp.gate_proj.weight",
+        "mlp.up_proj.weight", "mlp.down_proj.weight"};
+    for (uint32_t l = 0; l < shape_.num_hidden_layers; ++l)
+      for (const char *s : suffix) names.push_back("model.layers." + std::to_string(l) + "." + s);
+    return names;
+  }
+
+  // Global shape of a checkpoint tensor (rows, cols); vectors are 1 x n.
+  void global_shape(const std::string &name, uint64_t &rows, uint64_t &cols) const {
+    const uint64_t H = shape_.hidden_size, I = shape_.intermediate_size, V = shape_.vocab_size;
+    const uint64_t Q = shape_.num_attention_heads * 128ull, KV = shape_.num_key_value_heads * 128ull;
+    rows = 1;
+    if (name == "model.embed_tokens.weight" || name == "lm_head.weight") { rows = V; cols = H; return; }
+    if (name == "model.norm.weight") { cols = H; return; }
+    const std::string suf = layer_suffix(name);
+    if (suf == "input_layernorm.weight" || suf == "post_attention_layernorm.weight") { cols = H; return; }
+    if (suf == "self_attn.q_norm.weight" || suf == "self_attn.k_norm.weight") { cols = 128; return; }
+    if (suf == "self_attn.q_proj.weight") { rows = Q; cols = H; return; }
+    if (suf == "self_attn.k_proj.weight" || suf == "self_attn.v_proj.weight") { rows = KV; cols = H; return; }
+    if (suf == "self_attn.o_proj.weight") { rows = H; cols = Q; return; }
+    if (suf == "mlp.gate_proj.weight" || suf == "mlp.up_proj.weight") { rows = I; cols = H; return; }
+    if (suf == "mlp.down_proj.weight") { rows = H; cols = I; return; }
+    throw InvalidArg("unknown Qwen3 tensor name: " + name);
+  }
+
+  std::vector<Placement> placements(const std::string &name) const {
+    uint64_t rows, cols;
+    global_shape(name, rows, cols);
+    const uint64_t H = d_.H;
+    if (name == "model.embed_tokens.weight") return {{embed_, H, 0, rows, 0, cols, cols}};
+    if (name == "lm_head.weight") return {{lm_head_, H, d_.v_offset, d_.V_l, 0, cols, cols}};
+    if (name == "model.norm.weight") return {{final_norm_, cols, 0, 1, 0, cols, cols}};
+    const uint32_t l = layer_index(name);
+    const Layer &L = layers_[l];
+    const std::string suf = layer_suffix(name);
+    const uint64_t qr = d_.QH_l * 128ull, kvr = d_.KVH_l * 128ull;
+    if (suf == "input_layernorm.weight") return {{L.in_norm, cols, 0, 1, 0, cols, cols}};
+    if (suf == "post_attention_layernorm.weight") return {{L.post_norm, cols, 0, 1, 0, cols, cols}};
+    if (suf == "self_attn.q_norm.weight") return {{L.q_norm, cols, 0, 1, 0, cols, cols}};
+    if (suf == "self_attn.k_norm.weight") return {{L.k_norm, cols, 0, 1, 0, cols, cols}};
+    if (suf == "self_attn.q_proj.weight") return {{L.wqkv, H, rank_ * qr, qr, 0, H, H}};
+    if (suf == "self_attn.k_proj.weight") return {{L.wqkv + qr * H, H, rank_ * kvr, kvr, 0, H, H}};
+    if (suf == "self_attn.v_proj.weight") return {{L.wqkv + (qr + kvr) * H, H, rank_ * kvr, kvr, 0, H, H}};
+    if (suf == "self_attn.o_proj.weight") return {{L.wo, qr, 0, H, rank_ * qr, qr, cols}};
+    if (suf == "mlp.gate_proj.weight") return {{L.wgu, 2 * H, rank_ * d_.I_l, d_.I_l, 0, H, H}};
+    if (suf == "mlp.up_proj.weight") return {{L.wgu + H, 2 * H, rank_ * d_.I_l, d_.I_l, 0, H, H}};
+    if (suf == "mlp.down_proj.weight") return {{L.wd, d_.I_l, 0, H, rank_ * (uint64_t)d_.I_l, d_.I_l, cols}};
+    throw InvalidArg("unknown Qwen3 tensor name: " + name);
+  }
+
+  uint32_t tensor_tag(const std::string &name) const {
+    if (name == "model.embed_tokens.weight") return 0;
+    if (name == "model.norm.weight") return 1;
+    if (name == "lm_head.weight") return 2;
+    static const char *suffix[] = {
+        "input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_proj.weight",
+        "self_attn.k_proj.weight", "self_attn.v_proj.weight", "self_attn.o_proj.weight",
+        "self_attn.q_norm.weight", "self_attn.k_norm.weight", "mlp.gate_proj.weight",
+        "mlp.up_proj.weight", "mlp.down_proj.weight"};
+    const std::string suf = layer_suffix(name);
+    for (uint32_t j = 0; j < 11; ++j)
+      if (suf == suffix[j]) return 3 + 11 * layer_index(name) + j;
+    throw InvalidArg("unknown Qwen3 tensor name: " + name);
+  }
+
+  // Seeded synthetic checkpoint: norms 1, everything else N(0, stddev).
+  void init_synthetic(uint64_t seed, float stddev) {
+    CK(cudaSetDevice(device_));
+    for (const std::string &name : tensor_names()) {
+      const bool norm = name.size() >= 11 && name.compare(name.size() - 11, 11, "norm.weight") == 0;
+      for (const Placement &p : placements(name)) {
+        if (norm) {
+          CK(fill_value16(p.dst, p.nc, host_bf16(1.0f), stream_));
+        } else {
+          CK(fill_normal_window(p.dst, p.pitch, 1, p.nr, p.nc, p.cols, p.r0, p.c0, seed,
+                                tensor_tag(name), stddev, stream_));
+        }
+      }
+    }
+    CK(cudaStreamSynchronize(stream_));
+    loaded_ = true;
+  }
+
+  // Copy (this rank's part of) a full tensor from host memory.
+  void set_tensor(const std::string &name, const uint16_t *host, uint64_t elements) {
+    CK(cudaSetDevice(device_));
+    uint64_t rows, cols;
+    global_shape(name, rows, cols);
+    if (elements != rows * cols)
+      throw InvalidArg("tensor " + name + " has " + std::to_string(rows * cols) + " elements, got " +
+                       std::to_string(elements));
+    for (const Placement &p : placements(name))
+      CK(cudaMemcpy2DAsync(p.dst, p.pitch * 2, host + p.r0 * p.cols + p.c0, p.cols * 2, p.nc * 2, p.nr,
+                           cudaMemcpyHostToDevice, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    ++tensors_set_;
+    if (tensors_set_ >= tensor_names().size()) loaded_ = true;
+  }
+
+  void mark_loaded() { loaded_ = true; }
+
+  // ------------------------------------------------------------ decode ----
+  // One step: input token at position (qwen3/main.cpp:159-226 Engine::decode).
+  uint32_t decode(uint32_t token, uint32_t position) {
+    if (position >= max_seq_) throw InvalidArg("position " + std::to_string(position) + " >= maximum sequence " + std::to_string(max_seq_));
+    if (token >= shape_.vocab_size) throw InvalidArg("token id outside the vocabulary");
+    ensure_graph();
+    host_state_->token = token;
+    host_state_->position = position;
+    host_state_->prompt_len = 0;
+    host_state_->error = 0;
+    host_state_->steps = 0;
+    CK(cudaMemcpyAsync(state_, host_state_, sizeof(DecodeState), cudaMemcpyHostToDevice, stream_));
+    CK(cudaGraphLaunch(graph_exec_, stream_));
+    CK(cudaMemcpyAsync(host_state_, state_, sizeof(DecodeState), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    return host_state_->next;
+  }
+
+  // Device-resident prompt + greedy generation: prompt[0..n) fed token by
+  // token, then n_new greedy tokens; one host synchronisation at the end.
+  // Returns the number of generated tokens written to out (stops after EOS
+  // when stop_at_eos and the token is 151645 or 151643, main.cpp:345-352).
+  uint32_t generate(const uint32_t *prompt, uint32_t n, uint32_t n_new, uint32_t *out, bool stop_at_eos) {
+    if (n == 0) throw InvalidArg("at least one prompt token is required");
+    if (static_cast<uint64_t>(n) + n_new > max_seq_) throw InvalidArg("prompt plus generation exceeds the maximum sequence");
+    for (uint32_t i = 0; i < n; ++i)
+      if (prompt[i] >= shape_.vocab_size) throw InvalidArg("prompt token id outside the vocabulary");
+    ensure_graph();
+    CK(cudaMemcpyAsync(prompt_, prompt, n * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
+    *host_state_ = DecodeState{};
+    host_state_->prompt_len = n;
+    CK(cudaMemcpyAsync(state_, host_state_, sizeof(DecodeState), cudaMemcpyHostToDevice, stream_));
+    const uint32_t steps = n_new ? n + n_new - 1 : n;
+    for (uint32_t i = 0; i < steps; ++i) CK(cudaGraphLaunch(graph_exec_, stream_));
+    std::vector<uint32_t> log(n + n_new);
+    CK(cudaMemcpyAsync(log.data(), log_, (n + n_new) * sizeof(uint32_t), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaMemcpyAsync(host_state_, state_, sizeof(DecodeState), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    uint32_t count = 0;
+    for (uint32_t i = 0; i < n_new; ++i) {
+      const uint32_t t = log[n - 1 + i];
+      out[count++] = t;
+      if (t == 0xffffffffu) break;
+      if (stop_at_eos && (t == 151645u || t == 151643u)) break;
+    }
+    return count;
+  }
+
+  // Set the device state without running (for device-resident loops).
+  void set_state(uint32_t token, uint32_t position, uint32_t prompt_len) {
+    *host_state_ = DecodeState{};
+    host_state_->token = token;
+    host_state_->position = position;
+    host_state_->prompt_len = prompt_len;
+    CK(cudaMemcpyAsync(state_, host_state_, sizeof(DecodeState), cudaMemcpyHostToDevice, stream_));
+    CK(cudaStreamSynchronize(stream_));
+  }
+
+  DecodeState get_state() {
+    CK(cudaMemcpyAsync(host_state_, state_, sizeof(DecodeState), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    return *host_state_;
+  }
+
+  // Enqueue n device-resident steps on `stream` (or the engine's own).
+  void enqueue_steps(uint32_t n, cudaStream_t stream) {
+    ensure_graph();
+    cudaStream_t s = stream ? stream : stream_;
+    for (uint32_t i = 0; i < n; ++i) CK(cudaGraphLaunch(graph_exec_, s));
+  }
+
+  void logits(uint16_t *host, uint32_t count) {
+    if (count > d_.V_l) throw InvalidArg("logit count exceeds this rank's vocabulary rows");
+    CK(cudaMemcpyAsync(host, logits_, count * 2ull, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+  }
+
+  void sync() { CK(cudaStreamSynchronize(stream_)); }
+
+  const DecodeDims &dims() const { return d_; }
+  cudaStream_t stream() const { return stream_; }
+  uint32_t kernels_per_step() const { return 2 + 6 * shape_.num_hidden_layers; }
+  uint64_t weight_bytes() const { return weights_bytes_; }
+  uint64_t bytes_per_token(uint32_t context) const {
+    // weights streamed per step (embedding: one row) + K and V read for
+    // `context` positions + the new K/V row written
+    const uint64_t H = d_.H;
+    uint64_t w = weights_bytes_ - embed_bytes_ + H * 2;
+    if (shape_.tie_word_embeddings) w += static_cast<uint64_t>(d_.V_l) * H * 2;
+    const uint64_t kv = 2ull * shape_.num_hidden_layers * d_.KVH_l * 128 * 2;
+    return w + kv * context;
+  }
+
+ private:
+  struct Layer {
+    uint16_t *in_norm, *post_norm, *q_norm, *k_norm, *wqkv, *wo, *wgu, *wd, *kcache, *vcache;
+  };
+
+  static std::string layer_suffix(const std::string &name) {
+    const std::string prefix = "model.layers.";
+    if (name.compare(0, prefix.size(), prefix) != 0) return "";
+    const size_t dot = name.find('.', prefix.size());
+    return dot == std::string::npos ? "" : name.substr(dot + 1);
+  }
+
+  uint32_t layer_index(const std::string &name) const {
+    const std::string prefix = "model.layers.";
+    if (name.compare(0, prefix.size(), prefix) != 0) throw InvalidArg("unknown Qwen3 tensor name: " + name);
+    const size_t dot = name.find('.', prefix.size());
+    const std::string digits = name.substr(prefix.size(), dot - prefix.size());
+    if (digits.empty() || digits.find_first_not_of("0123456789") != std::string::npos)
+      throw InvalidArg("bad layer index in " + name);
+    const unsigned long l = std::stoul(digits);
+    if (l >= shape_.num_hidden_layers) throw InvalidArg("layer index out of range in " + name);
+    return static_cast<uint32_t>(l);
+  }
+
+  void validate() const {
+    const auto &s = shape_;
+    auto req = [](bool ok, const char *what) {
+      if (!ok) throw InvalidArg(std::string("unsupported Qwen3 shape: ") + what);
+    };
+    req(s.hidden_size > 0 && s.hidden_size % 128 == 0, "hidden_size must be a positive multiple of 128");
+    req(s.num_key_value_heads > 0 && s.num_attention_heads % s.num_key_value_heads == 0,
+        "num_attention_heads must be a multiple of num_key_value_heads");
+    const uint32_t g = s.num_attention_heads / s.num_key_value_heads;
+    req(g == 1 || g == 2 || g == 4 || g == 8, "query heads per key/value head must be 1, 2, 4 or 8");
+    req(s.intermediate_size > 0 && s.intermediate_size % 64 == 0, "intermediate_size must be a multiple of 64");
+    req(s.num_hidden_layers > 0 && s.vocab_size > 0, "layers and vocabulary must be positive");
+    req(max_seq_ > 0 && max_seq_ <= 40960, "maximum sequence must be in [1, 40960]");
+    req(tp_ == 1 || tp_ == 2 || tp_ == 4 || tp_ == 8, "tensor-parallel size must be 1, 2, 4 or 8");
+    req(rank_ < tp_, "tensor-parallel rank out of range");
+    req(s.num_key_value_heads % tp_ == 0 && s.num_attention_heads % tp_ == 0,
+        "heads must divide evenly across tensor-parallel ranks");
+    req(s.intermediate_size % (64 * tp_) == 0, "intermediate_size / tp must be a multiple of 64");
+    req(s.vocab_size % tp_ == 0 && (s.vocab_size / tp_) % 2 == 0, "vocabulary must split evenly");
+  }
+
+  void plan() {
+    const auto &s = shape_;
+    d_ = DecodeDims{};
+    d_.H = s.hidden_size;
+    d_.I_l = s.intermediate_size / tp_;
+    d_.QH_l = s.num_attention_heads / tp_;
+    d_.KVH_l = s.num_key_value_heads / tp_;
+    d_.vocab = s.vocab_size;
+    d_.V_l = s.vocab_size / tp_;
+    d_.v_offset = rank_ * d_.V_l;
+    d_.max_seq = max_seq_;
+    d_.qkv_splits = d_.H >= 2048 ? d_.H / 1024 : 1;
+    d_.chunks_l = kCanonChunks / tp_;
+    d_.chunk0 = rank_ * d_.chunks_l;
+    d_.tp_size = tp_;
+    d_.tp_rank = rank_;
+    d_.eps = s.rms_norm_eps;
+  }
+
+  template <typename T>
+  T *dev_alloc(uint64_t count) {
+    void *p = nullptr;
+    const cudaError_t e = cudaMalloc(&p, std::max<uint64_t>(count * sizeof(T), 16));
+    if (e != cudaSuccess) throw CudaError(e, "cudaMalloc of " + std::to_string(count * sizeof(T)) + " bytes");
+    allocations_.push_back(p);
+    return static_cast<T *>(p);
+  }
+
+  void allocate() {
+    const auto &s = shape_;
+    const uint64_t H = d_.H, L = s.num_hidden_layers;
+    const uint64_t qr = d_.QH_l * 128ull, kvr = d_.KVH_l * 128ull;
+    // One weight arena, every tensor 4 KiB aligned (qwen3/model.cpp:481-491).
+    struct Item { uint16_t **slot; uint64_t elems; };
+    std::vector<Item> items;
+    layers_.assign(L, Layer{});
+    items.push_back({&embed_, static_cast<uint64_t>(s.vocab_size) * H});
+    items.push_back({&final_norm_, H});
+    if (!s.tie_word_embeddings) items.push_back({&lm_head_, static_cast<uint64_t>(d_.V_l) * H});
+    for (uint64_t l = 0; l < L; ++l) {
+      Layer &Y = layers_[l];
+      items.push_back({&Y.in_norm, H});
+      items.push_back({&Y.post_norm, H});
+      items.push_back({&Y.q_norm, 128});
+      items.push_back({&Y.k_norm, 128});
+      items.push_back({&Y.wqkv, (qr + 2 * kvr) * H});
+      items.push_back({&Y.wo, H * qr});
+      items.push_back({&Y.wgu, 2ull * d_.I_l * H});
+      items.push_back({&Y.wd, H * d_.I_l});
+    }
+    uint64_t offset = 0;
+    std::vector<uint64_t> offsets;
+    for (const Item &it : items) {
+      offset = align_up(offset, 4096);
+      offsets.push_back(offset);
+      offset += it.elems * 2;
+    }
+    weights_bytes_ = offset;
+    embed_bytes_ = static_cast<uint64_t>(s.vocab_size) * H * 2;
+    uint8_t *arena = dev_alloc<uint8_t>(offset);
+    for (size_t i = 0; i < items.size(); ++i) *items[i].slot = reinterpret_cast<uint16_t *>(arena + offsets[i]);
+    if (s.tie_word_embeddings) lm_head_ = embed_ + static_cast<uint64_t>(d_.v_offset) * H;
+
+    const uint64_t cache_layer = static_cast<uint64_t>(max_seq_) * kvr;
+    uint16_t *kc = dev_alloc<uint16_t>(cache_layer * L), *vc = dev_alloc<uint16_t>(cache_layer * L);
+    CK(cudaMemset(kc, 0, cache_layer * L * 2));
+    CK(cudaMemset(vc, 0, cache_layer * L * 2));
+    for (uint64_t l = 0; l < L; ++l) {
+      layers_[l].kcache = kc + l * cache_layer;
+      layers_[l].vcache = vc + l * cache_layer;
+    }
+    cos_ = dev_alloc<uint16_t>(static_cast<uint64_t>(max_seq_) * 128);
+    sin_ = dev_alloc<uint16_t>(static_cast<uint64_t>(max_seq_) * 128);
+
+    const uint32_t npc = pos_chunks(max_seq_);
+    const uint64_t rows_qkv = qr + 2 * kvr;
+    b_ = DecodeBuffers{};
+    b_.x = dev_alloc<bf16>(H);
+    b_.q = dev_alloc<bf16>(qr);
+    b_.attn = dev_alloc<bf16>(qr);
+    b_.h = dev_alloc<bf16>(d_.I_l);
+    b_.part_qkv = dev_alloc<float>(d_.qkv_splits * rows_qkv);
+    b_.part = dev_alloc<float>(kCanonChunks * H);
+    b_.scores = dev_alloc<float>(static_cast<uint64_t>(d_.QH_l) * max_seq_);
+    b_.stats = dev_alloc<float>(static_cast<uint64_t>(d_.QH_l) * npc * 2);
+    b_.attn_part = dev_alloc<float>(static_cast<uint64_t>(d_.QH_l) * npc * 128);
+    const uint32_t lm_ctas = lmhead_ctas(d_);
+    b_.lm_best = dev_alloc<ArgBest>(lm_ctas);
+    b_.lm_bad = dev_alloc<uint32_t>(lm_ctas);
+    logits_ = dev_alloc<uint16_t>(d_.V_l);
+    b_.logits = logits_;
+    const uint64_t heads_qkv = d_.QH_l + 2ull * d_.KVH_l;
+    unsigned *counters = dev_alloc<unsigned>(heads_qkv + d_.KVH_l + H / kTileRows + 1);
+    CK(cudaMemset(counters, 0, (heads_qkv + d_.KVH_l + H / kTileRows + 1) * sizeof(unsigned)));
+    b_.cnt_qkv = counters;
+    b_.cnt_attn = counters + heads_qkv;
+    b_.cnt_tile = b_.cnt_attn + d_.KVH_l;
+    b_.cnt_lm = b_.cnt_tile + H / kTileRows;
+    state_ = dev_alloc<DecodeState>(1);
+    CK(cudaMemset(state_, 0, sizeof(DecodeState)));
+    b_.state = state_;
+    prompt_ = dev_alloc<uint32_t>(max_seq_);
+    log_ = dev_alloc<uint32_t>(max_seq_);
+    b_.prompt = prompt_;
+    b_.log = log_;
+    b_.cos_t = reinterpret_cast<const bf16 *>(cos_);
+    b_.sin_t = reinterpret_cast<const bf16 *>(sin_);
+    b_.embed = reinterpret_cast<const bf16 *>(embed_);
+    b_.final_norm = reinterpret_cast<const bf16 *>(final_norm_);
+    b_.lm_head = reinterpret_cast<const bf16 *>(lm_head_);
+    CK(cudaMallocHost(&host_state_, sizeof(DecodeState)));
+  }
+
+  // RoPE tables as transformers builds them (FP32 inv_freq = 1/theta^(2i/128),
+  // FP32 angle, FP32 cos/sin, bf16), frequency d % 64 for dimension d.
+  void upload_rope() {
+    std::vector<uint16_t> c(static_cast<size_t>(max_seq_) * 128), s(c.size());
+    float inv[64];
+    const float theta = static_cast<float>(shape_.rope_theta);
+    for (int i = 0; i < 64; ++i) inv[i] = 1.0f / std::pow(theta, static_cast<float>(2 * i) / 128.0f);
+    for (uint32_t p = 0; p < max_seq_; ++p)
+      for (uint32_t dd = 0; dd < 128; ++dd) {
+        const float angle = static_cast<float>(p) * inv[dd % 64];
+        c[static_cast<size_t>(p) * 128 + dd] = host_bf16(std::cos(angle));
+        s[static_cast<size_t>(p) * 128 + dd] = host_bf16(std::sin(angle));
+      }
+    CK(cudaMemcpy(cos_, c.data(), c.size() * 2, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(sin_, s.data(), s.size() * 2, cudaMemcpyHostToDevice));
+  }
+
+  LayerWeights layer_weights(uint32_t l) const {
+    const Layer &Y = layers_[l];
+    auto c = [](const uint16_t *p) { return reinterpret_cast<const bf16 *>(p); };
+    return LayerWeights{c(Y.in_norm), c(Y.post_norm), c(Y.q_norm), c(Y.k_norm), c(Y.wqkv), c(Y.wo),
+                        c(Y.wgu), c(Y.wd), reinterpret_cast<bf16 *>(Y.kcache),
+                        reinterpret_cast<bf16 *>(Y.vcache)};
+  }
+
+  void record_step(cudaStream_t s) {
+    CK(launch_embed(d_, b_, s));
+    for (uint32_t l = 0; l < shape_.num_hidden_layers; ++l) {
+      const LayerWeights w = layer_weights(l);
+      CK(launch_qkv(d_, b_, w, s));
+      CK(launch_attention(d_, b_, w, s));
+      CK(launch_oproj(d_, b_, w, s));
+      CK(launch_gateup(d_, b_, w, s));
+      CK(launch_down(d_, b_, w, s));
+    }
+    CK(launch_lmhead(d_, b_, s));
+  }
+
+  void ensure_graph() {
+    if (!loaded_) throw InvalidArg("no weights: call init_synthetic, load a checkpoint or set every tensor");
+    if (graph_exec_) return;
+    CK(cudaSetDevice(device_));
+    cudaGraph_t graph = nullptr;
+    CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    try {
+      record_step(stream_);
+    } catch (...) {
+      cudaStreamEndCapture(stream_, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      throw;
+    }
+    CK(cudaStreamEndCapture(stream_, &graph));
+    const cudaError_t e = cudaGraphInstantiate(&graph_exec_, graph, 0);
+    cudaGraphDestroy(graph);
+    CK(e);
+  }
+
+  xpu_qwen3_shape shape_;
+  uint32_t max_seq_;
+  int device_;
+  uint32_t rank_, tp_;
+  DecodeDims d_{};
+  DecodeBuffers b_{};
+  cudaStream_t stream_ = nullptr;
+  cudaGraphExec_t graph_exec_ = nullptr;
+  std::vector<void *> allocations_;
+  std::vector<Layer> layers_;
+  uint16_t *embed_ = nullptr, *final_norm_ = nullptr, *lm_head_ = nullptr;
+  uint16_t *cos_ = nullptr, *sin_ = nullptr, *logits_ = nullptr;
+  uint32_t *prompt_ = nullptr, *log_ = nullptr;
+  DecodeState *state_ = nullptr, *host_state_ = nullptr;
+  uint64_t weights_bytes_ = 0, embed_bytes_ = 0;
+  size_t tensors_set_ = 0;
+  bool loaded_ = false;
+};
+
+}  // namespace xpu
+
+// ------------------------------------------------------------- C ABI ----
+using xpu::Qwen3Engine;
+
+struct xpu_qwen3_engine {
+  std::unique_ptr<Qwen3Engine> impl;
+};
+
+namespace {
+
+template <typename F>
+int guarded(F &&f) {
+  try {
+    f();
+    return XPU_OK;
+  } catch (const xpu::CudaError &e) {
+    return xpu::fail(e.code == cudaErrorMemoryAllocation ? XPU_ERR_NO_MEMORY : XPU_ERR_CUDA, e.what());
+  } catch (const xpu::InvalidArg &e) {
+    return xpu::fail(XPU_ERR_INVALID, e.what());
+  } catch (const std::exception &e) {
+    return xpu::fail(XPU_ERR_INVALID, e.what());
+  } catch (...) {
+    return xpu::fail(XPU_ERR_INVALID, "unknown exception");
+  }
+}
+
+Qwen3Engine &eng(xpu_qwen3_engine *e) {
+  if (!e || !e->impl) throw xpu::InvalidArg("null engine");
+  return *e->impl;
+}
+
+}  // namespace
+
+extern "C" {
+
+int xpu_qwen3_create(const xpu_qwen3_shape *shape, uint32_t maximum_sequence, int device,
+                     uint32_t tp_rank, uint32_t tp_size, xpu_qwen3_engine **out) {
+  return guarded([&] {
+    if (!shape || !out) throw xpu::InvalidArg("xpu_qwen3_create: null pointer");
+    *out = nullptr;
+    auto holder = std::make_unique<xpu_qwen3_engine>();
+    holder->impl = std::make_unique<Qwen3Engine>(*shape, maximum_sequence, device, tp_rank, tp_size);
+    *out = holder.release();
+  });
+}
+
+int xpu_qwen3_destroy(xpu_qwen3_engine *engine) {
+  return guarded([&] { delete engine; });
+}
+
+int xpu_qwen3_init_synthetic(xpu_qwen3_engine *engine, uint64_t seed, float stddev) {
+  return guarded([&] { eng(engine).init_synthetic(seed, stddev); });
+}
+
+int xpu_qwen3_set_tensor(xpu_qwen3_engine *engine, const char *name, const uint16_t *host_bf16,
+                         uint64_t elements) {
+  return guarded([&] {
+    if (!name || !host_bf16) throw xpu::InvalidArg("xpu_qwen3_set_tensor: null pointer");
+    eng(engine).set_tensor(name, host_bf16, elements);
+  });
+}
+
+int xpu_qwen3_decode(xpu_qwen3_engine *engine, uint32_t token, uint32_t position, uint32_t *next_token) {
+  int status = guarded([&] {
+    if (!next_token) throw xpu::InvalidArg("xpu_qwen3_decode: null pointer");
+    *next_token = eng(engine).decode(token, position);
+  });
+  if (status == XPU_OK && *next_token == 0xffffffffu)
+    return xpu::fail(XPU_ERR_NONFINITE, "model produced a NaN or infinity in vocabulary logits");
+  return status;
+}
+
+int xpu_qwen3_generate(xpu_qwen3_engine *engine, const uint32_t *prompt, uint32_t prompt_len,
+                       uint32_t max_new_tokens, int stop_at_eos, uint32_t *out_tokens,
+                       uint32_t *out_count) {
+  int status = guarded([&] {
+    if (!prompt || !out_count || (max_new_tokens && !out_tokens))
+      throw xpu::InvalidArg("xpu_qwen3_generate: null pointer");
+    *out_count = eng(engine).generate(prompt, prompt_len, max_new_tokens, out_tokens, stop_at_eos != 0);
+  });
+  if (status == XPU_OK && *out_count && out_tokens[*out_count - 1] == 0xffffffffu)
+    return xpu::fail(XPU_ERR_NONFINITE, "model produced a NaN or infinity in vocabulary logits");
+  return status;
+}
+
+int xpu_qwen3_set_state(xpu_qwen3_engine *engine, uint32_t token, uint32_t position, uint32_t prompt_len) {
+  return guarded([&] { eng(engine).set_state(token, position, prompt_len); });
+}
+
+int xpu_qwen3_get_state(xpu_qwen3_engine *engine, uint32_t *token, uint32_t *position, uint32_t *error) {
+  return guarded([&] {
+    const xpu::DecodeState s = eng(engine).get_state();
+    if (token) *token = s.next;
+    if (position) *position = s.position;
+    if (error) *error = s.error;
+  });
+}
+
+int xpu_qwen3_enqueue_steps(xpu_qwen3_engine *engine, uint32_t steps, void *stream) {
+  return guarded([&] { eng(engine).enqueue_steps(steps, static_cast<cudaStream_t>(stream)); });
+}
+
+int xpu_qwen3_logits(xpu_qwen3_engine *engine, uint16_t *host_out, uint32_t count) {
+  return guarded([&] {
+    if (!host_out) throw xpu::InvalidArg("xpu_qwen3_logits: null pointer");
+    eng(engine).logits(host_out, count);
+  });
+}
+
+int xpu_qwen3_info(xpu_qwen3_engine *engine, xpu_qwen3_info_t *info) {
+  return guarded([&] {
+    if (!info) throw xpu::InvalidArg("xpu_qwen3_info: null pointer");
+    Qwen3Engine &e = eng(engine);
+    info->weight_bytes = e.weight_bytes();
+    info->kernels_per_step = e.kernels_per_step();
+    info->vocab_rows = e.dims().V_l;
+    info->vocab_offset = e.dims().v_offset;
+    info->stream = e.stream();
+  });
+}
+
+uint64_t xpu_qwen3_bytes_per_token(xpu_qwen3_engine *engine, uint32_t context) {
+  if (!engine || !engine->impl) return 0;
+  return engine->impl->bytes_per_token(context);
+}
+
+int xpu_qwen3_synchronize(xpu_qwen3_engine *engine) {
+  return guarded([&] { eng(engine).sync(); });
+}
+
+}  // extern "C"

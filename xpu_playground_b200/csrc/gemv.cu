@@ -10,6 +10,7 @@
 // Rows whose K is not a multiple of 8, or whose base is not 16-byte aligned,
 // take the scalar kernel below (same FP32 math, one element per lane step).
 #include "common.cuh"
+#include "gemv_core.cuh"
 #include "xpu_internal.h"
 
 namespace xpu {
@@ -37,30 +38,7 @@ gemv_vec_kernel(const T *__restrict__ A, const T *__restrict__ x, T *__restrict_
     rows[r] = reinterpret_cast<const uint4 *>(A + static_cast<size_t>(row) * k);
   }
   float acc[ROWS];
-#pragma unroll
-  for (int r = 0; r < ROWS; ++r) acc[r] = 0.f;
-
-  uint32_t c = lane;
-  for (; c + 32 * (UNROLL - 1) < chunks; c += 32 * UNROLL) {
-    uint4 a[ROWS][UNROLL];
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r)
-#pragma unroll
-      for (int u = 0; u < UNROLL; ++u) a[r][u] = ld_stream16(rows[r] + c + 32 * u);
-#pragma unroll
-    for (int u = 0; u < UNROLL; ++u) {
-      const uint4 xv = xs[c + 32 * u];
-#pragma unroll
-      for (int r = 0; r < ROWS; ++r) acc[r] = dot8<T>(a[r][u], xv, acc[r]);
-    }
-  }
-  for (; c < chunks; c += 32) {
-    const uint4 xv = xs[c];
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r) acc[r] = dot8<T>(ld_stream16(rows[r] + c), xv, acc[r]);
-  }
-#pragma unroll
-  for (int r = 0; r < ROWS; ++r) acc[r] = warp_sum(acc[r]);
+  warp_dot_rows<T, ROWS, UNROLL>(rows, xs, chunks, lane, acc);
   if (lane == 0) {
 #pragma unroll
     for (int r = 0; r < ROWS; ++r)

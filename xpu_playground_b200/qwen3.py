@@ -1,0 +1,108 @@
+"""Python face of the Qwen3 decode engine (xpu_qwen3_* in include/xpu_cuda.h).
+
+Mirrors the reference's Engine (qwen3/main.cpp:118-329): construct it for a
+shape and a maximum sequence length, load weights (a seeded synthetic
+checkpoint, per-tensor host uploads, or a safetensors directory through the
+C++ loader), then ``decode(token, position) -> next token``. ``generate``
+runs prompt + greedy generation device-resident (one host sync).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from .qwen3_config import WEIGHT_STD, Qwen3Shape
+
+XPU_ERR_NONFINITE = _lib.XPU_ERR_NONFINITE
+
+
+def shape_struct(shape: Qwen3Shape) -> _lib.Qwen3ShapeC:
+    return _lib.Qwen3ShapeC(shape.hidden, shape.intermediate, shape.layers, shape.q_heads,
+                            shape.kv_heads, shape.vocab, int(shape.tied), shape.eps,
+                            shape.rope_theta)
+
+
+class Qwen3Engine:
+    def __init__(self, shape: Qwen3Shape, max_seq: int, device: int = 0, tp_rank: int = 0,
+                 tp_size: int = 1):
+        self.lib = _lib.load()
+        self.shape, self.max_seq = shape, max_seq
+        self._h = ctypes.c_void_p()
+        self._shape_c = shape_struct(shape)
+        _lib.check(self.lib.xpu_qwen3_create(ctypes.byref(self._shape_c), max_seq, device, tp_rank,
+                                             tp_size, ctypes.byref(self._h)))
+
+    def close(self) -> None:
+        if self._h:
+            _lib.check(self.lib.xpu_qwen3_destroy(self._h))
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # ------------------------------------------------------------ weights ----
+    def init_synthetic(self, seed: int, std: float = WEIGHT_STD) -> None:
+        _lib.check(self.lib.xpu_qwen3_init_synthetic(self._h, seed, std))
+
+    def set_tensor(self, name: str, bits: np.ndarray) -> None:
+        a = np.ascontiguousarray(bits, dtype=np.uint16)
+        _lib.check(self.lib.xpu_qwen3_set_tensor(self._h, name.encode(), a.ctypes.data, a.size))
+
+    def load_weights(self, weights: dict[str, np.ndarray]) -> None:
+        for name, bits in weights.items():
+            self.set_tensor(name, bits)
+
+    # ------------------------------------------------------------- decode ----
+    def decode(self, token: int, position: int) -> int:
+        out = ctypes.c_uint32()
+        _lib.check(self.lib.xpu_qwen3_decode(self._h, token, position, ctypes.byref(out)))
+        return out.value
+
+    def generate(self, prompt: list[int], max_new_tokens: int, stop_at_eos: bool = False) -> list[int]:
+        p = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.zeros(max(max_new_tokens, 1), np.uint32)
+        count = ctypes.c_uint32()
+        _lib.check(self.lib.xpu_qwen3_generate(self._h, p.ctypes.data, p.size, max_new_tokens,
+                                               int(stop_at_eos), out.ctypes.data, ctypes.byref(count)))
+        return [int(t) for t in out[:count.value]]
+
+    def set_state(self, token: int, position: int, prompt_len: int = 0) -> None:
+        _lib.check(self.lib.xpu_qwen3_set_state(self._h, token, position, prompt_len))
+
+    def enqueue_steps(self, steps: int, stream: int | None = None) -> None:
+        _lib.check(self.lib.xpu_qwen3_enqueue_steps(self._h, steps, stream))
+
+    def state(self) -> tuple[int, int, int]:
+        tok, pos, err = ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_uint32()
+        _lib.check(self.lib.xpu_qwen3_get_state(self._h, ctypes.byref(tok), ctypes.byref(pos),
+                                                ctypes.byref(err)))
+        return tok.value, pos.value, err.value
+
+    def synchronize(self) -> None:
+        _lib.check(self.lib.xpu_qwen3_synchronize(self._h))
+
+    def logits(self) -> np.ndarray:
+        info = self.info()
+        out = np.empty(info.vocab_rows, np.uint16)
+        _lib.check(self.lib.xpu_qwen3_logits(self._h, out.ctypes.data, out.size))
+        return out
+
+    def info(self) -> _lib.Qwen3InfoC:
+        info = _lib.Qwen3InfoC()
+        _lib.check(self.lib.xpu_qwen3_info(self._h, ctypes.byref(info)))
+        return info
+
+    def bytes_per_token(self, context: int) -> int:
+        return int(self.lib.xpu_qwen3_bytes_per_token(self._h, context))

@@ -115,6 +115,10 @@ PRESETS: dict[str, Qwen3Shape] = {
     # 36 layers, hidden 4096, 32/8 heads, I 12288, untied.
     "qwen3-8b": Qwen3Shape(hidden=4096, intermediate=12288, layers=36, q_heads=32, kv_heads=8,
                            vocab=151936, tied=False),
+    # Qwen3-8B layer and vocabulary shapes, two layers: the 8B kernels' tiling
+    # (split-K QKV, 8 x 512 / 8 x 1536 canonical chunks) at CPU-checkable cost.
+    "qwen3-8b-l2": Qwen3Shape(hidden=4096, intermediate=12288, layers=2, q_heads=32, kv_heads=8,
+                              vocab=151936, tied=False),
     # Small shapes for CPU-checked parity tests.
     "tiny": Qwen3Shape(hidden=256, intermediate=768, layers=2, q_heads=4, kv_heads=2,
                        vocab=4096, tied=False),
