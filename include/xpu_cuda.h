@@ -184,6 +184,14 @@ int xpu_qwen3_enqueue_steps(xpu_qwen3_engine *engine, uint32_t steps, void *stre
 int xpu_qwen3_get_state(xpu_qwen3_engine *engine, uint32_t *last_token, uint32_t *next_position,
                         uint32_t *error);
 int xpu_qwen3_synchronize(xpu_qwen3_engine *engine);
+/* Decode-step implementation: 0 = one persistent cooperative kernel per
+ * token (default), 1 = a CUDA graph of per-phase kernels. Identical results;
+ * set before the first decode. */
+int xpu_qwen3_set_mode(xpu_qwen3_engine *engine, int mode);
+/* Step tracing (persistent mode, when the process runs with XPU_STEP_TRACE=1):
+ * per-CTA globaltimer stamps (ns) of the last step's phase boundaries,
+ * [cta][event]; *count = total stamps available (0 when tracing is off). */
+int xpu_qwen3_trace(xpu_qwen3_engine *engine, uint64_t *host_ns, uint32_t capacity, uint32_t *count);
 /* bf16 logits of the last step (this rank's vocab_rows rows). */
 int xpu_qwen3_logits(xpu_qwen3_engine *engine, uint16_t *host_out, uint32_t count);
 int xpu_qwen3_info(xpu_qwen3_engine *engine, xpu_qwen3_info_t *info);

@@ -30,7 +30,7 @@ constexpr uint32_t kHD = 128;            // head_dim
 constexpr uint32_t kCanonChunks = 8;     // K chunks of the row-parallel GEMVs
 constexpr uint32_t kPosChunk = 128;      // positions per attention chunk
 constexpr uint32_t kDecThreads = 256;    // threads per decode-GEMV CTA
-constexpr uint32_t kTileRows = 16;       // rows per decode-GEMV tile (8 warps x 2)
+constexpr uint32_t kTileRows = 32;       // rows per streamed row tile (8 warps x 4)
 constexpr float kAttnScale = 0.08838834764831845f;  // 1/sqrt(128)
 
 typedef __nv_bfloat16 bf16;
@@ -44,7 +44,7 @@ struct DecodeState {
   uint32_t next;        // greedy token of the last step (0xffffffff on NaN/Inf)
   uint32_t error;       // sticky: 1 = NaN/Inf logits, 2 = exchange timeout
   uint32_t steps;       // completed steps since the last reset
-  uint32_t pad[2];
+  uint64_t bar_base;    // grid-barrier arrivals before this step (persistent path)
 };
 
 struct DecodeDims {
@@ -86,7 +86,7 @@ struct DecodeBuffers {
   uint16_t *logits;  // [V_l] bf16 bits
   unsigned *cnt_qkv; // [heads_qkv]
   unsigned *cnt_attn;// [KVH_l]
-  unsigned *cnt_tile;// [H / 16]
+  unsigned *cnt_tile;// [H / 32]
   unsigned *cnt_lm;  // [1]
   DecodeState *state;
   const uint32_t *prompt;  // [max_seq]
@@ -96,6 +96,8 @@ struct DecodeBuffers {
   const bf16 *final_norm;
   const bf16 *lm_head;     // [V_l][H]
 };
+
+__host__ __device__ inline uint32_t pos_chunks_dev(uint32_t max_seq) { return (max_seq + kPosChunk - 1) / kPosChunk; }
 
 // Launchers (decode_kernels.cu). Each returns the launch error.
 cudaError_t launch_embed(const DecodeDims &d, const DecodeBuffers &b, cudaStream_t s);
@@ -113,6 +115,19 @@ cudaError_t launch_lmhead(const DecodeDims &d, const DecodeBuffers &b, cudaStrea
 
 // Number of CTAs the lm_head kernel launches (sizes lm_best / lm_bad).
 uint32_t lmhead_ctas(const DecodeDims &d);
+
+// Persistent single-kernel decode step (decode_step.cu): one cooperative
+// CTA per SM runs every layer, with grid barriers between phases.
+struct StepPlan;
+cudaError_t step_plan_create(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights *layers, uint32_t n_layers,
+                             StepPlan **plan);
+void step_plan_destroy(StepPlan *plan);
+cudaError_t launch_step(const StepPlan *plan, cudaStream_t s);
+uint32_t step_grid(const StepPlan *plan);
+// Phase timestamps of the last step (XPU_STEP_TRACE=1): returns the count.
+uint32_t step_trace(const StepPlan *plan, uint64_t *host, uint32_t capacity);
+// Re-arms the grid barrier (after a failed step or on reset).
+cudaError_t step_reset(const StepPlan *plan, cudaStream_t s);
 uint32_t pos_chunks(uint32_t max_seq);
 
 }  // namespace xpu

@@ -1,0 +1,470 @@
+// Device-side building blocks of the Qwen3 decode step, shared by the
+// multi-kernel CUDA-graph path (decode_kernels.cu) and the persistent
+// single-kernel path (decode_step.cu), so that both compute bit-identical
+// results.
+//
+// Thread conventions: a CTA is the producer warp (warp 0, see stream.cuh)
+// plus kConsumerWarps consumer warps; everything here runs on the consumer
+// warps (ctid() = threadIdx.x - 32) and synchronises with consumer_sync().
+// Data written by other CTAs during the same step (activations, partial
+// sums, the new KV-cache row) is read through L2 with ld.global.cg.
+#pragma once
+
+#include "decode.cuh"
+#include "stream.cuh"
+
+namespace xpu {
+namespace dec {
+
+__device__ __forceinline__ uint32_t ctid() { return threadIdx.x - 32; }
+__device__ __forceinline__ uint32_t cwarp() { return (threadIdx.x >> 5) - 1; }
+__device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31; }
+
+__device__ __forceinline__ uint4 ldcg16(const void *p) { return __ldcg(reinterpret_cast<const uint4 *>(p)); }
+__device__ __forceinline__ uint2 ldcg8(const void *p) { return __ldcg(reinterpret_cast<const uint2 *>(p)); }
+__device__ __forceinline__ float bfcg(const bf16 *p, size_t i) {
+  return bf16_bits_to_float(__ldcg(reinterpret_cast<const unsigned short *>(p) + i));
+}
+// Constant-per-step data (norm weights, RoPE tables).
+__device__ __forceinline__ float bf(const bf16 *p, size_t i) {
+  return bf16_bits_to_float(reinterpret_cast<const uint16_t *>(p)[i]);
+}
+__device__ __forceinline__ void put(bf16 *p, size_t i, float v) {
+  reinterpret_cast<uint16_t *>(p)[i] = float_to_bf16_bits(v);
+}
+
+__device__ __forceinline__ float sq8(const uint4 &v, float ss) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float a = bf16_lo(w[j]), b = bf16_hi(w[j]);
+    ss = __fadd_rn(ss, __fmul_rn(a, a));
+    ss = __fadd_rn(ss, __fmul_rn(b, b));
+  }
+  return ss;
+}
+
+// transformers Qwen3RMSNorm into shared memory:
+// xs = bf16(w * bf16(x * RN(1/RN(sqrt(mean(x^2) + eps))))), over [0, H).
+// x is read from L2 once into xs; the sum of squares and the normalisation
+// then work on the shared copy.
+__device__ inline void stage_rms(const bf16 *x, const bf16 *w, uint32_t H, float eps, uint4 *xs, float *scratch) {
+  const uint32_t t = ctid();
+  float ss = 0.f;
+  for (uint32_t c = t; c < H / 8; c += kConsumerThreads) {
+    const uint4 v = ldcg16(x + 8 * c);
+    xs[c] = v;
+    ss = sq8(v, ss);
+  }
+  ss = consumer_sum(ss, scratch);
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(H) + eps);
+  const uint4 *w4 = reinterpret_cast<const uint4 *>(w);
+  for (uint32_t c = t; c < H / 8; c += kConsumerThreads) {
+    const uint4 xv = xs[c], wv = w4[c];
+    const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lo = round_bf16(__fmul_rn(bf16_lo(wa[j]), round_bf16(__fmul_rn(bf16_lo(xa[j]), r))));
+      const float hi = round_bf16(__fmul_rn(bf16_hi(wa[j]), round_bf16(__fmul_rn(bf16_hi(xa[j]), r))));
+      o[j] = pack_bf16x2(lo, hi);
+    }
+    xs[c] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  consumer_sync();
+}
+
+__device__ inline void stage_copy(const bf16 *x, uint32_t n, uint4 *xs) {
+  for (uint32_t c = ctid(); c < n / 8; c += kConsumerThreads) xs[c] = ldcg16(x + 8 * c);
+  consumer_sync();
+}
+
+// Deferred arrivals of this CTA's items (blockIdx.x + j * gridDim.x, j < mine)
+// on counters[item / per_counter]; s_last[j] = this CTA completed the counter.
+constexpr uint32_t kMaxLocalItems = 64;
+
+__device__ inline uint32_t arrive_items(unsigned *counters, uint32_t items, uint32_t per_counter, unsigned total,
+                                        uint8_t *s_last) {
+  const uint32_t mine = items > blockIdx.x ? (items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  const uint32_t n = mine < kMaxLocalItems ? mine : kMaxLocalItems;
+  __threadfence();
+  consumer_sync();
+  for (uint32_t j = ctid(); j < n; j += kConsumerThreads) {
+    const uint32_t item = blockIdx.x + j * gridDim.x;
+    s_last[j] = atomicAdd(counters + item / per_counter, 1u) == total - 1u;
+  }
+  consumer_sync();
+  __threadfence();
+  return n;
+}
+
+// Whole-CTA (consumer warps) publish-then-count on one counter.
+__device__ inline bool arrive_one(unsigned *counter, unsigned total, int *flag) {
+  __threadfence();
+  consumer_sync();
+  if (ctid() == 0) *flag = (atomicAdd(counter, 1u) == total - 1u);
+  consumer_sync();
+  const bool last = *flag != 0;
+  if (last) __threadfence();
+  return last;
+}
+
+__device__ __forceinline__ void flag_error(DecodeState *st, uint32_t bits) { atomicOr(&st->error, bits); }
+
+// ------------------------------------------------------------------ QKV ----
+// Items: (tile, split) of [Wq; Wk; Wv]; partial sums to part_qkv[split][row].
+__device__ inline bool qkv_items(const DecodeDims &d, const DecodeBuffers &b, const StreamSmem &sm,
+                                 const StreamGeom &g, uint32_t &it) {
+  const uint32_t lane = lane_id(), cw = cwarp();
+  for (uint32_t item = blockIdx.x; item < g.items(); item += gridDim.x) {
+    const uint32_t tile = item / g.kparts, part = item % g.kparts;
+    float acc[kRowsPerWarp];
+    if (!stream_consume_item<bf16>(sm, g, sm.xs + part * (g.kt / 8), it, acc)) return false;
+    const uint32_t row = tile * kStageRows + kRowsPerWarp * cw;
+    if (lane == 0)
+#pragma unroll
+      for (uint32_t r = 0; r < kRowsPerWarp; ++r) b.part_qkv[static_cast<size_t>(part) * g.rows + row + r] = acc[r];
+  }
+  return true;
+}
+
+// Finish head `head` of the QKV output with one warp (lane l owns dimensions
+// l, l+32, l+64, l+96, so both rotate-half pairs sit in one lane): sum the
+// splits, then q/k RMSNorm + RoPE (transformers rounding) into the q buffer /
+// key cache, or v into the value cache, at `pos`.
+__device__ inline void qkv_head_warp(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w,
+                                     uint32_t head, uint32_t pos) {
+  const uint32_t lane = lane_id();
+  const uint32_t rows_total = (d.QH_l + 2 * d.KVH_l) * kHD;
+  float v[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float y = 0.f;
+    for (uint32_t s = 0; s < d.qkv_splits; ++s)
+      y += __ldcg(b.part_qkv + static_cast<size_t>(s) * rows_total + head * kHD + lane + 32 * j);
+    v[j] = round_bf16(y);
+  }
+  if (head >= d.QH_l + d.KVH_l) {  // value head: straight into the cache
+    const size_t slot = (static_cast<size_t>(pos) * d.KVH_l + (head - d.QH_l - d.KVH_l)) * kHD;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) put(w.vcache, slot + lane + 32 * j, v[j]);
+    return;
+  }
+  const bool is_q = head < d.QH_l;
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(kHD) + d.eps);
+  const bf16 *nw = is_q ? w.q_norm : w.k_norm;
+  float nv[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) nv[j] = round_bf16(__fmul_rn(bf(nw, lane + 32 * j), round_bf16(__fmul_rn(v[j], r))));
+  const bf16 *cr = b.cos_t + static_cast<size_t>(pos) * kHD, *sr = b.sin_t + static_cast<size_t>(pos) * kHD;
+  float out[4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const uint32_t i = lane + 32 * j;  // pairs (i, i + 64): rotate_half
+    const float a = nv[j], c = nv[j + 2];
+    out[j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(a, bf(cr, i))), round_bf16(__fmul_rn(-c, bf(sr, i)))));
+    out[j + 2] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(c, bf(cr, i + 64))), round_bf16(__fmul_rn(a, bf(sr, i + 64)))));
+  }
+  bf16 *dst = is_q ? b.q + static_cast<size_t>(head) * kHD
+                   : w.kcache + (static_cast<size_t>(pos) * d.KVH_l + (head - d.QH_l)) * kHD;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) put(dst, lane + 32 * j, out[j]);
+}
+
+// Deferred arrivals of this CTA's QKV items; every head it completed is
+// finished by one warp (heads spread over the 8 consumer warps).
+__device__ inline void qkv_finish(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w,
+                                  const StreamGeom &g, uint32_t pos, uint8_t *s_last) {
+  const uint32_t per_head = g.kparts * (kHD / kStageRows);
+  const uint32_t n = arrive_items(b.cnt_qkv, g.items(), per_head, per_head, s_last);
+  uint32_t k = 0;
+  for (uint32_t j = 0; j < n; ++j) {
+    if (!s_last[j]) continue;
+    if (k++ % kConsumerWarps != cwarp()) continue;
+    const uint32_t head = (blockIdx.x + j * gridDim.x) / per_head;
+    qkv_head_warp(d, b, w, head, pos);
+    if (lane_id() == 0) b.cnt_qkv[head] = 0;
+  }
+  consumer_sync();
+}
+
+// ---------------------------------------------------- row-parallel (o, down) ----
+// Items: (tile, local chunk j) of W [H][K_l]; partials to part[chunk0 + j][row].
+__device__ inline bool rowpar_items(const DecodeDims &d, const DecodeBuffers &b, const StreamSmem &sm,
+                                    const StreamGeom &g, uint32_t &it) {
+  const uint32_t lane = lane_id(), cw = cwarp();
+  for (uint32_t item = blockIdx.x; item < g.items(); item += gridDim.x) {
+    const uint32_t tile = item / g.kparts, part = item % g.kparts, chunk = d.chunk0 + part;
+    float acc[kRowsPerWarp];
+    if (!stream_consume_item<bf16>(sm, g, sm.xs + part * (g.kt / 8), it, acc)) return false;
+    const uint32_t row = tile * kStageRows + kRowsPerWarp * cw;
+    if (lane == 0)
+#pragma unroll
+      for (uint32_t r = 0; r < kRowsPerWarp; ++r) b.part[static_cast<size_t>(chunk) * d.H + row + r] = acc[r];
+  }
+  return true;
+}
+
+// Residual epilogue of every row tile this CTA completed:
+// x = bf16(x + bf16(sum of the 8 canonical chunks, in chunk order)).
+__device__ inline void rowpar_finish(const DecodeDims &d, const DecodeBuffers &b, const StreamGeom &g,
+                                     uint8_t *s_last) {
+  const uint32_t n = arrive_items(b.cnt_tile, g.items(), g.kparts, g.kparts, s_last);
+  const uint32_t t = ctid();
+  for (uint32_t j0 = 0; j0 < n; j0 += kConsumerThreads / kStageRows) {
+    const uint32_t j = j0 + t / kStageRows;
+    if (j < n && s_last[j]) {
+      const uint32_t tile = (blockIdx.x + j * gridDim.x) / g.kparts;
+      const uint32_t r = tile * kStageRows + t % kStageRows;
+      float y = 0.f;
+      for (uint32_t c = 0; c < kCanonChunks; ++c) y += __ldcg(b.part + static_cast<size_t>(c) * d.H + r);
+      put(b.x, r, __fadd_rn(bfcg(b.x, r), round_bf16(y)));
+      if (t % kStageRows == 0) b.cnt_tile[tile] = 0;
+    }
+  }
+  consumer_sync();
+}
+
+// ------------------------------------------------------------- gate / up ----
+// Rows 2i, 2i+1 of Wgu are gate and up of unit i; warp cw of tile t holds
+// units i = 16t + 2cw and 16t + 2cw + 1: h = bf16(bf16(silu(bf16 g)) * bf16 u).
+__device__ inline bool gateup_items(const DecodeDims &d, const DecodeBuffers &b, const StreamSmem &sm,
+                                    const StreamGeom &g, uint32_t &it) {
+  const uint32_t lane = lane_id(), cw = cwarp();
+  for (uint32_t item = blockIdx.x; item < g.items(); item += gridDim.x) {
+    float acc[kRowsPerWarp];
+    if (!stream_consume_item<bf16>(sm, g, sm.xs, it, acc)) return false;
+    if (lane == 0)
+#pragma unroll
+      for (uint32_t u = 0; u < kRowsPerWarp / 2; ++u) {
+        const uint32_t i = item * (kStageRows / 2) + (kRowsPerWarp / 2) * cw + u;
+        if (i >= d.I_l) break;
+        const float gv = round_bf16(acc[2 * u]), uv = round_bf16(acc[2 * u + 1]);
+        const float act = round_bf16(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))));
+        put(b.h, i, __fmul_rn(act, uv));
+      }
+  }
+  consumer_sync();
+  return true;
+}
+
+// --------------------------------------------------------------- lm_head ----
+struct LmShared {
+  ArgBest wbest[kConsumerWarps];
+  uint32_t wbad[kConsumerWarps];
+  int flag;
+};
+
+// Logits of this CTA's rows, then the CTA's (max, lowest index) candidate;
+// the last CTA reduces all candidates (fixed order) into the greedy token
+// and advances the step state. Returns false on a timeout.
+__device__ inline bool lm_items_and_argmax(const DecodeDims &d, const DecodeBuffers &b, const StreamSmem &sm,
+                                           const StreamGeom &g, uint32_t &it, LmShared &ls, uint32_t pos,
+                                           uint64_t bar_advance) {
+  const uint32_t lane = lane_id(), cw = cwarp(), t = ctid();
+  ArgBest best{-INFINITY, 0xffffffffu};
+  uint32_t bad = 0;
+  for (uint32_t item = blockIdx.x; item < g.items(); item += gridDim.x) {
+    float acc[kRowsPerWarp];
+    if (!stream_consume_item<bf16>(sm, g, sm.xs, it, acc)) return false;
+    if (lane == 0) {
+#pragma unroll
+      for (uint32_t rr = 0; rr < kRowsPerWarp; ++rr) {
+        const uint32_t row = item * kStageRows + kRowsPerWarp * cw + rr;
+        if (row >= d.V_l) break;
+        const float v = round_bf16(acc[rr]);
+        b.logits[row] = float_to_bf16_bits(v);
+        bad |= not_finite(v) ? 1u : 0u;
+        best = arg_better(best, ArgBest{v, d.v_offset + row});
+      }
+    }
+  }
+  if (lane == 0) { ls.wbest[cw] = best; ls.wbad[cw] = bad; }
+  consumer_sync();
+  if (t == 0) {
+    ArgBest cb = ls.wbest[0];
+    uint32_t cbad = ls.wbad[0];
+    for (int i = 1; i < kConsumerWarps; ++i) { cb = arg_better(cb, ls.wbest[i]); cbad |= ls.wbad[i]; }
+    b.lm_best[blockIdx.x] = cb;
+    b.lm_bad[blockIdx.x] = cbad;
+  }
+  if (arrive_one(b.cnt_lm, gridDim.x, &ls.flag)) {
+    ArgBest tb{-INFINITY, 0xffffffffu};
+    uint32_t tbad = 0;
+    for (uint32_t i = t; i < gridDim.x; i += kConsumerThreads) {
+      ArgBest e;
+      e.value = __ldcg(&b.lm_best[i].value);
+      e.index = __ldcg(&b.lm_best[i].index);
+      tb = arg_better(tb, e);
+      tbad |= __ldcg(b.lm_bad + i);
+    }
+    tb = warp_argbest(tb);
+    tbad = __reduce_or_sync(kFullMask, tbad);
+    consumer_sync();
+    if (lane == 0) { ls.wbest[cw] = tb; ls.wbad[cw] = tbad; }
+    consumer_sync();
+    if (t == 0) {
+      ArgBest fb = ls.wbest[0];
+      uint32_t fbad = ls.wbad[0];
+      for (int i = 1; i < kConsumerWarps; ++i) { fb = arg_better(fb, ls.wbest[i]); fbad |= ls.wbad[i]; }
+      DecodeState *st = b.state;
+      const uint32_t next = (fbad || fb.index == 0xffffffffu) ? 0xffffffffu : fb.index;
+      if (next == 0xffffffffu) st->error |= 1u;
+      st->next = next;
+      st->token = next;
+      if (pos < d.max_seq) b.log[pos] = next;
+      st->bar_base += bar_advance;
+      st->steps += 1;
+      __threadfence();
+      st->position = pos + 1;
+      *b.cnt_lm = 0;
+    }
+  }
+  return true;
+}
+
+// ------------------------------------------------------------- attention ----
+// Item (kv head, 128-position chunk): 8 consumer warps x 16 positions; each
+// warp issues its 16 cache-row loads before using any.
+constexpr uint32_t kPosPerWarp = kPosChunk / kConsumerWarps;  // 16
+
+template <int G>
+struct AttnShared {
+  float sc[G][kPosChunk];
+  float sM[G], sInv[G];
+  float sacc[kConsumerWarps][G][kHD];
+  int flag;
+};
+
+// s = bf16(bf16(q.k) * scale) for the chunk's positions; chunk max and sum of
+// exp(s - max) into stats.
+template <int G>
+__device__ inline void scores_item(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w, uint32_t kvh,
+                                   uint32_t chunk, uint32_t nchunks, uint32_t n, AttnShared<G> &as) {
+  const uint32_t lane = lane_id(), cw = cwarp();
+  const uint32_t p0 = chunk * kPosChunk, p1 = min(p0 + kPosChunk, n);
+  const uint32_t pw = p0 + cw * kPosPerWarp;
+  uint2 kr[kPosPerWarp];
+#pragma unroll
+  for (uint32_t i = 0; i < kPosPerWarp; ++i) {
+    const uint32_t p = pw + i;
+    kr[i] = p < p1 ? ldcg8(w.kcache + (static_cast<size_t>(p) * d.KVH_l + kvh) * kHD + lane * 4) : make_uint2(0, 0);
+  }
+  float q[G][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const uint2 raw = ldcg8(b.q + (static_cast<size_t>(kvh) * G + g) * kHD + lane * 4);
+    q[g][0] = bf16_lo(raw.x); q[g][1] = bf16_hi(raw.x);
+    q[g][2] = bf16_lo(raw.y); q[g][3] = bf16_hi(raw.y);
+  }
+#pragma unroll
+  for (uint32_t i = 0; i < kPosPerWarp; ++i) {
+    const float k4[4] = {bf16_lo(kr[i].x), bf16_hi(kr[i].x), bf16_lo(kr[i].y), bf16_hi(kr[i].y)};
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s = fmaf(q[g][j], k4[j], s);
+      s = warp_sum(s);
+      if (lane == 0) as.sc[g][cw * kPosPerWarp + i] = round_bf16(__fmul_rn(round_bf16(s), kAttnScale));
+    }
+  }
+  consumer_sync();
+  for (uint32_t g = cw; g < static_cast<uint32_t>(G); g += kConsumerWarps) {
+    float m = -INFINITY;
+    for (uint32_t i = lane; i < p1 - p0; i += 32) m = fmaxf(m, as.sc[g][i]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (uint32_t i = lane; i < p1 - p0; i += 32) l += expf(as.sc[g][i] - m);
+    l = warp_sum(l);
+    const uint32_t h = kvh * G + g;
+    for (uint32_t i = lane; i < p1 - p0; i += 32) b.scores[static_cast<size_t>(h) * d.max_seq + p0 + i] = as.sc[g][i];
+    if (lane == 0) {
+      b.stats[(static_cast<size_t>(h) * nchunks + chunk) * 2] = m;
+      b.stats[(static_cast<size_t>(h) * nchunks + chunk) * 2 + 1] = l;
+    }
+  }
+  consumer_sync();
+}
+
+// Probabilities bf16(exp(s - M) * (1 / S)) over all chunks' statistics, the
+// chunk's partial sum of p * v, and (last CTA of the kv head) the sum over
+// chunks into the attention output.
+template <int G>
+__device__ inline void pv_item(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w, uint32_t kvh,
+                               uint32_t chunk, uint32_t nchunks, uint32_t n, AttnShared<G> &as) {
+  const uint32_t lane = lane_id(), cw = cwarp(), t = ctid();
+  const uint32_t nch = (n + kPosChunk - 1) / kPosChunk;
+  const uint32_t p0 = chunk * kPosChunk, p1 = min(p0 + kPosChunk, n);
+  const uint32_t pw = p0 + cw * kPosPerWarp;
+  uint2 vr[kPosPerWarp];
+#pragma unroll
+  for (uint32_t i = 0; i < kPosPerWarp; ++i) {
+    const uint32_t p = pw + i;
+    vr[i] = p < p1 ? ldcg8(w.vcache + (static_cast<size_t>(p) * d.KVH_l + kvh) * kHD + lane * 4) : make_uint2(0, 0);
+  }
+  for (uint32_t g = cw; g < static_cast<uint32_t>(G); g += kConsumerWarps) {
+    const float *st = b.stats + static_cast<size_t>(kvh * G + g) * nchunks * 2;
+    float m = -INFINITY;
+    for (uint32_t c = lane; c < nch; c += 32) m = fmaxf(m, __ldcg(st + 2 * c));
+    m = warp_max(m);
+    float sum = 0.f;
+    for (uint32_t c = lane; c < nch; c += 32) sum += __ldcg(st + 2 * c + 1) * expf(__ldcg(st + 2 * c) - m);
+    sum = warp_sum(sum);
+    if (lane == 0) { as.sM[g] = m; as.sInv[g] = 1.0f / sum; }
+  }
+  consumer_sync();
+  for (uint32_t i = t; i < G * kPosChunk; i += kConsumerThreads) {
+    const uint32_t g = i / kPosChunk, j = i % kPosChunk, p = p0 + j;
+    as.sc[g][j] = p < p1 ? round_bf16(__fmul_rn(
+                               expf(__ldcg(b.scores + static_cast<size_t>(kvh * G + g) * d.max_seq + p) - as.sM[g]),
+                               as.sInv[g]))
+                         : 0.f;
+  }
+  consumer_sync();
+  float acc[G][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[g][j] = 0.f;
+#pragma unroll
+  for (uint32_t i = 0; i < kPosPerWarp; ++i) {
+    const float v4[4] = {bf16_lo(vr[i].x), bf16_hi(vr[i].x), bf16_lo(vr[i].y), bf16_hi(vr[i].y)};
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float prob = as.sc[g][cw * kPosPerWarp + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[g][j] = fmaf(prob, v4[j], acc[g][j]);
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) as.sacc[cw][g][lane * 4 + j] = acc[g][j];
+  consumer_sync();
+  for (uint32_t e = t; e < G * kHD; e += kConsumerThreads) {
+    const uint32_t g = e / kHD, dd = e % kHD;
+    float tot = 0.f;
+#pragma unroll
+    for (uint32_t ww = 0; ww < static_cast<uint32_t>(kConsumerWarps); ++ww) tot += as.sacc[ww][g][dd];
+    b.attn_part[(static_cast<size_t>(kvh * G + g) * nchunks + chunk) * kHD + dd] = tot;
+  }
+  if (arrive_one(b.cnt_attn + kvh, nch, &as.flag)) {
+    for (uint32_t e = t; e < G * kHD; e += kConsumerThreads) {
+      const uint32_t g = e / kHD, dd = e % kHD;
+      const float *src = b.attn_part + static_cast<size_t>(kvh * G + g) * nchunks * kHD + dd;
+      float o = 0.f;
+      for (uint32_t c = 0; c < nch; ++c) o += __ldcg(src + static_cast<size_t>(c) * kHD);
+      put(b.attn, static_cast<size_t>(kvh * G + g) * kHD + dd, o);
+    }
+    if (t == 0) b.cnt_attn[kvh] = 0;
+  }
+  consumer_sync();
+}
+
+}  // namespace dec
+}  // namespace xpu

@@ -1,0 +1,342 @@
+// Persistent single-kernel Qwen3 decode step.
+//
+// One cooperative launch per token: exactly one CTA per SM (co-residency is
+// what makes the grid barriers below safe), each CTA = the TMA producer warp
+// plus 8 consumer warps. The producer streams this CTA's share of every
+// weight matrix of every layer - QKV, o_proj, gate/up, down, ..., lm_head -
+// through one shared-memory ring, in the order the consumers will need them,
+// without ever waiting for the consumers' phases: while the consumers sit in
+// a grid barrier or run attention (which reads no weights), the ring keeps
+// filling with the next matrix, so HBM never idles between phases and no
+// kernel launch, prologue or tail separates them.
+//
+// Phases per layer (grid barrier after each): qkv (+ per-head q/k norm,
+// RoPE, cache write by the last CTA of the head), attention scores,
+// attention p.v (+ chunk combine by the last CTA of the kv head), o_proj
+// (+ residual by the last CTA of each row tile), gate/up + SwiGLU, down
+// (+ residual); then lm_head + argmax. The per-item math is the same code as
+// the multi-kernel path (decode_device.cuh), so both give identical bits.
+//
+// Grid barrier: a monotonic 64-bit arrival counter; barrier k of a step
+// completes at bar_base + k * gridDim.x arrivals, where bar_base (in the step
+// state) is advanced by the CTA that finishes the step. Waits are bounded
+// (kWaitCycles); a timeout sets error bit 4, every other waiter sees it and
+// leaves, and the host re-arms the barrier.
+#include <cstdlib>
+#include <vector>
+
+#include "decode_device.cuh"
+#include "xpu_internal.h"
+
+namespace xpu {
+
+struct StepGeoms {
+  StreamGeom qkv, o, gu, down, lm;
+};
+
+struct StepParams {
+  DecodeDims d;
+  DecodeBuffers b;
+  const LayerWeights *layers;  // [n_layers] (device)
+  const CUtensorMap *maps;     // [4 * n_layers + 1] (device): qkv, o, gate/up, down per layer; lm_head
+  StepGeoms g;
+  unsigned long long *bar;     // grid-barrier arrival counter (device)
+  uint32_t n_layers;
+  uint32_t x_elems;            // capacity (bf16 elements) of the staging/attention region
+  uint64_t *trace;             // optional: [gridDim.x][trace_events] globaltimer stamps
+  uint32_t trace_events;
+};
+
+struct StepPlan {
+  StepParams p;
+  LayerWeights *d_layers = nullptr;
+  CUtensorMap *d_maps = nullptr;
+  unsigned long long *d_bar = nullptr;
+  uint32_t grid = 0;
+  size_t smem = 0;
+  int group = 0;
+};
+
+namespace {
+
+using namespace dec;
+
+// XPU_STEP_TRACE=1 records per-CTA phase timestamps (read with xpu_qwen3_trace).
+bool trace_enabled() {
+  const char *v = getenv("XPU_STEP_TRACE");
+  return v && v[0] == '1';
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ bool grid_barrier(unsigned long long *counter, unsigned long long target, DecodeState *st, int *flag) {
+  __threadfence();
+  consumer_sync();
+  if (ctid() == 0) {
+    atomicAdd(counter, 1ull);
+    bool ok = false;
+    const long long start = clock64();
+    while (true) {
+      unsigned long long v;
+      asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(counter) : "memory");
+      if (v >= target) { ok = true; break; }
+      if (*reinterpret_cast<volatile uint32_t *>(&st->error) & kErrPipelineTimeout) break;
+      if (clock64() - start > kWaitCycles) { atomicOr(&st->error, kErrPipelineTimeout); break; }
+    }
+    *flag = ok;
+  }
+  consumer_sync();
+  return *flag != 0;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constant__ StepParams p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __shared__ uint8_t s_last[kMaxLocalItems];
+  __shared__ LmShared ls;
+  __shared__ int bflag;
+  const DecodeDims &d = p.d;
+  const DecodeBuffers &b = p.b;
+  DecodeState *st = b.state;
+  const StreamSmem sm = stream_smem(smem_raw, p.g.qkv, p.x_elems);
+  if (!stream_init(sm, p.g.qkv)) {
+    if (threadIdx.x == 0) flag_error(st, kErrPipelineTimeout);
+    return;
+  }
+  if (threadIdx.x < 32) {  // producer: every weight stage of this CTA, in consumption order
+    if (threadIdx.x == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (uint32_t l = 0; ok && l < p.n_layers; ++l) {
+        ok = stream_produce(sm, p.g.qkv, p.maps + 4 * l, it) && stream_produce(sm, p.g.o, p.maps + 4 * l + 1, it) &&
+             stream_produce(sm, p.g.gu, p.maps + 4 * l + 2, it) && stream_produce(sm, p.g.down, p.maps + 4 * l + 3, it);
+      }
+      if (ok) ok = stream_produce(sm, p.g.lm, p.maps + 4 * p.n_layers, it);
+      if (!ok) flag_error(st, kErrPipelineTimeout);
+    }
+    return;
+  }
+  const uint32_t pos = st->position, n = pos + 1;
+  const unsigned long long bar_base = st->bar_base;
+  uint32_t tok = pos < st->prompt_len ? b.prompt[pos] : st->token;
+  if (tok >= d.vocab) {
+    if (blockIdx.x == 0 && ctid() == 0) flag_error(st, 1u);
+    tok = 0;
+  }
+  const bf16 *x_embed = b.embed + static_cast<size_t>(tok) * d.H;
+  if (blockIdx.x == 0)  // the residual stream starts as the embedding row
+    for (uint32_t c = ctid(); c < d.H / 8; c += kConsumerThreads)
+      reinterpret_cast<uint4 *>(b.x)[c] = reinterpret_cast<const uint4 *>(x_embed)[c];
+  AttnShared<G> &as = *reinterpret_cast<AttnShared<G> *>(sm.xs);
+  uint32_t ev = 0;
+  auto stamp = [&]() {
+    if (p.trace && ctid() == 0 && ev < p.trace_events) p.trace[static_cast<size_t>(blockIdx.x) * p.trace_events + ev] = global_ns();
+    ++ev;
+  };
+  stamp();
+  const uint32_t npc = pos_chunks_dev(d.max_seq), nch = (n + kPosChunk - 1) / kPosChunk;
+  const uint32_t attn_items = d.KVH_l * nch;
+  uint32_t it = 0, nbar = 0;
+  auto barrier = [&]() -> bool {
+    ++nbar;
+    return grid_barrier(p.bar, bar_base + static_cast<unsigned long long>(nbar) * gridDim.x, st, &bflag);
+  };
+  for (uint32_t l = 0; l < p.n_layers; ++l) {
+    const LayerWeights w = p.layers[l];
+    // trace events per layer: [staged, items, finished, barrier] x 6 phases
+    stage_rms(l == 0 ? x_embed : b.x, w.in_norm, d.H, d.eps, sm.xs, sm.scratch);
+    stamp();
+    if (!qkv_items(d, b, sm, p.g.qkv, it)) { flag_error(st, kErrPipelineTimeout); return; }
+    stamp();
+    qkv_finish(d, b, w, p.g.qkv, pos, s_last);
+    stamp();
+    if (!barrier()) return;
+    stamp();
+    stamp();
+    for (uint32_t item = blockIdx.x; item < attn_items; item += gridDim.x)
+      scores_item<G>(d, b, w, item / nch, item % nch, npc, n, as);
+    stamp();
+    stamp();
+    if (!barrier()) return;
+    stamp();
+    stamp();
+    for (uint32_t item = blockIdx.x; item < attn_items; item += gridDim.x)
+      pv_item<G>(d, b, w, item / nch, item % nch, npc, n, as);
+    stamp();
+    stamp();
+    if (!barrier()) return;
+    stamp();
+    stage_copy(b.attn, d.QH_l * kHD, sm.xs);
+    stamp();
+    if (!rowpar_items(d, b, sm, p.g.o, it)) { flag_error(st, kErrPipelineTimeout); return; }
+    stamp();
+    rowpar_finish(d, b, p.g.o, s_last);
+    stamp();
+    if (!barrier()) return;
+    stamp();
+    stage_rms(b.x, w.post_norm, d.H, d.eps, sm.xs, sm.scratch);
+    stamp();
+    if (!gateup_items(d, b, sm, p.g.gu, it)) { flag_error(st, kErrPipelineTimeout); return; }
+    stamp();
+    stamp();
+    if (!barrier()) return;
+    stamp();
+    stage_copy(b.h, d.I_l, sm.xs);
+    stamp();
+    if (!rowpar_items(d, b, sm, p.g.down, it)) { flag_error(st, kErrPipelineTimeout); return; }
+    stamp();
+    rowpar_finish(d, b, p.g.down, s_last);
+    stamp();
+    if (!barrier()) return;
+    stamp();
+  }
+  stage_rms(b.x, b.final_norm, d.H, d.eps, sm.xs, sm.scratch);
+  stamp();
+  if (!lm_items_and_argmax(d, b, sm, p.g.lm, it, ls, pos, static_cast<uint64_t>(nbar) * gridDim.x))
+    flag_error(st, kErrPipelineTimeout);
+  stamp();
+}
+
+template <int G>
+cudaError_t launch_g(const StepPlan *plan, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan->grid);
+  cfg.blockDim = dim3(kStreamThreads);
+  cfg.dynamicSmemBytes = plan->smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_step<G>, plan->p);
+}
+
+template <int G>
+const void *step_kernel() {
+  return reinterpret_cast<const void *>(k_step<G>);
+}
+
+}  // namespace
+
+cudaError_t step_plan_create(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights *layers, uint32_t n_layers,
+                             StepPlan **out) {
+  *out = nullptr;
+  auto plan = new StepPlan();
+  StepParams &p = plan->p;
+  p.d = d;
+  p.b = b;
+  p.n_layers = n_layers;
+  const uint32_t K_o = d.QH_l * kHD;
+  StepGeoms &g = p.g;
+  g.qkv = make_geom(layers[0].wqkv, d.H, 0, (d.QH_l + 2 * d.KVH_l) * kHD, d.H / d.qkv_splits, d.qkv_splits);
+  g.o = make_geom(layers[0].wo, K_o, 0, d.H, K_o / d.chunks_l, d.chunks_l);
+  g.gu = make_geom(layers[0].wgu, d.H, 0, 2 * d.I_l, d.H, 1);
+  g.down = make_geom(layers[0].wd, d.I_l, 0, d.H, d.I_l / d.chunks_l, d.chunks_l);
+  g.lm = make_geom(b.lm_head, d.H, 0, d.V_l, d.H, 1);
+  // One ring for every matrix: slot = the largest stage, 128 KB in all.
+  uint32_t slot = 0;
+  for (const StreamGeom *x : {&g.qkv, &g.o, &g.gu, &g.down, &g.lm}) slot = std::max(slot, stage_bytes(*x));
+  const uint32_t nslots = std::max(2u, std::min(8u, (128u * 1024u) / slot));
+  for (StreamGeom *x : {&g.qkv, &g.o, &g.gu, &g.down, &g.lm}) { x->slot = slot; x->stages = nslots; }
+  plan->group = static_cast<int>(d.QH_l / d.KVH_l);
+  size_t attn_bytes = 0;
+  switch (plan->group) {
+    case 1: attn_bytes = sizeof(AttnShared<1>); break;
+    case 2: attn_bytes = sizeof(AttnShared<2>); break;
+    case 4: attn_bytes = sizeof(AttnShared<4>); break;
+    case 8: attn_bytes = sizeof(AttnShared<8>); break;
+    default: delete plan; return cudaErrorInvalidValue;
+  }
+  const uint32_t stage_elems = std::max(std::max(d.H, K_o), d.I_l);
+  p.x_elems = std::max<uint32_t>(stage_elems, static_cast<uint32_t>((attn_bytes + 1) / 2));
+  plan->smem = stream_smem_bytes(g.qkv, p.x_elems);
+
+  // Items a CTA owns in one phase must fit the deferred-arrival table.
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) { delete plan; return e; }
+  plan->grid = static_cast<uint32_t>(sms);
+  for (const StreamGeom *x : {&g.qkv, &g.o, &g.down})
+    if ((x->items() + plan->grid - 1) / plan->grid > kMaxLocalItems) { delete plan; return cudaErrorInvalidConfiguration; }
+
+  const void *kernel = nullptr;
+  switch (plan->group) {
+    case 1: kernel = step_kernel<1>(); break;
+    case 2: kernel = step_kernel<2>(); break;
+    case 4: kernel = step_kernel<4>(); break;
+    default: kernel = step_kernel<8>(); break;
+  }
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan->smem));
+  int per_sm = 0;
+  if (e == cudaSuccess)
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kStreamThreads, plan->smem);
+  if (e == cudaSuccess && per_sm < 1) e = cudaErrorCooperativeLaunchTooLarge;
+  if (e != cudaSuccess) { delete plan; return e; }
+
+  std::vector<CUtensorMap> maps(4 * n_layers + 1);
+  for (uint32_t l = 0; l < n_layers && e == cudaSuccess; ++l) {
+    e = make_tmap_2d_u16(&maps[4 * l], layers[l].wqkv, d.H, g.qkv.rows, d.H, g.qkv.box, kStageRows);
+    if (e == cudaSuccess) e = make_tmap_2d_u16(&maps[4 * l + 1], layers[l].wo, K_o, d.H, K_o, g.o.box, kStageRows);
+    if (e == cudaSuccess) e = make_tmap_2d_u16(&maps[4 * l + 2], layers[l].wgu, d.H, g.gu.rows, d.H, g.gu.box, kStageRows);
+    if (e == cudaSuccess) e = make_tmap_2d_u16(&maps[4 * l + 3], layers[l].wd, d.I_l, d.H, d.I_l, g.down.box, kStageRows);
+  }
+  if (e == cudaSuccess) e = make_tmap_2d_u16(&maps[4 * n_layers], b.lm_head, d.H, d.V_l, d.H, g.lm.box, kStageRows);
+  if (e == cudaSuccess) e = cudaMalloc(&plan->d_maps, maps.size() * sizeof(CUtensorMap));
+  if (e == cudaSuccess) e = cudaMemcpy(plan->d_maps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMalloc(&plan->d_layers, n_layers * sizeof(LayerWeights));
+  if (e == cudaSuccess) e = cudaMemcpy(plan->d_layers, layers, n_layers * sizeof(LayerWeights), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && trace_enabled()) {
+    p.trace_events = 1 + 24 * n_layers + 2;
+    e = cudaMalloc(&p.trace, static_cast<size_t>(plan->grid) * p.trace_events * sizeof(uint64_t));
+    if (e == cudaSuccess) e = cudaMemset(p.trace, 0, static_cast<size_t>(plan->grid) * p.trace_events * sizeof(uint64_t));
+  }
+  if (e == cudaSuccess) e = cudaMalloc(&plan->d_bar, sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMemset(plan->d_bar, 0, sizeof(unsigned long long));
+  if (e != cudaSuccess) { step_plan_destroy(plan); return e; }
+  p.layers = plan->d_layers;
+  p.maps = plan->d_maps;
+  p.bar = plan->d_bar;
+  *out = plan;
+  return cudaSuccess;
+}
+
+void step_plan_destroy(StepPlan *plan) {
+  if (!plan) return;
+  if (plan->p.trace) cudaFree(plan->p.trace);
+  if (plan->d_maps) cudaFree(plan->d_maps);
+  if (plan->d_layers) cudaFree(plan->d_layers);
+  if (plan->d_bar) cudaFree(plan->d_bar);
+  delete plan;
+}
+
+uint32_t step_grid(const StepPlan *plan) { return plan->grid; }
+
+uint32_t step_trace(const StepPlan *plan, uint64_t *host, uint32_t capacity) {
+  const uint32_t n = plan->p.trace ? plan->grid * plan->p.trace_events : 0;
+  if (!n || !host) return n;
+  cudaMemcpy(host, plan->p.trace, std::min(n, capacity) * sizeof(uint64_t), cudaMemcpyDeviceToHost);
+  return n;
+}
+
+cudaError_t launch_step(const StepPlan *plan, cudaStream_t s) {
+  switch (plan->group) {
+    case 1: return launch_g<1>(plan, s);
+    case 2: return launch_g<2>(plan, s);
+    case 4: return launch_g<4>(plan, s);
+    default: return launch_g<8>(plan, s);
+  }
+}
+
+cudaError_t step_reset(const StepPlan *plan, cudaStream_t s) {
+  cudaError_t e = cudaMemsetAsync(plan->d_bar, 0, sizeof(unsigned long long), s);
+  if (e != cudaSuccess) return e;
+  return cudaMemsetAsync(&plan->p.b.state->bar_base, 0, sizeof(uint64_t), s);
+}
+
+}  // namespace xpu

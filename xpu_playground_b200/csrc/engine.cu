@@ -13,6 +13,7 @@
 #include <algorithm>
 #include <cmath>
 #include <stdexcept>
+#include <cstddef>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -45,6 +46,15 @@ struct CudaError : std::runtime_error {
 struct InvalidArg : std::runtime_error {
   using std::runtime_error::runtime_error;
 };
+
+// A bounded device-side wait gave up (DecodeState::error bit 4).
+struct DeviceTimeout : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+void check_state_error(uint32_t error) {
+  if (error & 4u) throw DeviceTimeout("a decode kernel's bounded wait timed out (device error word " + std::to_string(error) + ")");
+}
 
 uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
 
@@ -82,6 +92,7 @@ class Qwen3Engine {
   ~Qwen3Engine() {
     cudaSetDevice(device_);
     if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
+    if (plan_) step_plan_destroy(plan_);
     if (stream_) cudaStreamSynchronize(stream_);
     for (void *p : allocations_) cudaFree(p);
     if (host_state_) cudaFreeHost(host_state_);
@@ -199,6 +210,14 @@ class Qwen3Engine {
 
   void mark_loaded() { loaded_ = true; }
 
+  // 0 = persistent single kernel per step (default), 1 = CUDA graph of
+  // per-phase kernels. Both compute identical bits.
+  void set_mode(int mode) {
+    if (mode != 0 && mode != 1) throw InvalidArg("decode mode must be 0 (persistent) or 1 (graph)");
+    mode_ = mode;
+  }
+  int mode() const { return mode_; }
+
   // ------------------------------------------------------------ decode ----
   // One step: input token at position (qwen3/main.cpp:159-226 Engine::decode).
   uint32_t decode(uint32_t token, uint32_t position) {
@@ -210,10 +229,11 @@ class Qwen3Engine {
     host_state_->prompt_len = 0;
     host_state_->error = 0;
     host_state_->steps = 0;
-    CK(cudaMemcpyAsync(state_, host_state_, sizeof(DecodeState), cudaMemcpyHostToDevice, stream_));
-    CK(cudaGraphLaunch(graph_exec_, stream_));
+    write_state();
+    launch_one(stream_);
     CK(cudaMemcpyAsync(host_state_, state_, sizeof(DecodeState), cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));
+    after_step_check();
     return host_state_->next;
   }
 
@@ -230,13 +250,14 @@ class Qwen3Engine {
     CK(cudaMemcpyAsync(prompt_, prompt, n * sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
     *host_state_ = DecodeState{};
     host_state_->prompt_len = n;
-    CK(cudaMemcpyAsync(state_, host_state_, sizeof(DecodeState), cudaMemcpyHostToDevice, stream_));
+    write_state();
     const uint32_t steps = n_new ? n + n_new - 1 : n;
-    for (uint32_t i = 0; i < steps; ++i) CK(cudaGraphLaunch(graph_exec_, stream_));
+    for (uint32_t i = 0; i < steps; ++i) launch_one(stream_);
     std::vector<uint32_t> log(n + n_new);
     CK(cudaMemcpyAsync(log.data(), log_, (n + n_new) * sizeof(uint32_t), cudaMemcpyDeviceToHost, stream_));
     CK(cudaMemcpyAsync(host_state_, state_, sizeof(DecodeState), cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));
+    after_step_check();
     uint32_t count = 0;
     for (uint32_t i = 0; i < n_new; ++i) {
       const uint32_t t = log[n - 1 + i];
@@ -253,7 +274,7 @@ class Qwen3Engine {
     host_state_->token = token;
     host_state_->position = position;
     host_state_->prompt_len = prompt_len;
-    CK(cudaMemcpyAsync(state_, host_state_, sizeof(DecodeState), cudaMemcpyHostToDevice, stream_));
+    write_state();
     CK(cudaStreamSynchronize(stream_));
   }
 
@@ -267,7 +288,7 @@ class Qwen3Engine {
   void enqueue_steps(uint32_t n, cudaStream_t stream) {
     ensure_graph();
     cudaStream_t s = stream ? stream : stream_;
-    for (uint32_t i = 0; i < n; ++i) CK(cudaGraphLaunch(graph_exec_, s));
+    for (uint32_t i = 0; i < n; ++i) launch_one(s);
   }
 
   void logits(uint16_t *host, uint32_t count) {
@@ -278,9 +299,14 @@ class Qwen3Engine {
 
   void sync() { CK(cudaStreamSynchronize(stream_)); }
 
+  uint32_t trace(uint64_t *host, uint32_t capacity) {
+    CK(cudaStreamSynchronize(stream_));
+    return plan_ ? step_trace(plan_, host, capacity) : 0;
+  }
+
   const DecodeDims &dims() const { return d_; }
   cudaStream_t stream() const { return stream_; }
-  uint32_t kernels_per_step() const { return 2 + 6 * shape_.num_hidden_layers; }
+  uint32_t kernels_per_step() const { return mode_ == 0 ? 1 : 2 + 6 * shape_.num_hidden_layers; }
   uint64_t weight_bytes() const { return weights_bytes_; }
   uint64_t bytes_per_token(uint32_t context) const {
     // weights streamed per step (embedding: one row) + K and V read for
@@ -423,7 +449,11 @@ class Qwen3Engine {
     b_.scores = dev_alloc<float>(static_cast<uint64_t>(d_.QH_l) * max_seq_);
     b_.stats = dev_alloc<float>(static_cast<uint64_t>(d_.QH_l) * npc * 2);
     b_.attn_part = dev_alloc<float>(static_cast<uint64_t>(d_.QH_l) * npc * 128);
-    const uint32_t lm_ctas = lmhead_ctas(d_);
+    // lm_head candidates: one per CTA of either decode path (the persistent
+    // step runs one CTA per SM, the graph path up to lmhead_ctas).
+    int sms = 0;
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_));
+    const uint32_t lm_ctas = std::max<uint32_t>(lmhead_ctas(d_), static_cast<uint32_t>(sms));
     b_.lm_best = dev_alloc<ArgBest>(lm_ctas);
     b_.lm_bad = dev_alloc<uint32_t>(lm_ctas);
     logits_ = dev_alloc<uint16_t>(d_.V_l);
@@ -488,8 +518,41 @@ class Qwen3Engine {
     CK(launch_lmhead(d_, b_, s));
   }
 
+  // Host -> device copy of the step inputs (every field before bar_base,
+  // which only the device advances).
+  void write_state() {
+    CK(cudaMemcpyAsync(state_, host_state_, offsetof(DecodeState, bar_base), cudaMemcpyHostToDevice, stream_));
+  }
+
+  // A timed-out step leaves the grid barrier mid-count: re-arm it and clear
+  // the sticky bit before reporting, so the next call starts clean.
+  void after_step_check() {
+    const uint32_t err = host_state_->error;
+    if (err & 4u) {
+      if (plan_) CK(step_reset(plan_, stream_));
+      host_state_->error = 0;
+      write_state();
+      CK(cudaStreamSynchronize(stream_));
+      check_state_error(err);
+    }
+  }
+
+  void launch_one(cudaStream_t s) {
+    if (mode_ == 0) CK(launch_step(plan_, s));
+    else CK(cudaGraphLaunch(graph_exec_, s));
+  }
+
   void ensure_graph() {
     if (!loaded_) throw InvalidArg("no weights: call init_synthetic, load a checkpoint or set every tensor");
+    if (mode_ == 0) {
+      if (!plan_) {
+        CK(cudaSetDevice(device_));
+        std::vector<LayerWeights> lw(shape_.num_hidden_layers);
+        for (uint32_t l = 0; l < shape_.num_hidden_layers; ++l) lw[l] = layer_weights(l);
+        CK(step_plan_create(d_, b_, lw.data(), shape_.num_hidden_layers, &plan_));
+      }
+      return;
+    }
     if (graph_exec_) return;
     CK(cudaSetDevice(device_));
     cudaGraph_t graph = nullptr;
@@ -515,6 +578,8 @@ class Qwen3Engine {
   DecodeBuffers b_{};
   cudaStream_t stream_ = nullptr;
   cudaGraphExec_t graph_exec_ = nullptr;
+  StepPlan *plan_ = nullptr;
+  int mode_ = 0;
   std::vector<void *> allocations_;
   std::vector<Layer> layers_;
   uint16_t *embed_ = nullptr, *final_norm_ = nullptr, *lm_head_ = nullptr;
@@ -546,6 +611,8 @@ int guarded(F &&f) {
     return xpu::fail(e.code == cudaErrorMemoryAllocation ? XPU_ERR_NO_MEMORY : XPU_ERR_CUDA, e.what());
   } catch (const xpu::InvalidArg &e) {
     return xpu::fail(XPU_ERR_INVALID, e.what());
+  } catch (const xpu::DeviceTimeout &e) {
+    return xpu::fail(XPU_ERR_TIMEOUT, e.what());
   } catch (const std::exception &e) {
     return xpu::fail(XPU_ERR_INVALID, e.what());
   } catch (...) {
@@ -651,6 +718,17 @@ int xpu_qwen3_info(xpu_qwen3_engine *engine, xpu_qwen3_info_t *info) {
 uint64_t xpu_qwen3_bytes_per_token(xpu_qwen3_engine *engine, uint32_t context) {
   if (!engine || !engine->impl) return 0;
   return engine->impl->bytes_per_token(context);
+}
+
+int xpu_qwen3_trace(xpu_qwen3_engine *engine, uint64_t *host_ns, uint32_t capacity, uint32_t *count) {
+  return guarded([&] {
+    if (!count) throw xpu::InvalidArg("xpu_qwen3_trace: null pointer");
+    *count = eng(engine).trace(host_ns, capacity);
+  });
+}
+
+int xpu_qwen3_set_mode(xpu_qwen3_engine *engine, int mode) {
+  return guarded([&] { eng(engine).set_mode(mode); });
 }
 
 int xpu_qwen3_synchronize(xpu_qwen3_engine *engine) {

@@ -24,6 +24,10 @@ void set_error(const std::string &message);
 int fail(int status, const std::string &message);
 int cuda_status(cudaError_t error, const char *what);
 
+// ---- TMA tensor maps (tmap.cu) ----
+cudaError_t make_tmap_2d_u16(struct CUtensorMap_st *map, const void *base, uint64_t cols, uint64_t rows,
+                             uint64_t pitch_elems, uint32_t box_cols, uint32_t box_rows);
+
 // ---- GEMV ----
 template <typename T>
 cudaError_t gemv_launch(const T *A, const T *x, T *y, uint32_t m, uint32_t k,

@@ -27,13 +27,15 @@ def shape_struct(shape: Qwen3Shape) -> _lib.Qwen3ShapeC:
 
 class Qwen3Engine:
     def __init__(self, shape: Qwen3Shape, max_seq: int, device: int = 0, tp_rank: int = 0,
-                 tp_size: int = 1):
+                 tp_size: int = 1, mode: str | None = None):
         self.lib = _lib.load()
         self.shape, self.max_seq = shape, max_seq
         self._h = ctypes.c_void_p()
         self._shape_c = shape_struct(shape)
         _lib.check(self.lib.xpu_qwen3_create(ctypes.byref(self._shape_c), max_seq, device, tp_rank,
                                              tp_size, ctypes.byref(self._h)))
+        if mode is not None:
+            self.set_mode(mode)
 
     def close(self) -> None:
         if self._h:
@@ -89,6 +91,10 @@ class Qwen3Engine:
         _lib.check(self.lib.xpu_qwen3_get_state(self._h, ctypes.byref(tok), ctypes.byref(pos),
                                                 ctypes.byref(err)))
         return tok.value, pos.value, err.value
+
+    def set_mode(self, mode: str) -> None:
+        """"persistent" (one cooperative kernel per token) or "graph"."""
+        _lib.check(self.lib.xpu_qwen3_set_mode(self._h, {"persistent": 0, "graph": 1}[mode]))
 
     def synchronize(self) -> None:
         _lib.check(self.lib.xpu_qwen3_synchronize(self._h))
