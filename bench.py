@@ -1,0 +1,346 @@
+#!/usr/bin/env python3
+"""Benchmark: Qwen3-8B-shaped greedy decode on B200 (the headline metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one greedy decode token of a batch-1 Qwen3-8B-shaped model
+(36 layers, hidden 4096, 32/8 heads, intermediate 12288, vocabulary 151936,
+untied lm_head; seeded synthetic bf16 weights N(0, 0.02), norms 1) after a
+2048-token seeded prompt, i.e. BASELINE configs[4] at batch 1.
+
+* value: device-resident decoding (the step's input token is the previous
+  step's greedy token, no host round trip), timed with CUDA events around
+  exactly K steps on the engine's stream, max over ranks.
+* e2e: the same decode through the reference-facing API (xpu_qwen3_decode,
+  qwen3/main.cpp Engine::decode): per step a host->device copy of the input
+  token/position from pinned memory and a device->host read of the result.
+* roofline: the decode step is one persistent kernel per token (k_step), so
+  the dominant kernel's achieved bandwidth is its algorithmic bytes per launch
+  (every weight once, one embedding row, K/V for the live context) over its
+  event-timed duration.
+* cpu_baseline / --impl reference: transformers' Qwen3ForCausalLM in bf16
+  (qwen3/reference.py's model) on the host cores, bounded sample (see
+  oracle/cpu_baseline.py).
+
+Multi-GPU: with torchrun, N ranks run N independent engine replicas (one per
+GPU) and report the aggregate; tensor-parallel decoding is not wired into
+this bench yet.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import signal
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Qwen3 decode tok/s @1/2/4/8 B200; GEMV GB/s & GEMM TFLOP/s vs roofline"
+FALLBACK_HBM_GBS = 6650.0  # profiling recipe's fallback, used only without MEASURED_PEAKS.json
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of k_step divided by
+# its algorithmic bytes, from the ncu capture summarised in
+# profiles/k_step_qwen3-8b-l2_decode.md (None until captured).
+TRAFFIC_RATIO = None
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--preset", default="qwen3-8b")
+    ap.add_argument("--context", type=int, default=2048)
+    ap.add_argument("--mode", choices=["persistent", "graph"], default="persistent")
+    ap.add_argument("--e2e-steps", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemv", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def measured_peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_uuid: str | None):
+        self.uuid = device_uuid
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"]
+        if self.uuid:
+            cmd.insert(1, f"--id={self.uuid}")
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self) -> dict:
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.send_signal(signal.SIGTERM)
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for name, val in zip(names, parts[5:9]):
+                    if val.lower().startswith("active"):
+                        reasons.add(name)
+            os.unlink(self.path)
+        except OSError:
+            pass
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def seeded_prompt(n: int, vocab: int, seed: int = 7) -> list[int]:
+    import numpy as np
+    return [int(t) for t in np.random.default_rng(seed).integers(0, vocab, size=n)]
+
+
+def gemv_extra(torch, device) -> dict:
+    """GEMV GB/s at BASELINE configs[0]/[1] shapes (seeded uniform inputs,
+    matrix read once per launch, inputs rotated so nothing stays in L2)."""
+    from xpu_playground_b200 import _lib, kernels
+    L = _lib.load()
+    out = {}
+    for name, m, k, dt, code in (("gemv_4096_bf16", 4096, 4096, torch.bfloat16, _lib.XPU_BF16),
+                                 ("gemv_16384_bf16", 16384, 16384, torch.bfloat16, _lib.XPU_BF16),
+                                 ("gemv_16384_fp16", 16384, 16384, torch.float16, _lib.XPU_FP16)):
+        copies = max(1, (512 << 20) // (2 * m * k))  # > L2 worth of matrices, used round-robin
+        mats = []
+        for c in range(copies):
+            A = torch.empty(m, k, dtype=dt, device=device)
+            _lib.check(L.xpu_fill_uniform16(code, A.data_ptr(), m * k, 11 + c, 1, None))
+            mats.append(A)
+        x = torch.empty(k, dtype=dt, device=device)
+        _lib.check(L.xpu_fill_uniform16(code, x.data_ptr(), k, 12, 2, None))
+        y = torch.empty(m, dtype=dt, device=device)
+        for i in range(5):
+            kernels.gemv(mats[i % copies], x, y)
+        reps = 50
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for i in range(reps):
+            kernels.gemv(mats[i % copies], x, y)
+        e1.record()
+        e1.synchronize()
+        sec = e0.elapsed_time(e1) * 1e-3 / reps
+        out[name] = {"GB/s": round(2 * m * k / sec / 1e9, 1), "us": round(sec * 1e6, 2)}
+        del mats
+    return out
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from xpu_playground_b200.qwen3 import Qwen3Engine
+    from xpu_playground_b200.qwen3_config import PRESETS
+
+    rank, world, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    shape = PRESETS[args.preset]
+    K, W, E = args.steps, args.warmup, args.e2e_steps
+    max_seq = args.context + W + K + E + 8
+    eng = Qwen3Engine(shape, max_seq, device=local, mode=args.mode)
+    eng.init_synthetic(2026)
+    prompt = seeded_prompt(args.context, shape.vocab)
+    eng.generate(prompt, 1)  # device-resident prefill, token by token
+    stream = torch.cuda.ExternalStream(eng.info().stream, device=device)
+    eng.enqueue_steps(W)
+    eng.synchronize()
+    _, pos0, err = eng.state()
+    if world > 1:
+        dist.barrier()
+    props = torch.cuda.get_device_properties(device)
+    uuid = str(getattr(props, "uuid", "") or "")
+    clocks = ClockSampler(("GPU-" + uuid) if uuid and not uuid.startswith("GPU-") else (uuid or None))
+    clocks.start()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    eng.enqueue_steps(K)
+    e1.record(stream)
+    e1.synchronize()
+    torch.cuda.synchronize(device)
+    clock_info = clocks.stop()
+    ms = e0.elapsed_time(e1) / K
+    tok, pos1, err = eng.state()
+    if err:
+        raise SystemExit(f"decode error word {err}")
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+
+    # e2e through the reference-facing API: host token in, host token out.
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    nxt = tok
+    f0.record(stream)
+    for i in range(E):
+        nxt = eng.decode(nxt, pos1 + i)
+    f1.record(stream)
+    f1.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / E
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    mid_context = (pos0 + pos1) // 2
+    bytes_step = eng.bytes_per_token(mid_context)
+    achieved = bytes_step / (ms * 1e-3) / 1e9
+    peak, peak_kind = measured_peaks()
+
+    extra = {}
+    if rank == 0 and not args.no_gemv:
+        eng.synchronize()
+        extra.update(gemv_extra(torch, device))
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        from oracle.cpu_baseline import hf_decode_baseline
+        cpu = hf_decode_baseline(shape, args.context, steps=4)
+        cpu.pop("per_token_s", None)
+        cpu["value"] = round(cpu["value"], 3)
+
+    if rank == 0:
+        value = world * 1000.0 / ms
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": K,
+            "warmup": W,
+            "ms_per_step": round(ms, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) bf16 weights, seeded uniform prompt ids)",
+            "config": {
+                "workload": f"{args.preset}-shaped greedy decode, batch 1, {args.context}-token prompt then "
+                            f"{K} timed decode steps",
+                "layers": shape.layers, "hidden": shape.hidden, "heads": f"{shape.q_heads}/{shape.kv_heads}",
+                "intermediate": shape.intermediate, "vocab": shape.vocab, "tied_lm_head": shape.tied,
+                "context_tokens": [pos0, pos1],
+                "decode_mode": args.mode,
+                "parallelism": "single GPU" if world == 1 else f"{world} independent replicas",
+                "l2": "inputs larger than L2: each step streams all weights (15.4 GB) once",
+            },
+            "e2e": {"value": round(world * 1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 24,
+                    "d2h_bytes_per_step": 32},
+            "roofline": {
+                "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4),
+                "traffic": round(TRAFFIC_RATIO * bytes_step) if TRAFFIC_RATIO else None,
+                "kernel": "k_step (persistent decode step)" if args.mode == "persistent" else "decode graph",
+                "algorithmic_bytes_per_launch": bytes_step,
+                "peak_source": f"{peak_kind} HBM copy bandwidth",
+            },
+            "cpu_baseline": cpu,
+            "clocks": clock_info,
+            "gpu_launches": K * eng.info().kernels_per_step,
+            "extra": extra,
+        }
+        print(json.dumps(line))
+    eng.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_reference(args) -> None:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle.cpu_baseline import hf_decode_baseline
+    from xpu_playground_b200.qwen3_config import PRESETS
+
+    shape = PRESETS[args.preset]
+    t0 = time.time()
+    cpu = hf_decode_baseline(shape, args.context, steps=max(2, min(args.steps, 6)))
+    value = cpu["value"]
+    cpu.pop("per_token_s", None)
+    line = {
+        "metric": METRIC,
+        "impl": "reference",
+        "value": round(value, 3),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(1000.0 / value, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random N(0,0.02) bf16 weights, seeded prompt ids)",
+        "config": {"workload": f"{args.preset}-shaped greedy decode, batch 1, {args.context}-token prompt",
+                   "layers": shape.layers, "hidden": shape.hidden, "vocab": shape.vocab},
+        "cpu_baseline": dict(cpu, value=round(value, 3)),
+        "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": round(time.time() - t0, 1),
+    }
+    print(json.dumps(line))
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()
