@@ -98,6 +98,24 @@ int xpu_qwen_attention(const uint16_t *query, const uint16_t *key_cache,
                        uint32_t query_heads, uint32_t key_value_heads, void *workspace,
                        size_t workspace_bytes, void *stream);
 
+/* Attention for callers that cannot allocate device memory (no counterpart in
+ * the reference): same inputs, output and kernels as xpu_qwen_attention, but
+ * the split-K scratch is a fixed 6 MiB array inside this library instead of a
+ * caller-owned workspace, and nothing is allocated. For hosts whose allocator
+ * owns the device, serving loops that may not call cudaMalloc/cudaFree (they
+ * can synchronise the device), or plugin hosts that pass only inputs and
+ * outputs. Limit: xpu_qwen_attention_workspace_size(query_heads, position + 1)
+ * must be at most 6 MiB (32 query heads: every position up to 40,959);
+ * larger requests return XPU_ERR_INVALID. The array costs 6 MiB on each device
+ * where this code is loaded, until exit. The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress), so make that first call
+ * before any stream capture. All calls share the one array: calls that can
+ * overlap on the GPU (different streams, or different threads on one device)
+ * race on it and must be ordered by the caller. */
+int xpu_qwen_attention_noalloc(const uint16_t *query, const uint16_t *key_cache,
+                               const uint16_t *value_cache, uint16_t *output, uint32_t position,
+                               uint32_t query_heads, uint32_t key_value_heads, void *stream);
+
 /* QwenAdd (kernels_entry.cpp:53-58, kernels.hpp:194-207): left = bf16(left + right). */
 int xpu_qwen_add(uint16_t *left, const uint16_t *right, uint32_t width, void *stream);
 

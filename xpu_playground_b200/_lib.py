@@ -47,6 +47,7 @@ SIGNATURES: dict[str, tuple] = {
     "xpu_qwen_qkv_rope_cache": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, vp]),
     "xpu_qwen_attention_workspace_size": (sz, [u32, u32]),
     "xpu_qwen_attention": (i32, [vp, vp, vp, vp, u32, u32, u32, vp, sz, vp]),
+    "xpu_qwen_attention_noalloc": (i32, [vp, vp, vp, vp, u32, u32, u32, vp]),
     "xpu_qwen_add": (i32, [vp, vp, u32, vp]),
     "xpu_qwen_silu_multiply": (i32, [vp, vp, u32, vp]),
     "xpu_qwen_argmax": (i32, [vp, vp, u32, vp]),
