@@ -49,6 +49,23 @@ int xpu_abi_version(void);
 int xpu_gemv(int dtype, const void *matrix, const void *vector, void *output, uint32_t m,
              uint32_t k, void *stream);
 
+/* ------------------------------------------------------------------ GEMM --
+ * C[m,n] = A[m,k] . B[k,n], all row-major, FP32 accumulation on the tensor
+ * cores, output rounded to dtype. Replaces gemm::Kernel<T, LargeTile>
+ * (gemm_kernel.hpp:25-143) as launched by run<T, LargeTile>
+ * (gemm.cpp:73-131). Unlike the reference, m, n and k need no padding to the
+ * tile sizes. n and k multiples of 8 with 16-byte aligned pointers take the
+ * tensor-core path; other shapes run a CUDA-core kernel.
+ */
+int xpu_gemm(int dtype, const void *a, const void *b, void *c, uint32_t m, uint32_t n, uint32_t k,
+             void *stream);
+
+/* Sticky device-side error word of this library's asynchronous kernels,
+ * read and cleared (synchronises the device). Bit 0: a GEMM pipeline wait
+ * timed out and its tile is incomplete. No reference counterpart (the
+ * reference's kernels have no bounded waits). */
+int xpu_device_status(uint32_t *flags);
+
 /* ------------------------------------------------------- Qwen3 operators --
  * One entry per reference kernel entry (qwen3/kernels_entry.cpp:8-72), with
  * the same argument order. All tensors are bf16 (uint16_t bit patterns).

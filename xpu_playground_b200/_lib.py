@@ -41,6 +41,8 @@ SIGNATURES: dict[str, tuple] = {
     "xpu_last_error": (ctypes.c_char_p, []),
     "xpu_abi_version": (i32, []),
     "xpu_gemv": (i32, [i32, vp, vp, vp, u32, u32, vp]),
+    "xpu_gemm": (i32, [i32, vp, vp, vp, u32, u32, u32, vp]),
+    "xpu_device_status": (i32, [ctypes.POINTER(u32)]),
     "xpu_qwen_embedding": (i32, [vp, vp, u32, u32, vp]),
     "xpu_qwen_rms_norm": (i32, [vp, vp, vp, u32, f32, vp]),
     "xpu_qwen_gemv": (i32, [vp, vp, vp, u32, u32, vp]),

@@ -71,6 +71,27 @@ int xpu_gemv(int dtype, const void *matrix, const void *vector, void *output, ui
   })
 }
 
+int xpu_gemm(int dtype, const void *a, const void *b, void *c, uint32_t m, uint32_t n, uint32_t k,
+             void *stream) {
+  XPU_GUARD({
+    XPU_REQUIRE(a && b && c, "xpu_gemm: null pointer");
+    XPU_REQUIRE(m > 0 && n > 0 && k > 0, "xpu_gemm: m, n and k must be positive");
+    if (dtype != XPU_BF16 && dtype != XPU_FP16)
+      return fail(XPU_ERR_INVALID, "xpu_gemm: dtype must be XPU_BF16 or XPU_FP16");
+    return cuda_status(gemm_launch(dtype == XPU_FP16, a, b, c, m, n, k, as_stream(stream)), "xpu_gemm");
+  })
+}
+
+int xpu_device_status(uint32_t *flags) {
+  XPU_GUARD({
+    XPU_REQUIRE(flags, "xpu_device_status: null pointer");
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_status(e, "xpu_device_status");
+    *flags = take_device_error();
+    return XPU_OK;
+  })
+}
+
 int xpu_qwen_embedding(const uint16_t *table, uint16_t *output, uint32_t token, uint32_t width,
                        void *stream) {
   XPU_GUARD({

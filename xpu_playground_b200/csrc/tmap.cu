@@ -28,11 +28,9 @@ EncodeTiledFn encode_fn() {
 }
 }  // namespace
 
-// Row-major [rows][cols] matrix of 16-bit elements with a row pitch of
-// pitch_elems; box = box_rows rows x box_cols columns, no swizzle, rows past
-// the end read as zero.
-cudaError_t make_tmap_2d_u16(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
-                             uint64_t pitch_elems, uint32_t box_cols, uint32_t box_rows) {
+namespace {
+cudaError_t encode_2d_u16(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows, uint64_t pitch_elems,
+                          uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return cudaErrorNotSupported;
   if ((reinterpret_cast<uintptr_t>(base) & 15u) || (pitch_elems * 2) % 16 || (box_cols * 2) % 16 || box_cols > 256 ||
@@ -43,9 +41,27 @@ cudaError_t make_tmap_2d_u16(CUtensorMap *map, const void *base, uint64_t cols, 
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estride[2] = {1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(base), dims, strides, box, estride,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+}  // namespace
+
+// Row-major [rows][cols] matrix of 16-bit elements with a row pitch of
+// pitch_elems; box = box_rows rows x box_cols columns, no swizzle, rows past
+// the end read as zero.
+cudaError_t make_tmap_2d_u16(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
+                             uint64_t pitch_elems, uint32_t box_cols, uint32_t box_rows) {
+  return encode_2d_u16(map, base, cols, rows, pitch_elems, box_cols, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// Same, with the 128-byte swizzle the tensor-core shared-memory descriptors
+// expect (box_cols x 2 bytes must then be at most 128). Elements outside the
+// matrix (either dimension) read as zero.
+cudaError_t make_tmap_2d_u16_swizzled(CUtensorMap *map, const void *base, uint64_t cols, uint64_t rows,
+                                      uint64_t pitch_elems, uint32_t box_cols, uint32_t box_rows) {
+  if (box_cols * 2 > 128) return cudaErrorInvalidValue;
+  return encode_2d_u16(map, base, cols, rows, pitch_elems, box_cols, box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 }  // namespace xpu

@@ -27,6 +27,14 @@ int cuda_status(cudaError_t error, const char *what);
 // ---- TMA tensor maps (tmap.cu) ----
 cudaError_t make_tmap_2d_u16(struct CUtensorMap_st *map, const void *base, uint64_t cols, uint64_t rows,
                              uint64_t pitch_elems, uint32_t box_cols, uint32_t box_rows);
+cudaError_t make_tmap_2d_u16_swizzled(struct CUtensorMap_st *map, const void *base, uint64_t cols, uint64_t rows,
+                                      uint64_t pitch_elems, uint32_t box_cols, uint32_t box_rows);
+
+// ---- GEMM (gemm.cu) ----
+cudaError_t gemm_launch(bool fp16, const void *A, const void *B, void *C, uint32_t m, uint32_t n, uint32_t k,
+                        cudaStream_t stream);
+// Reads and clears the sticky device error word (bit 0: a GEMM wait timed out).
+unsigned take_device_error();
 
 // ---- GEMV ----
 template <typename T>

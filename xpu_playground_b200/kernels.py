@@ -7,6 +7,8 @@ a contiguous CUDA tensor; 16-bit tensors are passed by their bit patterns.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -42,6 +44,26 @@ def gemv(matrix: torch.Tensor, vector: torch.Tensor, out: torch.Tensor | None = 
     call("xpu_gemv", _dtype_code(matrix), _ptr(matrix), _ptr(vector), _ptr(out), m, k,
          _stream(stream))
     return out
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
+         stream=None) -> torch.Tensor:
+    """C[m,n] = A[m,k] . B[k,n] (row-major, contiguous, bf16 or fp16)."""
+    m, k = a.shape
+    k2, n = b.shape
+    if k2 != k or a.dtype != b.dtype:
+        raise ValueError("gemm: A is [m,k] and B is [k,n] of the same dtype")
+    if out is None:
+        out = torch.empty(m, n, dtype=a.dtype, device=a.device)
+    call("xpu_gemm", _dtype_code(a), _ptr(a), _ptr(b), _ptr(out), m, n, k, _stream(stream))
+    return out
+
+
+def device_status() -> int:
+    """Reads and clears the library's sticky device error word (synchronises)."""
+    flags = ctypes.c_uint32(0)
+    call("xpu_device_status", ctypes.byref(flags))
+    return flags.value
 
 
 def qwen_embedding(table, output, token: int, width: int, stream=None):
