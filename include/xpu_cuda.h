@@ -62,9 +62,28 @@ int xpu_gemm(int dtype, const void *a, const void *b, void *c, uint32_t m, uint3
 
 /* Sticky device-side error word of this library's asynchronous kernels,
  * read and cleared (synchronises the device). Bit 0: a GEMM pipeline wait
- * timed out and its tile is incomplete. No reference counterpart (the
+ * timed out and its tile is incomplete; bit 1: a calibrator wait timed out. No reference counterpart (the
  * reference's kernels have no bounded waits). */
 int xpu_device_status(uint32_t *flags);
+
+/* ----------------------------------------------------------- Calibrators --
+ * Roofline calibrators with the reference benchmarks' checksums.
+ *
+ * xpu_peak_mem_fill: surface[i] = 1 + (hash(i) & 0xffff) / 65536, the
+ * irregular fill of peak_mem_2d.cpp:36-47 (defeats memory compression).
+ * xpu_peak_mem_read: reads a row-major float surface 1024 wide and
+ * surface_height rows (a multiple of 32) once; sink[u] (one per 2 KiB read
+ * unit, surface_height * 2 units) = the FP32 sum of the unit's elements at
+ * rows y, y+8, y+16, y+24 of column x, x = 16 (u % 64), y = 32 (u / 64).
+ * Replaces peak_mem_2d_kernel (peak_mem_2d_kernel.cpp:16-52).
+ * xpu_peak_compute: `ctas` CTAs each issue rounds x 8 tensor-core MMAs of
+ * 128x256x16 bf16 (1,048,576 FLOP each) on 0.5-filled tiles; sink[cta] =
+ * 1 + 32 * rounds. rounds <= 524287. Replaces peak_compute_dpas_kernel
+ * (peak_compute_dpas_kernel.cpp:13-68).
+ */
+int xpu_peak_mem_fill(float *surface, uint64_t elements, void *stream);
+int xpu_peak_mem_read(const float *surface, float *sink, uint32_t surface_height, void *stream);
+int xpu_peak_compute(float *sink, uint32_t ctas, uint32_t rounds, void *stream);
 
 /* ------------------------------------------------------- Qwen3 operators --
  * One entry per reference kernel entry (qwen3/kernels_entry.cpp:8-72), with

@@ -145,6 +145,45 @@ def rel_frobenius(actual, expected) -> float:
     return float(np.linalg.norm(a - e) / max(np.linalg.norm(e), 1e-30))
 
 
+# ------------------------------------------------------- calibrators ----
+
+def _hash_u32(i: np.ndarray) -> np.ndarray:
+    b = i.astype(np.uint32)
+    b ^= b >> np.uint32(16)
+    b *= np.uint32(0x7FEB352D)
+    b ^= b >> np.uint32(15)
+    b *= np.uint32(0x846CA68B)
+    b ^= b >> np.uint32(16)
+    return b
+
+
+def peak_mem_surface(elements: int) -> np.ndarray:
+    """The read calibrator's fill, 1 + (hash(i) & 0xffff) / 65536
+    (peak_mem_2d.cpp:36-47); index truncated to 32 bits like the reference."""
+    idx = np.arange(elements, dtype=np.uint64).astype(np.uint32)
+    return (np.float32(1.0) + (_hash_u32(idx) & np.uint32(0xFFFF)).astype(np.float32)
+            * np.float32(1.0 / 65536.0)).astype(np.float32)
+
+
+def peak_mem_checksums(surface: np.ndarray) -> np.ndarray:
+    """Per read unit (16 columns x 32 rows of the 1024-wide surface), the FP32
+    sum in load order of the elements at rows y, y+8, y+16, y+24 of column x
+    (peak_mem_2d.cpp:49-59, peak_mem_2d_kernel.cpp:28-50)."""
+    s = surface.reshape(-1, 32, 1024)          # band, row in band, column
+    picks = s[:, 0::8, 0::16]                  # band, load, unit column
+    out = np.zeros((s.shape[0], 64), np.float32)
+    for load in range(4):
+        out = (out + picks[:, load, :]).astype(np.float32)
+    return out.reshape(-1)
+
+
+def peak_compute_checksum(rounds: int) -> float:
+    """Tensor calibrator sink value: accumulator offsets 0 + 1 plus 4 per
+    MMA, 8 MMAs per round (the closed form of peak_compute_dpas.cpp:197-198
+    for this kernel's two accumulators)."""
+    return float(np.float32(1.0) + np.float32(8 * rounds * 4))
+
+
 # ------------------------------------- Qwen3 operators (kernels.hpp) ----
 
 def embedding(table, token, width):

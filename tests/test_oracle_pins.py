@@ -258,3 +258,23 @@ def test_c_decode_matches_transformers(fixture):
             assert near_tie(fx["logits"][pos], nxt, ref_ids[pos]), f"step {pos}: {nxt} vs {ref_ids[pos]}"
             flips += 1
     assert flips <= 1
+
+
+def test_peak_mem_checksums_follow_the_reference_formula():
+    # peak_mem_2d.cpp:49-59: unit u reads x = 16 (u % 64), y = 32 (u / 64);
+    # checksum = sum over load of value(x + (y + 8 load) * 1024), in order.
+    height = 96
+    surface = orc.peak_mem_surface(1024 * height)
+    sums = orc.peak_mem_checksums(surface)
+    assert sums.shape == (height * 2,)
+    for u in (0, 1, 63, 64, 100, height * 2 - 1):
+        x, y = (u % 64) * 16, (u // 64) * 32
+        expected = np.float32(0.0)
+        for load in range(4):
+            expected = np.float32(expected + orc.lib().orc_peak_mem_value(x + (y + load * 8) * 1024))
+        assert sums[u] == expected
+    assert np.array_equal(surface[:5], np.array([orc.lib().orc_peak_mem_value(i) for i in range(5)], np.float32))
+
+
+def test_peak_compute_checksum_closed_form():
+    assert orc.peak_compute_checksum(8192) == 1.0 + 8 * 8192 * 4

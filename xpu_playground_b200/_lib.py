@@ -43,6 +43,9 @@ SIGNATURES: dict[str, tuple] = {
     "xpu_gemv": (i32, [i32, vp, vp, vp, u32, u32, vp]),
     "xpu_gemm": (i32, [i32, vp, vp, vp, u32, u32, u32, vp]),
     "xpu_device_status": (i32, [ctypes.POINTER(u32)]),
+    "xpu_peak_mem_fill": (i32, [vp, u64, vp]),
+    "xpu_peak_mem_read": (i32, [vp, vp, u32, vp]),
+    "xpu_peak_compute": (i32, [vp, u32, u32, vp]),
     "xpu_qwen_embedding": (i32, [vp, vp, u32, u32, vp]),
     "xpu_qwen_rms_norm": (i32, [vp, vp, vp, u32, f32, vp]),
     "xpu_qwen_gemv": (i32, [vp, vp, vp, u32, u32, vp]),

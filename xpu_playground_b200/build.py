@@ -38,10 +38,25 @@ NVCC_FLAGS = ARCH + [
     "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
     f"-I{INCLUDE}", f"-I{CSRC}",
 ]
-CXX_FLAGS = ["-O2", "-std=c++17", "-Wall", "-Wextra", "-Werror", f"-I{INCLUDE}", f"-I{HOST}"]
+CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+CXX_FLAGS = ["-O2", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-fPIC", f"-I{INCLUDE}", f"-I{HOST}",
+             f"-I{CUDA_HOME / 'include'}"]
+CUDART_LINK = [f"-L{CUDA_HOME / 'lib64'}", "-lcudart_static", "-ldl", "-lpthread", "-lrt"]
+BENCH_LIB = LIB_DIR / "libxpu_bench.so"
 
-# C++ host programs: name -> sources under host/ (all link libxpu_cuda.so).
-HOST_PROGRAMS: dict[str, list[str]] = {}
+# Benchmark programs (name -> source under host/): each source defines its
+# extern "C" run_* entry (collected into libxpu_bench.so) and, built with
+# -DXPU_STANDALONE_HOST, a main() of its own.
+BENCH_PROGRAMS: dict[str, str] = {
+    "gemv": "gemv.cpp",
+    "gemm": "gemm.cpp",
+    "peak_mem_2d": "peak_mem_2d.cpp",
+    "peak_compute_dpas": "peak_compute_dpas.cpp",
+}
+# Other C++ host programs: name -> sources under host/ (all link libxpu_cuda.so).
+HOST_PROGRAMS: dict[str, list[str]] = {
+    "peak_sycl": ["peak_sycl.cpp"],
+}
 
 
 def _headers() -> list[Path]:
@@ -84,17 +99,29 @@ def build_library(jobs: int | None = None) -> Path:
 
 
 def build_programs() -> list[Path]:
-    """Link the C++ host programs against libxpu_cuda.so."""
+    """Link the benchmark programs, libxpu_bench.so and the other C++ host
+    programs against libxpu_cuda.so."""
     BIN_DIR.mkdir(parents=True, exist_ok=True)
     headers = _headers()
+    rpath = "-Wl,-rpath,$ORIGIN/../lib"
+    link = [f"-L{LIB_DIR}", "-lxpu_cuda", *CUDART_LINK]
     outputs = []
+    bench_srcs = [HOST / f for f in BENCH_PROGRAMS.values()]
+    if _stale(BENCH_LIB, [*bench_srcs, LIB, Path(__file__), *headers]):
+        _run([CXX, *CXX_FLAGS, "-shared", *map(str, bench_srcs), "-o", str(BENCH_LIB), *link,
+              "-Wl,-rpath,$ORIGIN"])
+    outputs.append(BENCH_LIB)
+    for name, src in BENCH_PROGRAMS.items():
+        out = BIN_DIR / name
+        outputs.append(out)
+        if _stale(out, [HOST / src, LIB, Path(__file__), *headers]):
+            _run([CXX, *CXX_FLAGS, "-DXPU_STANDALONE_HOST", str(HOST / src), "-o", str(out), *link, rpath])
     for name, files in HOST_PROGRAMS.items():
         srcs = [HOST / f for f in files]
         out = BIN_DIR / name
         outputs.append(out)
         if _stale(out, [*srcs, LIB, Path(__file__), *headers]):
-            _run([CXX, *CXX_FLAGS, *map(str, srcs), "-o", str(out), f"-L{LIB_DIR}", "-lxpu_cuda",
-                  f"-Wl,-rpath,$ORIGIN/../lib"])
+            _run([CXX, *CXX_FLAGS, *map(str, srcs), "-o", str(out), *link, rpath])
     return outputs
 
 

@@ -87,7 +87,7 @@ int xpu_device_status(uint32_t *flags) {
     XPU_REQUIRE(flags, "xpu_device_status: null pointer");
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) return cuda_status(e, "xpu_device_status");
-    *flags = take_device_error();
+    *flags = take_device_error() | take_peak_error();
     return XPU_OK;
   })
 }

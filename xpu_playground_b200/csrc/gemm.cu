@@ -3,25 +3,39 @@
 // out. Replaces gemm::Kernel<T, LargeTile> (gemm_kernel.hpp:25-143), whose
 // work-items run 8x16x16 DPAS tiles out of registers.
 //
-// One CTA per 128 x 256 output tile; 192 threads in four roles:
-//   warp 0     TMA producer: per 64-deep K stage, A as one 128 x 64 box and B
-//              as four 64(N) x 64(K) boxes, 128-byte swizzled, into a ring of
-//              4 x 48 KB shared-memory stages (full/empty mbarriers);
-//   warp 1     allocates 256 TMEM columns (the FP32 128 x 256 accumulator)
-//              and, from one elected lane, issues four 128x256x16
-//              tcgen05.mma per stage; tcgen05.commit releases each stage and,
-//              after the last, signals the epilogue;
-//   warps 2-5  epilogue: tcgen05.ld 32 rows x 32 columns at a time (warp w
-//              reads TMEM lanes 32 (w % 4) .. + 31 = output rows), round to
-//              bf16/fp16 and store with row/column predication.
+// Persistent, two CTAs per cluster working as one pair (cta_group::2): a pair
+// owns 256 x 256 output tiles, visited in groups of 8 tile-rows so that the
+// pairs running at once share A and B panels in L2. Each CTA of the pair
+// stages its half of the operands, A rows [128 r, 128 r + 128) and B columns
+// [128 r, 128 r + 128) of the tile, and holds its 128 rows x 256 columns of
+// the FP32 accumulator in its own TMEM; one thread of the even CTA issues
+// the 256x256x16 MMAs that read both CTAs' shared memory. 320 threads:
+//   warp 0     TMA producer: per 64-deep K stage, a 128 x 64 A box and two
+//              64(N) x 64(K) B boxes, 128-byte swizzled, into a ring of
+//              6 x 32 KB stages; both CTAs' copies complete on the even
+//              CTA's full barrier;
+//   warp 1     TMEM owner (2 x 256 columns: a double-buffered accumulator);
+//              in the even CTA its elected lane issues the MMAs, releases
+//              each stage to both CTAs' producers with tcgen05.commit and
+//              signals both epilogues when a tile's accumulator is final;
+//   warps 2-9  epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (its
+//              rows), columns [128 h, 128 h + 128) for h = (w - 2) / 4,
+//              rounds to bf16/fp16 and stores with row/column predication,
+//              then frees the accumulator buffer for the tile after next.
 // A is K-major (row-major [M,K]); B is used MN-major straight from its
 // row-major [K,N] layout (instruction descriptor b_major = MN), so neither
 // operand is transposed or padded in memory: TMA zero-fills out-of-range
-// rows/columns/K and the epilogue masks the edge tiles.
+// rows/columns/K and the epilogue masks the edge tiles. No load uses
+// multicast; the even CTA signals the odd CTA's barriers by their cluster
+// addresses.
 //
-// Waits are bounded; a timeout sets a sticky device error word (reported by
-// xpu_device_status) and the CTA still frees its TMEM before it exits.
+// Waits are bounded; a timeout sets a sticky device error word (read by
+// xpu_device_status) and every role leaves its loop, so both CTAs still meet
+// at the closing cluster barrier and free their TMEM.
 #include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "stream.cuh"
@@ -33,18 +47,43 @@ __device__ unsigned int g_device_error = 0;
 
 namespace {
 
-constexpr uint32_t kBM = 128, kBN = 256, kBK = 64;
-constexpr uint32_t kStages = 4;
-constexpr uint32_t kABytes = kBM * kBK * 2;        // 16 KB
+constexpr uint32_t kBM = 256, kBN = 256, kBK = 64;  // pair tile
+constexpr uint32_t kHalfM = kBM / 2, kHalfN = kBN / 2;
+constexpr uint32_t kStages = 6;
+constexpr uint32_t kABytes = kHalfM * kBK * 2;     // 16 KB: 128 rows x 64 K
 constexpr uint32_t kBBoxBytes = 64 * kBK * 2;      // 8 KB: 64 (N) x 64 (K)
-constexpr uint32_t kBBytes = kBN * kBK * 2;        // 32 KB
+constexpr uint32_t kBBytes = kHalfN * kBK * 2;     // 16 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr uint32_t kTmemCols = 256;
-constexpr int kGemmThreads = 192;
+constexpr uint32_t kAccCols = kBN;                 // FP32 columns of one accumulator
+constexpr uint32_t kTmemCols = 2 * kAccCols;       // double buffered: all 512
+constexpr uint32_t kGroupRows = 8;                 // tile-rows per L2 group
+constexpr int kEpilogueWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpilogueWarps;
 constexpr unsigned kErrGemmTimeout = 1u;
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void *p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr(p)), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ void remote_arrive(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
 
 // Shared-memory matrix descriptor: 128-byte swizzle, version 1 (sm_100).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
@@ -58,35 +97,39 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes,
 }
 
 // Instruction descriptor, kind::f16: FP32 accumulator, A K-major, B MN-major.
-__host__ __device__ constexpr uint32_t instr_desc(bool fp16) {
+__host__ __device__ constexpr uint32_t instr_desc(bool fp16, uint32_t m, uint32_t n) {
   return (1u << 4) |                          // D format F32
          ((fp16 ? 0u : 1u) << 7) |            // A format: F16 = 0, BF16 = 1
          ((fp16 ? 0u : 1u) << 10) |           // B format
          (0u << 15) |                         // A K-major
          (1u << 16) |                         // B MN-major
-         ((kBN >> 3) << 17) |                 // N / 8
-         ((kBM >> 4) << 24);                  // M / 16
+         ((n >> 3) << 17) |                   // N / 8
+         ((m >> 4) << 24);                    // M / 16
 }
 
-__device__ __forceinline__ void tma_load_2d_plain(void *dst, const CUtensorMap *map, int32_t x, int32_t y,
-                                                  uint64_t *bar) {
+// 2D tiled TMA load into this CTA's shared memory, completing on an mbarrier
+// that may belong to either CTA of the pair (cluster address).
+__device__ __forceinline__ void tma_load_pair(void *dst, const CUtensorMap *map, int32_t x, int32_t y,
+                                              uint32_t cluster_bar) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_addr(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(cluster_bar)
       : "memory");
 }
 
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+__device__ __forceinline__ void mma_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
       "l"(a), "l"(b), "r"(idesc), "r"(acc)
       : "memory");
 }
 
-__device__ __forceinline__ void mma_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+// Arrives once on `cluster_bar` when every MMA this thread issued so far has
+// completed (on both CTAs of the pair).
+__device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
                : "memory");
 }
 
@@ -111,110 +154,155 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return pack_bf16x2(lo, hi);
 }
 
+__device__ __forceinline__ bool has_failed(const int *flag) { return *reinterpret_cast<const volatile int *>(flag) != 0; }
+
+struct TileCoord {
+  uint32_t m, n;
+};
+
+// Tile t in group-of-rows order: kGroupRows tile-rows at a time, column by
+// column inside the group.
+__device__ __forceinline__ TileCoord tile_coord(uint32_t t, uint32_t tiles_m, uint32_t tiles_n) {
+  const uint32_t per_group = kGroupRows * tiles_n;
+  const uint32_t group = t / per_group, first = group * kGroupRows;
+  const uint32_t rows = min(kGroupRows, tiles_m - first);
+  const uint32_t local = t - group * per_group;
+  return {first + local % rows, local / rows};
+}
+
 template <bool FP16>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, uint16_t *C,
           uint32_t M, uint32_t N, uint32_t K) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  __shared__ uint64_t full[kStages], empty[kStages], accum_full;
+  __shared__ uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int failed;
-  // 1024-byte aligned stage ring (128-byte swizzle atoms).
+  // 1024-byte aligned stage ring (128-byte swizzle atoms); same offset in both CTAs.
   const uint32_t a0 = smem_addr(smem_raw);
   uint8_t *ring = smem_raw + ((a0 + 1023u) / 1024u * 1024u - a0);
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t tiles_m = (M + kBM - 1) / kBM;
-  const uint32_t tm = blockIdx.x % tiles_m, tn = blockIdx.x / tiles_m;
+  const uint32_t rank = cluster_rank();  // 0 = the CTA that issues the MMAs
+  const uint32_t pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const uint32_t tiles_m = (M + kBM - 1) / kBM, tiles_n = (N + kBN - 1) / kBN, tiles = tiles_m * tiles_n;
   const uint32_t nk = (K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < kStages; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
+      mbar_init(&full[i], 1);   // the even CTA's expect_tx; both CTAs' bytes
+      mbar_init(&empty[i], 1);  // one commit per use
     }
-    mbar_init(&accum_full, 1);
+    for (uint32_t i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 2 * kEpilogueWarps);  // every epilogue warp of the pair
+    }
     fence_mbar_init();
     failed = 0;
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
                  "r"(kTmemCols)
                  : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
   tc_fence_after();
   const uint32_t tmem = tmem_base;
 
   if (warp == 0) {
     if (lane == 0) {
-      for (uint32_t k = 0; k < nk; ++k) {
-        const uint32_t s = k % kStages, use = k / kStages;
-        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) { failed = 1; break; }
-        if (*reinterpret_cast<volatile int *>(&failed)) break;
-        mbar_expect_tx(&full[s], kStageBytes);
-        uint8_t *st = ring + s * kStageBytes;
-        tma_load_2d_plain(st, &map_a, static_cast<int32_t>(k * kBK), static_cast<int32_t>(tm * kBM), &full[s]);
-        for (uint32_t j = 0; j < kBN / 64; ++j)
-          tma_load_2d_plain(st + kABytes + j * kBBoxBytes, &map_b, static_cast<int32_t>(tn * kBN + j * 64),
-                            static_cast<int32_t>(k * kBK), &full[s]);
+      const uint32_t full0 = cluster_addr(&full[0], 0);
+      uint32_t g = 0;
+      for (uint32_t t = pair; t < tiles && !has_failed(&failed); t += pairs) {
+        const TileCoord tc = tile_coord(t, tiles_m, tiles_n);
+        const int32_t ya = static_cast<int32_t>(tc.m * kBM + rank * kHalfM);
+        const int32_t xb = static_cast<int32_t>(tc.n * kBN + rank * kHalfN);
+        for (uint32_t k = 0; k < nk; ++k, ++g) {
+          const uint32_t s = g % kStages, use = g / kStages;
+          if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) { failed = 1; break; }
+          if (rank == 0) mbar_expect_tx(&full[s], 2 * kStageBytes);
+          const uint32_t bar = full0 + s * 8u;
+          uint8_t *st = ring + s * kStageBytes;
+          const int32_t xk = static_cast<int32_t>(k * kBK);
+          tma_load_pair(st, &map_a, xk, ya, bar);
+          tma_load_pair(st + kABytes, &map_b, xb, xk, bar);
+          tma_load_pair(st + kABytes + kBBoxBytes, &map_b, xb + 64, xk, bar);
+        }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc(FP16);
-      uint32_t k = 0;
-      for (; k < nk; ++k) {
-        const uint32_t s = k % kStages, use = k / kStages;
-        if (!mbar_wait(&full[s], use & 1)) { failed = 1; break; }
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc = instr_desc(FP16, kBM, kBN);
+      uint32_t g = 0, i = 0;
+      for (uint32_t t = pair; t < tiles && !has_failed(&failed); t += pairs, ++i) {
+        const uint32_t b = i & 1, use_b = i >> 1;
+        if (use_b > 0 && !mbar_wait(&acc_empty[b], (use_b - 1) & 1)) { failed = 1; break; }
         tc_fence_after();
-        const uint32_t sa = smem_addr(ring + s * kStageBytes), sb = sa + kABytes;
-        const uint64_t da = smem_desc(sa, 16, 1024), db = smem_desc(sb, kBBoxBytes, 1024);
+        const uint32_t d = tmem + b * kAccCols;
+        for (uint32_t k = 0; k < nk; ++k, ++g) {
+          const uint32_t s = g % kStages, use = g / kStages;
+          if (!mbar_wait(&full[s], use & 1)) { failed = 1; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_addr(ring + s * kStageBytes), sb = sa + kABytes;
+          const uint64_t da = smem_desc(sa, 16, 1024), db = smem_desc(sb, kBBoxBytes, 1024);
 #pragma unroll
-        for (uint32_t kk = 0; kk < kBK / 16; ++kk)
-          // K step of 16: +32 bytes inside A's 128-byte swizzled rows, +2 eight-row groups of B.
-          mma_bf16(tmem, da + ((kk * 32u) >> 4), db + ((kk * 2048u) >> 4), idesc, (k | kk) != 0);
-        mma_commit(&empty[s]);
+          for (uint32_t kk = 0; kk < kBK / 16; ++kk)
+            // K step of 16: +32 bytes inside A's 128-byte swizzled rows, +2 eight-row groups of B.
+            mma_pair(d, da + ((kk * 32u) >> 4), db + ((kk * 2048u) >> 4), idesc, (k | kk) != 0);
+          mma_commit_pair(cluster_addr(&empty[s], 0));
+          mma_commit_pair(cluster_addr(&empty[s], 1));
+        }
+        if (has_failed(&failed)) break;
+        mma_commit_pair(cluster_addr(&acc_full[b], 0));
+        mma_commit_pair(cluster_addr(&acc_full[b], 1));
       }
-      mma_commit(&accum_full);  // fires once every issued MMA has completed
     }
   } else {
-    // Epilogue warps 2..5: TMEM lanes 32 (warp % 4) .. + 31 hold rows of the tile.
-    const uint32_t quarter = warp & 3;
-    const bool ok = mbar_wait(&accum_full, 0);
-    tc_fence_after();
-    const uint32_t row = tm * kBM + quarter * 32 + lane;
-    if (!ok) {
-      failed = 1;
-    } else {
-      for (uint32_t c = 0; c < kBN; c += 32) {
+    // Epilogue warps 2..9: TMEM lanes 32 (warp % 4) .. + 31 hold 32 rows of
+    // this CTA's half; column half h = (warp - 2) / 4.
+    const uint32_t quarter = warp & 3, h = (warp - 2) >> 2;
+    const uint32_t release = cluster_addr(&acc_empty[0], 0);
+    uint32_t i = 0;
+    for (uint32_t t = pair; t < tiles; t += pairs, ++i) {
+      const uint32_t b = i & 1;
+      if (!mbar_wait(&acc_full[b], (i >> 1) & 1)) { failed = 1; break; }
+      tc_fence_after();
+      const TileCoord tc = tile_coord(t, tiles_m, tiles_n);
+      const uint32_t row = tc.m * kBM + rank * kHalfM + quarter * 32 + lane;
+#pragma unroll 1
+      for (uint32_t c = h * 128; c < h * 128 + 128; c += 32) {
         uint32_t r[32];
-        tmem_ld32(tmem + ((quarter * 32u) << 16) + c, r);
-        const uint32_t col = tn * kBN + c;
+        tmem_ld32(tmem + ((quarter * 32u) << 16) + b * kAccCols + c, r);
+        const uint32_t col = tc.n * kBN + c;
         if (row < M && col < N) {
           uint16_t *dst = C + static_cast<size_t>(row) * N + col;
 #pragma unroll
-          for (uint32_t g = 0; g < 4; ++g) {
-            if (col + 8 * g >= N) break;
+          for (uint32_t q = 0; q < 4; ++q) {
+            if (col + 8 * q >= N) break;
             uint4 v;
-            v.x = pack2<FP16>(__uint_as_float(r[8 * g + 0]), __uint_as_float(r[8 * g + 1]));
-            v.y = pack2<FP16>(__uint_as_float(r[8 * g + 2]), __uint_as_float(r[8 * g + 3]));
-            v.z = pack2<FP16>(__uint_as_float(r[8 * g + 4]), __uint_as_float(r[8 * g + 5]));
-            v.w = pack2<FP16>(__uint_as_float(r[8 * g + 6]), __uint_as_float(r[8 * g + 7]));
-            *reinterpret_cast<uint4 *>(dst + 8 * g) = v;
+            v.x = pack2<FP16>(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
+            v.y = pack2<FP16>(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
+            v.z = pack2<FP16>(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
+            v.w = pack2<FP16>(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
+            *reinterpret_cast<uint4 *>(dst + 8 * q) = v;
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) remote_arrive(release + b * 8u);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0 && failed) atomicOr(&g_device_error, kErrGemmTimeout);
+  cluster_sync();  // no CTA of the pair touches the other's barriers or TMEM after this
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
+  cluster_sync();
 }
 
 // CUDA-core fallback for shapes the TMA path cannot describe (a row stride
@@ -265,7 +353,7 @@ cudaError_t gemm_launch(bool fp16, const void *A, const void *B, void *C, uint32
     return cudaGetLastError();
   }
   CUtensorMap map_a, map_b;
-  cudaError_t e = make_tmap_2d_u16_swizzled(&map_a, A, K, M, K, kBK, kBM);
+  cudaError_t e = make_tmap_2d_u16_swizzled(&map_a, A, K, M, K, kBK, kHalfM);
   if (e != cudaSuccess) return e;
   e = make_tmap_2d_u16_swizzled(&map_b, B, N, K, N, 64, kBK);
   if (e != cudaSuccess) return e;
@@ -273,8 +361,41 @@ cudaError_t gemm_launch(bool fp16, const void *A, const void *B, void *C, uint32
   auto kernel = fp16 ? k_gemm_tc<true> : k_gemm_tc<false>;
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
+
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // Persistent grid: as many pairs as can be resident at once (the pairs do
+  // not wait on one another, so fewer resident pairs only cost time).
+  int device = 0;
+  e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  static std::mutex cache_mutex;
+  static int resident_pairs[2][64] = {};
+  int pairs = 0;
+  {
+    std::lock_guard<std::mutex> lock(cache_mutex);
+    int &cached = resident_pairs[fp16 ? 1 : 0][device & 63];
+    if (cached == 0) {
+      cfg.gridDim = dim3(2);
+      e = cudaOccupancyMaxActiveClusters(&cached, kernel, &cfg);
+      if (e != cudaSuccess) return e;
+      if (cached < 1) return cudaErrorLaunchOutOfResources;
+    }
+    pairs = cached;
+  }
   const uint32_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
-  kernel<<<tiles, kGemmThreads, smem, stream>>>(map_a, map_b, static_cast<uint16_t *>(C), M, N, K);
+  cfg.gridDim = dim3(2 * std::min<uint32_t>(tiles, static_cast<uint32_t>(pairs)));
+  e = cudaLaunchKernelEx(&cfg, kernel, map_a, map_b, static_cast<uint16_t *>(C), M, N, K);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

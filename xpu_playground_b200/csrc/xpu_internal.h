@@ -35,6 +35,8 @@ cudaError_t gemm_launch(bool fp16, const void *A, const void *B, void *C, uint32
                         cudaStream_t stream);
 // Reads and clears the sticky device error word (bit 0: a GEMM wait timed out).
 unsigned take_device_error();
+// Same for the calibrator kernels (peak.cu; bit 1: a pipeline wait timed out).
+unsigned take_peak_error();
 
 // ---- GEMV ----
 template <typename T>

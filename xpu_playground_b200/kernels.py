@@ -66,6 +66,29 @@ def device_status() -> int:
     return flags.value
 
 
+def peak_mem_fill(surface: torch.Tensor, stream=None) -> None:
+    """surface[i] = 1 + (hash(i) & 0xffff) / 65536 (float32 tensor)."""
+    call("xpu_peak_mem_fill", _ptr(surface), surface.numel(), _stream(stream))
+
+
+def peak_mem_read(surface: torch.Tensor, sink: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """One read of a [height, 1024] float32 surface; returns the per-unit
+    checksums (one per 2 KiB unit: height * 2 of them)."""
+    height = surface.numel() // 1024
+    if sink is None:
+        sink = torch.zeros(height * 2, dtype=torch.float32, device=surface.device)
+    call("xpu_peak_mem_read", _ptr(surface), _ptr(sink), height, _stream(stream))
+    return sink
+
+
+def peak_compute(ctas: int, rounds: int, sink: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """ctas x rounds x 8 tensor-core MMAs; returns sink (1 + 32 rounds each)."""
+    if sink is None:
+        sink = torch.zeros(ctas, dtype=torch.float32, device="cuda")
+    call("xpu_peak_compute", _ptr(sink), ctas, rounds, _stream(stream))
+    return sink
+
+
 def qwen_embedding(table, output, token: int, width: int, stream=None):
     call("xpu_qwen_embedding", _ptr(table), _ptr(output), token, width, _stream(stream))
 
