@@ -10,10 +10,11 @@
 // [128 r, 128 r + 128) of the tile, and holds its 128 rows x 256 columns of
 // the FP32 accumulator in its own TMEM; one thread of the even CTA issues
 // the 256x256x16 MMAs that read both CTAs' shared memory. 320 threads:
-//   warp 0     TMA producer: per 64-deep K stage, a 128 x 64 A box and two
-//              64(N) x 64(K) B boxes, 128-byte swizzled, into a ring of
-//              6 x 32 KB stages; both CTAs' copies complete on the even
-//              CTA's full barrier;
+//   warp 0     TMA producer: per 128-deep K stage, two 128 x 64 A boxes
+//              and two 64(N) x 128(K) B boxes, 128-byte swizzled, into a
+//              ring of 3 x 64 KB stages; both CTAs' copies complete on the
+//              even CTA's full barrier (128-deep stages halve the barrier
+//              and commit traffic per MMA against 64-deep ones);
 //   warp 1     TMEM owner (2 x 256 columns: a double-buffered accumulator);
 //              in the even CTA its elected lane issues the MMAs, releases
 //              each stage to both CTAs' producers with tcgen05.commit and
@@ -47,12 +48,14 @@ __device__ unsigned int g_device_error = 0;
 
 namespace {
 
-constexpr uint32_t kBM = 256, kBN = 256, kBK = 64;  // pair tile
+constexpr uint32_t kBM = 256, kBN = 256, kBK = 128;  // pair tile, K stage
 constexpr uint32_t kHalfM = kBM / 2, kHalfN = kBN / 2;
-constexpr uint32_t kStages = 6;
-constexpr uint32_t kABytes = kHalfM * kBK * 2;     // 16 KB: 128 rows x 64 K
-constexpr uint32_t kBBoxBytes = 64 * kBK * 2;      // 8 KB: 64 (N) x 64 (K)
-constexpr uint32_t kBBytes = kHalfN * kBK * 2;     // 16 KB
+constexpr uint32_t kStages = 3;
+constexpr uint32_t kSwz = 64;                       // elements per 128-byte swizzled row
+constexpr uint32_t kABoxBytes = kHalfM * kSwz * 2;  // 16 KB: 128 rows x 64 K
+constexpr uint32_t kABytes = kHalfM * kBK * 2;      // 32 KB: two boxes along K
+constexpr uint32_t kBBoxBytes = kSwz * kBK * 2;     // 16 KB: 64 (N) x 128 (K)
+constexpr uint32_t kBBytes = kHalfN * kBK * 2;      // 32 KB: two boxes along N
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kAccCols = kBN;                 // FP32 columns of one accumulator
 constexpr uint32_t kTmemCols = 2 * kAccCols;       // double buffered: all 512
@@ -226,8 +229,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
           uint8_t *st = ring + s * kStageBytes;
           const int32_t xk = static_cast<int32_t>(k * kBK);
           tma_load_pair(st, &map_a, xk, ya, bar);
+          tma_load_pair(st + kABoxBytes, &map_a, xk + static_cast<int32_t>(kSwz), ya, bar);
           tma_load_pair(st + kABytes, &map_b, xb, xk, bar);
-          tma_load_pair(st + kABytes + kBBoxBytes, &map_b, xb + 64, xk, bar);
+          tma_load_pair(st + kABytes + kBBoxBytes, &map_b, xb + static_cast<int32_t>(kSwz), xk, bar);
         }
       }
     }
@@ -247,9 +251,12 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
           const uint32_t sa = smem_addr(ring + s * kStageBytes), sb = sa + kABytes;
           const uint64_t da = smem_desc(sa, 16, 1024), db = smem_desc(sb, kBBoxBytes, 1024);
 #pragma unroll
-          for (uint32_t kk = 0; kk < kBK / 16; ++kk)
-            // K step of 16: +32 bytes inside A's 128-byte swizzled rows, +2 eight-row groups of B.
-            mma_pair(d, da + ((kk * 32u) >> 4), db + ((kk * 2048u) >> 4), idesc, (k | kk) != 0);
+          for (uint32_t kk = 0; kk < kBK / 16; ++kk) {
+            // K step of 16: +32 bytes inside A's 128-byte swizzled rows (the
+            // next A box every 4 steps), +2 eight-row groups of B.
+            const uint32_t a_off = (kk / 4) * kABoxBytes + (kk % 4) * 32u;
+            mma_pair(d, da + (a_off >> 4), db + ((kk * 2048u) >> 4), idesc, (k | kk) != 0);
+          }
           mma_commit_pair(cluster_addr(&empty[s], 0));
           mma_commit_pair(cluster_addr(&empty[s], 1));
         }
@@ -353,9 +360,9 @@ cudaError_t gemm_launch(bool fp16, const void *A, const void *B, void *C, uint32
     return cudaGetLastError();
   }
   CUtensorMap map_a, map_b;
-  cudaError_t e = make_tmap_2d_u16_swizzled(&map_a, A, K, M, K, kBK, kHalfM);
+  cudaError_t e = make_tmap_2d_u16_swizzled(&map_a, A, K, M, K, kSwz, kHalfM);
   if (e != cudaSuccess) return e;
-  e = make_tmap_2d_u16_swizzled(&map_b, B, N, K, N, 64, kBK);
+  e = make_tmap_2d_u16_swizzled(&map_b, B, N, K, N, kSwz, kBK);
   if (e != cudaSuccess) return e;
   const size_t smem = gemm_smem_bytes();
   auto kernel = fp16 ? k_gemm_tc<true> : k_gemm_tc<false>;
