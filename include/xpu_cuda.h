@@ -211,6 +211,20 @@ typedef struct {
 int xpu_qwen3_create(const xpu_qwen3_shape *shape, uint32_t maximum_sequence, int device,
                      uint32_t tp_rank, uint32_t tp_size, xpu_qwen3_engine **out);
 int xpu_qwen3_destroy(xpu_qwen3_engine *engine);
+/* Tensor-parallel rendezvous (tp_size > 1; ranks are processes, one GPU
+ * each, on one NVLink/NVSwitch node). Each rank writes its exchange-region
+ * handle (XPU_TP_HANDLE_BYTES bytes, a CUDA IPC handle) with
+ * xpu_qwen3_tp_handle; the caller all-gathers the handles over its host
+ * process group (the reference has no tensor parallelism; this replaces
+ * nothing) and every rank calls xpu_qwen3_tp_connect with all tp_size handles
+ * in rank order. Decoding before that fails with XPU_ERR_INVALID. Every rank
+ * must then make the same decode/generate calls in the same order; an
+ * exchange that times out (a rank stopped) returns XPU_ERR_TIMEOUT on the
+ * waiting ranks and leaves the engines unusable (recreate them). */
+#define XPU_TP_HANDLE_BYTES 64
+int xpu_qwen3_tp_handle(xpu_qwen3_engine *engine, void *handle);
+int xpu_qwen3_tp_connect(xpu_qwen3_engine *engine, const void *handles, uint32_t count);
+
 /* Seeded synthetic checkpoint: norm weights 1, all other tensors N(0, stddev)
  * drawn per tensor (xpu_fill_normal_bf16 stream = tensor tag: 0 embed, 1 final
  * norm, 2 lm_head, 3 + 11*layer + index in the layer's tensor list). */

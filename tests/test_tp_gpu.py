@@ -1,0 +1,131 @@
+"""Tensor-parallel decode on 2, 4 and 8 GPUs (one process per GPU, gloo for
+the host rendezvous, NVLink peer stores for the exchange): every tp_size
+gives the same greedy tokens and bit-identical logits as one GPU, and a rank
+that never joins a step makes its peers' bounded waits end with
+XPU_ERR_TIMEOUT instead of a hang."""
+
+import os
+import socket
+from datetime import timedelta
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle.qwen3_ref import prompt_ids
+from xpu_playground_b200.qwen3 import Qwen3Engine
+from xpu_playground_b200.qwen3_config import PRESETS
+
+pytestmark = pytest.mark.gpu
+
+NGPU = torch.cuda.device_count() if torch.cuda.is_available() else 0
+SEED = 11
+MAX_SEQ = 256
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_generate(rank, world, port, preset, prompt, n_new, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        eng = Qwen3Engine(PRESETS[preset], MAX_SEQ, device=rank, tp_rank=rank, tp_size=world)
+        eng.init_synthetic(SEED)
+        eng.connect_tensor_parallel()
+        toks = eng.generate(prompt, n_new)
+        q.put((rank, toks, eng.logits()))
+        dist.barrier()
+        eng.close()
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put((rank, repr(e), None))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_ranks(target, world, *args):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, *args, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        results = {}
+        for _ in procs:
+            rank, a, b = q.get(timeout=600)
+            results[rank] = (a, b)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.exitcode is None:
+                p.kill()
+    return results
+
+
+def _single_gpu(preset, prompt, n_new):
+    with Qwen3Engine(PRESETS[preset], MAX_SEQ, device=0) as eng:
+        eng.init_synthetic(SEED)
+        return eng.generate(prompt, n_new), eng.logits()
+
+
+@pytest.mark.parametrize("preset,world", [("tiny", 2), ("qwen3-0.6b", 2), ("qwen3-8b-l2", 2),
+                                          ("qwen3-0.6b", 4), ("qwen3-8b-l2", 4), ("qwen3-8b-l2", 8)])
+def test_tp_matches_single_gpu(preset, world):
+    if NGPU < world:
+        pytest.skip(f"needs {world} GPUs")
+    shape = PRESETS[preset]
+    prompt = prompt_ids(24, shape.vocab, seed=5)
+    n_new = 24
+    ref_toks, ref_logits = _single_gpu(preset, prompt, n_new)
+    results = _run_ranks(_rank_generate, world, preset, prompt, n_new)
+    shard = shape.vocab // world
+    for rank in range(world):
+        toks, logits = results[rank]
+        assert not isinstance(toks, str), toks
+        assert toks == ref_toks, f"rank {rank} tokens differ from tp=1"
+        assert np.array_equal(logits, ref_logits[rank * shard:(rank + 1) * shard]), f"rank {rank} logits differ"
+
+
+def _rank_absent_peer(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    from xpu_playground_b200._lib import XpuError
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        eng = Qwen3Engine(PRESETS["tiny"], MAX_SEQ, device=rank, tp_rank=rank, tp_size=world)
+        eng.init_synthetic(SEED)
+        eng.connect_tensor_parallel()
+        outcome = "no-step"
+        if rank == 0:  # rank 1 never runs the step: rank 0's exchange waits must run out
+            try:
+                eng.decode(7, 0)
+                outcome = "completed"
+            except XpuError as e:
+                outcome = f"status {e.status}"
+            # the engine refuses to continue after a failed exchange
+            try:
+                eng.decode(7, 0)
+                outcome += ", reused"
+            except XpuError as e:
+                outcome += f", then status {e.status}"
+        dist.barrier()  # rank 1 keeps its region mapped until rank 0 is done
+        q.put((rank, outcome, None))
+        eng.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_absent_rank_times_out():
+    if NGPU < 2:
+        pytest.skip("needs 2 GPUs")
+    results = _run_ranks(_rank_absent_peer, 2)
+    assert results[0][0] == "status 4, then status 1"  # XPU_ERR_TIMEOUT, then XPU_ERR_INVALID
+    assert results[1][0] == "no-step"

@@ -60,6 +60,8 @@ SIGNATURES: dict[str, tuple] = {
     "xpu_fill_normal_bf16": (i32, [vp, u64, u64, u64, f32, vp]),
     "xpu_qwen3_create": (i32, [vp, u32, i32, u32, u32, vp]),
     "xpu_qwen3_destroy": (i32, [vp]),
+    "xpu_qwen3_tp_handle": (i32, [vp, vp]),
+    "xpu_qwen3_tp_connect": (i32, [vp, vp, u32]),
     "xpu_qwen3_init_synthetic": (i32, [vp, u64, f32]),
     "xpu_qwen3_set_tensor": (i32, [vp, ctypes.c_char_p, vp, u64]),
     "xpu_qwen3_decode": (i32, [vp, u32, u32, vp]),

@@ -45,7 +45,39 @@ struct DecodeState {
   uint32_t error;       // sticky: 1 = NaN/Inf logits, 2 = exchange timeout
   uint32_t steps;       // completed steps since the last reset
   uint64_t bar_base;    // grid-barrier arrivals before this step (persistent path)
+  uint64_t x_base;      // cross-rank exchange epochs before this step (tensor parallel)
 };
+
+// ---- tensor-parallel exchange (persistent path, tp_size > 1) ----
+// Every rank owns one exchange region in its device memory; every rank
+// writes into every region (its own and its peers', the latter over NVLink
+// through CUDA IPC mappings):
+//   part[2][8][H]   FP32 canonical-chunk partials of o_proj (0) and down (1):
+//                   rank r writes chunks [8 r / tp, 8 (r + 1) / tp)
+//   flag[kMaxTp]    flag[r] = the last exchange epoch rank r has published
+//   lm[kMaxTp]      lm[r] = rank r's lm_head candidate for the current step
+// Exchange k (1-based) of a step has epoch x_base + k; a step makes
+// 2 * layers + 1 of them, so epochs only grow and never need clearing.
+constexpr uint32_t kMaxTp = 8;
+
+struct LmSlot {
+  float value;
+  uint32_t index;
+  uint32_t bad;
+  uint32_t pad;
+  unsigned long long epoch;
+};
+
+struct TpLinks {
+  float *part[kMaxTp];                // region base of rank q ([2][8][H] floats)
+  unsigned long long *flag[kMaxTp];   // flag array of rank q
+  LmSlot *lm[kMaxTp];                 // lm slots of rank q
+};
+
+__host__ __device__ inline size_t tp_region_part_bytes(uint32_t H) { return static_cast<size_t>(2) * 8 * H * 4; }
+__host__ __device__ inline size_t tp_region_flag_offset(uint32_t H) { return tp_region_part_bytes(H); }
+__host__ __device__ inline size_t tp_region_lm_offset(uint32_t H) { return tp_region_flag_offset(H) + 8 * kMaxTp; }
+__host__ __device__ inline size_t tp_region_bytes(uint32_t H) { return tp_region_lm_offset(H) + sizeof(LmSlot) * kMaxTp; }
 
 struct DecodeDims {
   uint32_t H;           // hidden size
@@ -73,6 +105,7 @@ struct LayerWeights {
 
 struct DecodeBuffers {
   bf16 *x;           // residual stream [H]
+  bf16 *x2;          // second residual buffer (tensor parallel: x and x2 alternate)
   bf16 *q;           // [QH_l * 128]
   bf16 *attn;        // attention output [QH_l * 128]
   bf16 *h;           // SwiGLU output [I_l]
@@ -95,6 +128,7 @@ struct DecodeBuffers {
   const bf16 *embed;       // [vocab][H]
   const bf16 *final_norm;
   const bf16 *lm_head;     // [V_l][H]
+  TpLinks tp;              // tensor-parallel exchange regions (tp_size > 1)
 };
 
 __host__ __device__ inline uint32_t pos_chunks_dev(uint32_t max_seq) { return (max_seq + kPosChunk - 1) / kPosChunk; }

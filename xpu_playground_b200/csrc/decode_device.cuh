@@ -111,6 +111,33 @@ __device__ inline bool arrive_one(unsigned *counter, unsigned total, int *flag) 
 
 __device__ __forceinline__ void flag_error(DecodeState *st, uint32_t bits) { atomicOr(&st->error, bits); }
 
+// System-scope release store / acquire load (cross-GPU exchange flags).
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits (bounded) until every rank's flag in this rank's region reaches
+// epoch; false on a timeout (error bit 4 set) or when another waiter failed.
+__device__ inline bool wait_rank_flags(const DecodeDims &d, const DecodeBuffers &b, unsigned long long epoch) {
+  const unsigned long long *own = b.tp.flag[d.tp_rank];
+  const long long start = clock64();
+  for (uint32_t q = 0; q < d.tp_size; ++q) {
+    while (ld_acquire_sys(own + q) < epoch) {
+      if (*reinterpret_cast<volatile uint32_t *>(&b.state->error) & kErrPipelineTimeout) return false;
+      if (clock64() - start > kWaitCycles) {
+        flag_error(b.state, kErrPipelineTimeout);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
 // ------------------------------------------------------------------ QKV ----
 // Items: (tile, split) of [Wq; Wk; Wv]; partial sums to part_qkv[split][row].
 __device__ inline bool qkv_items(const DecodeDims &d, const DecodeBuffers &b, const StreamSmem &sm,
@@ -209,6 +236,73 @@ __device__ inline bool rowpar_items(const DecodeDims &d, const DecodeBuffers &b,
   return true;
 }
 
+// Tensor-parallel variant: this rank's canonical-chunk partials go to every
+// rank's exchange region (slot `which`: 0 o_proj, 1 down), 4 rows per 16-byte
+// store; the residual is applied after the cross-rank barrier by
+// stage_residual_rms.
+__device__ inline bool rowpar_items_tp(const DecodeDims &d, const DecodeBuffers &b, const StreamSmem &sm,
+                                       const StreamGeom &g, uint32_t &it, uint32_t which) {
+  const uint32_t lane = lane_id(), cw = cwarp();
+  for (uint32_t item = blockIdx.x; item < g.items(); item += gridDim.x) {
+    const uint32_t tile = item / g.kparts, part = item % g.kparts, chunk = d.chunk0 + part;
+    float acc[kRowsPerWarp];
+    if (!stream_consume_item<bf16>(sm, g, sm.xs + part * (g.kt / 8), it, acc)) return false;
+    const uint32_t row = tile * kStageRows + kRowsPerWarp * cw;
+    if (lane < d.tp_size) {
+      const size_t off = (static_cast<size_t>(which) * kCanonChunks + chunk) * d.H + row;
+      *reinterpret_cast<float4 *>(b.tp.part[lane] + off) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    }
+  }
+  return true;
+}
+
+// After the cross-rank barrier: x_new = bf16(x_old + bf16(sum of the 8
+// canonical chunks of exchange slot `which`, in chunk order)) - the same
+// arithmetic as rowpar_finish - staged into xs and RMS-normalised with w
+// (as stage_rms); CTA 0 also stores x_new to x_out for the next residual.
+__device__ inline void stage_residual_rms(const DecodeDims &d, const DecodeBuffers &b, uint32_t which,
+                                          const bf16 *x_old, bf16 *x_out, const bf16 *w, uint4 *xs,
+                                          float *scratch) {
+  const uint32_t t = ctid(), H = d.H;
+  const float *part = b.tp.part[d.tp_rank] + static_cast<size_t>(which) * kCanonChunks * H;
+  float ss = 0.f;
+  for (uint32_t c = t; c < H / 8; c += kConsumerThreads) {
+    float y[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (uint32_t k = 0; k < kCanonChunks; ++k) {
+      const float4 lo = __ldcg(reinterpret_cast<const float4 *>(part + static_cast<size_t>(k) * H + 8 * c));
+      const float4 hi = __ldcg(reinterpret_cast<const float4 *>(part + static_cast<size_t>(k) * H + 8 * c + 4));
+      y[0] = __fadd_rn(y[0], lo.x); y[1] = __fadd_rn(y[1], lo.y); y[2] = __fadd_rn(y[2], lo.z); y[3] = __fadd_rn(y[3], lo.w);
+      y[4] = __fadd_rn(y[4], hi.x); y[5] = __fadd_rn(y[5], hi.y); y[6] = __fadd_rn(y[6], hi.z); y[7] = __fadd_rn(y[7], hi.w);
+    }
+    const uint4 xv = ldcg16(x_old + 8 * c);
+    const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      o[j] = pack_bf16x2(__fadd_rn(bf16_lo(xa[j]), round_bf16(y[2 * j])), __fadd_rn(bf16_hi(xa[j]), round_bf16(y[2 * j + 1])));
+    const uint4 nv = make_uint4(o[0], o[1], o[2], o[3]);
+    xs[c] = nv;
+    if (blockIdx.x == 0) reinterpret_cast<uint4 *>(x_out)[c] = nv;
+    ss = sq8(nv, ss);
+  }
+  ss = consumer_sum(ss, scratch);
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(H) + d.eps);
+  const uint4 *w4 = reinterpret_cast<const uint4 *>(w);
+  for (uint32_t c = t; c < H / 8; c += kConsumerThreads) {
+    const uint4 xv = xs[c], wv = w4[c];
+    const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lo = round_bf16(__fmul_rn(bf16_lo(wa[j]), round_bf16(__fmul_rn(bf16_lo(xa[j]), r))));
+      const float hi = round_bf16(__fmul_rn(bf16_hi(wa[j]), round_bf16(__fmul_rn(bf16_hi(xa[j]), r))));
+      o[j] = pack_bf16x2(lo, hi);
+    }
+    xs[c] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  consumer_sync();
+}
+
 // Residual epilogue of every row tile this CTA completed:
 // x = bf16(x + bf16(sum of the 8 canonical chunks, in chunk order)).
 __device__ inline void rowpar_finish(const DecodeDims &d, const DecodeBuffers &b, const StreamGeom &g,
@@ -264,7 +358,7 @@ struct LmShared {
 // and advances the step state. Returns false on a timeout.
 __device__ inline bool lm_items_and_argmax(const DecodeDims &d, const DecodeBuffers &b, const StreamSmem &sm,
                                            const StreamGeom &g, uint32_t &it, LmShared &ls, uint32_t pos,
-                                           uint64_t bar_advance) {
+                                           uint64_t bar_advance, uint64_t lm_epoch = 0, uint64_t x_advance = 0) {
   const uint32_t lane = lane_id(), cw = cwarp(), t = ctid();
   ArgBest best{-INFINITY, 0xffffffffu};
   uint32_t bad = 0;
@@ -312,6 +406,37 @@ __device__ inline bool lm_items_and_argmax(const DecodeDims &d, const DecodeBuff
       uint32_t fbad = ls.wbad[0];
       for (int i = 1; i < kConsumerWarps; ++i) { fb = arg_better(fb, ls.wbest[i]); fbad |= ls.wbad[i]; }
       DecodeState *st = b.state;
+      if (d.tp_size > 1) {
+        // Publish this rank's candidate to every rank, then combine all
+        // ranks' candidates (global indices; lowest index on ties).
+        for (uint32_t q = 0; q < d.tp_size; ++q) {
+          LmSlot *slot = b.tp.lm[q] + d.tp_rank;
+          slot->value = fb.value;
+          slot->index = fb.index;
+          slot->bad = fbad;
+        }
+        __threadfence_system();
+        for (uint32_t q = 0; q < d.tp_size; ++q) st_release_sys(&(b.tp.lm[q] + d.tp_rank)->epoch, lm_epoch);
+        const LmSlot *own = b.tp.lm[d.tp_rank];
+        bool ok = true;
+        const long long start = clock64();
+        for (uint32_t q = 0; ok && q < d.tp_size; ++q)
+          while (ld_acquire_sys(&own[q].epoch) < lm_epoch) {
+            if (clock64() - start > kWaitCycles) { ok = false; break; }
+          }
+        if (!ok) {
+          flag_error(st, kErrPipelineTimeout);
+        } else {
+          fb = ArgBest{-INFINITY, 0xffffffffu};
+          fbad = 0;
+          for (uint32_t q = 0; q < d.tp_size; ++q) {
+            const ArgBest e{__ldcg(&own[q].value), __ldcg(&own[q].index)};
+            fb = arg_better(fb, e);
+            fbad |= __ldcg(&own[q].bad);
+          }
+        }
+        st->x_base += x_advance;
+      }
       const uint32_t next = (fbad || fb.index == 0xffffffffu) ? 0xffffffffu : fb.index;
       if (next == 0xffffffffu) st->error |= 1u;
       st->next = next;

@@ -22,6 +22,17 @@
 // state) is advanced by the CTA that finishes the step. Waits are bounded
 // (kWaitCycles); a timeout sets error bit 4, every other waiter sees it and
 // leaves, and the host re-arms the barrier.
+//
+// Tensor parallelism (tp_size > 1): o_proj and down write this rank's
+// canonical-chunk partials into every rank's exchange region (NVLink stores
+// through CUDA IPC mappings), then pass a cross-rank barrier: the grid
+// barrier's last arriving CTA publishes the exchange epoch to every rank's
+// flag slot, and every CTA waits until all ranks' flags carry it. Each CTA
+// then sums the 8 chunks in canonical order itself (stage_residual_rms: the
+// same arithmetic as the single-GPU residual epilogue, so every tp_size
+// yields identical bits) and stages the next RMSNorm input. The lm_head
+// candidates are exchanged the same way and combined with the lowest index
+// winning ties.
 #include <cstdlib>
 #include <vector>
 
@@ -93,6 +104,25 @@ __device__ bool grid_barrier(unsigned long long *counter, unsigned long long tar
   return *flag != 0;
 }
 
+// Cross-rank barrier: this rank's grid barrier, whose last arriving CTA
+// publishes `epoch` to every rank's flag slot after a system-scope fence;
+// every CTA then waits until all ranks' flags reach epoch, which makes every
+// rank's remote stores issued before the barrier visible here.
+__device__ bool tp_barrier(const StepParams &p, unsigned long long target, unsigned long long epoch, int *flag) {
+  __threadfence_system();
+  consumer_sync();
+  if (ctid() == 0) {
+    const unsigned long long old = atomicAdd(p.bar, 1ull);
+    if (old + 1 == target) {
+      __threadfence_system();
+      for (uint32_t q = 0; q < p.d.tp_size; ++q) st_release_sys(p.b.tp.flag[q] + p.d.tp_rank, epoch);
+    }
+    *flag = wait_rank_flags(p.d, p.b, epoch);
+  }
+  consumer_sync();
+  return *flag != 0;
+}
+
 template <int G>
 __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constant__ StepParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -140,15 +170,24 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constan
   stamp();
   const uint32_t npc = pos_chunks_dev(d.max_seq), nch = (n + kPosChunk - 1) / kPosChunk;
   const uint32_t attn_items = d.KVH_l * nch;
-  uint32_t it = 0, nbar = 0;
+  const bool tp = d.tp_size > 1;
+  const unsigned long long x_base = st->x_base;
+  uint32_t it = 0, nbar = 0, nx = 0;
   auto barrier = [&]() -> bool {
     ++nbar;
     return grid_barrier(p.bar, bar_base + static_cast<unsigned long long>(nbar) * gridDim.x, st, &bflag);
   };
+  auto xbarrier = [&]() -> bool {
+    ++nbar;
+    ++nx;
+    return tp_barrier(p, bar_base + static_cast<unsigned long long>(nbar) * gridDim.x, x_base + nx, &bflag);
+  };
   for (uint32_t l = 0; l < p.n_layers; ++l) {
     const LayerWeights w = p.layers[l];
     // trace events per layer: [staged, items, finished, barrier] x 6 phases
-    stage_rms(l == 0 ? x_embed : b.x, w.in_norm, d.H, d.eps, sm.xs, sm.scratch);
+    // (tensor parallel: layers after the first were staged by the previous
+    // layer's down-projection exchange)
+    if (!tp || l == 0) stage_rms(l == 0 ? x_embed : b.x, w.in_norm, d.H, d.eps, sm.xs, sm.scratch);
     stamp();
     if (!qkv_items(d, b, sm, p.g.qkv, it)) { flag_error(st, kErrPipelineTimeout); return; }
     stamp();
@@ -172,13 +211,22 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constan
     stamp();
     stage_copy(b.attn, d.QH_l * kHD, sm.xs);
     stamp();
-    if (!rowpar_items(d, b, sm, p.g.o, it)) { flag_error(st, kErrPipelineTimeout); return; }
-    stamp();
-    rowpar_finish(d, b, p.g.o, s_last);
-    stamp();
-    if (!barrier()) return;
-    stamp();
-    stage_rms(b.x, w.post_norm, d.H, d.eps, sm.xs, sm.scratch);
+    if (tp) {
+      if (!rowpar_items_tp(d, b, sm, p.g.o, it, 0)) { flag_error(st, kErrPipelineTimeout); return; }
+      stamp();
+      stamp();
+      if (!xbarrier()) return;
+      stamp();
+      stage_residual_rms(d, b, 0, b.x, b.x2, w.post_norm, sm.xs, sm.scratch);
+    } else {
+      if (!rowpar_items(d, b, sm, p.g.o, it)) { flag_error(st, kErrPipelineTimeout); return; }
+      stamp();
+      rowpar_finish(d, b, p.g.o, s_last);
+      stamp();
+      if (!barrier()) return;
+      stamp();
+      stage_rms(b.x, w.post_norm, d.H, d.eps, sm.xs, sm.scratch);
+    }
     stamp();
     if (!gateup_items(d, b, sm, p.g.gu, it)) { flag_error(st, kErrPipelineTimeout); return; }
     stamp();
@@ -187,16 +235,27 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constan
     stamp();
     stage_copy(b.h, d.I_l, sm.xs);
     stamp();
-    if (!rowpar_items(d, b, sm, p.g.down, it)) { flag_error(st, kErrPipelineTimeout); return; }
-    stamp();
-    rowpar_finish(d, b, p.g.down, s_last);
-    stamp();
-    if (!barrier()) return;
-    stamp();
+    if (tp) {
+      if (!rowpar_items_tp(d, b, sm, p.g.down, it, 1)) { flag_error(st, kErrPipelineTimeout); return; }
+      stamp();
+      stamp();
+      if (!xbarrier()) return;
+      stamp();
+      const bf16 *next_norm = l + 1 < p.n_layers ? p.layers[l + 1].in_norm : b.final_norm;
+      stage_residual_rms(d, b, 1, b.x2, b.x, next_norm, sm.xs, sm.scratch);
+    } else {
+      if (!rowpar_items(d, b, sm, p.g.down, it)) { flag_error(st, kErrPipelineTimeout); return; }
+      stamp();
+      rowpar_finish(d, b, p.g.down, s_last);
+      stamp();
+      if (!barrier()) return;
+      stamp();
+    }
   }
-  stage_rms(b.x, b.final_norm, d.H, d.eps, sm.xs, sm.scratch);
+  if (!tp) stage_rms(b.x, b.final_norm, d.H, d.eps, sm.xs, sm.scratch);
   stamp();
-  if (!lm_items_and_argmax(d, b, sm, p.g.lm, it, ls, pos, static_cast<uint64_t>(nbar) * gridDim.x))
+  if (!lm_items_and_argmax(d, b, sm, p.g.lm, it, ls, pos, static_cast<uint64_t>(nbar) * gridDim.x,
+                           tp ? x_base + nx + 1 : 0, tp ? nx + 1 : 0))
     flag_error(st, kErrPipelineTimeout);
   stamp();
 }

@@ -9,7 +9,11 @@
 //
 // Tensor parallelism (tp_size > 1) shards q/k/v and gate/up by rows (heads,
 // intermediate units), o_proj/down by columns in canonical chunks, and the
-// lm_head by vocabulary rows.
+// lm_head by vocabulary rows. Ranks are separate processes, one per GPU:
+// each exports its exchange region as a CUDA IPC handle, the caller
+// all-gathers the handles over its host process group and hands them to
+// tp_connect, which maps the peers' regions (NVLink peer access). The
+// persistent step kernel then exchanges partials through them.
 #include <algorithm>
 #include <cmath>
 #include <stdexcept>
@@ -94,6 +98,7 @@ class Qwen3Engine {
     if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
     if (plan_) step_plan_destroy(plan_);
     if (stream_) cudaStreamSynchronize(stream_);
+    for (void *p : peer_regions_) cudaIpcCloseMemHandle(p);
     for (void *p : allocations_) cudaFree(p);
     if (host_state_) cudaFreeHost(host_state_);
     if (stream_) cudaStreamDestroy(stream_);
@@ -214,7 +219,50 @@ class Qwen3Engine {
   // per-phase kernels. Both compute identical bits.
   void set_mode(int mode) {
     if (mode != 0 && mode != 1) throw InvalidArg("decode mode must be 0 (persistent) or 1 (graph)");
+    if (mode == 1 && tp_ > 1) throw InvalidArg("tensor-parallel decode runs in persistent mode (0) only");
     mode_ = mode;
+  }
+
+  // ------------------------------------------------- tensor parallel ----
+  // CUDA IPC handle of this rank's exchange region.
+  void tp_handle(void *out) const {
+    if (tp_ == 1) throw InvalidArg("tp_handle: engine is not tensor parallel (tp_size 1)");
+    cudaIpcMemHandle_t h;
+    CK(cudaSetDevice(device_));
+    CK(cudaIpcGetMemHandle(&h, xregion_));
+    static_assert(sizeof(h) == XPU_TP_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(out, &h, sizeof(h));
+  }
+
+  // Maps every peer's exchange region (handles[q] from rank q; this rank's
+  // own entry is not used) and links all regions into the decode buffers.
+  void tp_connect(const uint8_t *handles, uint32_t count) {
+    if (tp_ == 1) throw InvalidArg("tp_connect: engine is not tensor parallel (tp_size 1)");
+    if (count != tp_) throw InvalidArg("tp_connect: expected " + std::to_string(tp_) + " handles, got " + std::to_string(count));
+    if (connected_) throw InvalidArg("tp_connect: already connected");
+    CK(cudaSetDevice(device_));
+    TpLinks links{};
+    const uint32_t H = d_.H;
+    for (uint32_t q = 0; q < tp_; ++q) {
+      uint8_t *base = xregion_;
+      if (q != rank_) {
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, handles + static_cast<size_t>(q) * XPU_TP_HANDLE_BYTES, sizeof(h));
+        void *ptr = nullptr;
+        CK(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess));
+        peer_regions_.push_back(ptr);
+        base = static_cast<uint8_t *>(ptr);
+      }
+      links.part[q] = reinterpret_cast<float *>(base);
+      links.flag[q] = reinterpret_cast<unsigned long long *>(base + tp_region_flag_offset(H));
+      links.lm[q] = reinterpret_cast<LmSlot *>(base + tp_region_lm_offset(H));
+    }
+    b_.tp = links;
+    connected_ = true;
+    if (plan_) {  // parameters hold the decode buffers: rebuild on next use
+      step_plan_destroy(plan_);
+      plan_ = nullptr;
+    }
   }
   int mode() const { return mode_; }
 
@@ -441,6 +489,11 @@ class Qwen3Engine {
     const uint64_t rows_qkv = qr + 2 * kvr;
     b_ = DecodeBuffers{};
     b_.x = dev_alloc<bf16>(H);
+    b_.x2 = dev_alloc<bf16>(H);
+    if (tp_ > 1) {
+      xregion_ = dev_alloc<uint8_t>(tp_region_bytes(static_cast<uint32_t>(H)));
+      CK(cudaMemset(xregion_, 0, tp_region_bytes(static_cast<uint32_t>(H))));
+    }
     b_.q = dev_alloc<bf16>(qr);
     b_.attn = dev_alloc<bf16>(qr);
     b_.h = dev_alloc<bf16>(d_.I_l);
@@ -528,6 +581,11 @@ class Qwen3Engine {
   // the sticky bit before reporting, so the next call starts clean.
   void after_step_check() {
     const uint32_t err = host_state_->error;
+    if ((err & 4u) && tp_ > 1) {
+      // The ranks' exchange epochs may now disagree: the engines cannot resume.
+      broken_ = true;
+      check_state_error(err);
+    }
     if (err & 4u) {
       if (plan_) CK(step_reset(plan_, stream_));
       host_state_->error = 0;
@@ -544,6 +602,10 @@ class Qwen3Engine {
 
   void ensure_graph() {
     if (!loaded_) throw InvalidArg("no weights: call init_synthetic, load a checkpoint or set every tensor");
+    if (broken_)
+      throw InvalidArg("a tensor-parallel exchange timed out earlier: destroy and recreate the engines on every rank");
+    if (tp_ > 1 && !connected_) throw InvalidArg("tensor-parallel engine not connected: call xpu_qwen3_tp_connect");
+    if (tp_ > 1 && mode_ != 0) throw InvalidArg("tensor-parallel decode runs in persistent mode (0) only");
     if (mode_ == 0) {
       if (!plan_) {
         CK(cudaSetDevice(device_));
@@ -589,6 +651,9 @@ class Qwen3Engine {
   uint64_t weights_bytes_ = 0, embed_bytes_ = 0;
   size_t tensors_set_ = 0;
   bool loaded_ = false;
+  uint8_t *xregion_ = nullptr;            // this rank's exchange region (tp_size > 1)
+  std::vector<void *> peer_regions_;      // peers' regions mapped through CUDA IPC
+  bool connected_ = false, broken_ = false;
 };
 
 }  // namespace xpu
@@ -642,6 +707,20 @@ int xpu_qwen3_create(const xpu_qwen3_shape *shape, uint32_t maximum_sequence, in
 
 int xpu_qwen3_destroy(xpu_qwen3_engine *engine) {
   return guarded([&] { delete engine; });
+}
+
+int xpu_qwen3_tp_handle(xpu_qwen3_engine *engine, void *handle) {
+  return guarded([&] {
+    if (!handle) throw xpu::InvalidArg("xpu_qwen3_tp_handle: null pointer");
+    eng(engine).tp_handle(handle);
+  });
+}
+
+int xpu_qwen3_tp_connect(xpu_qwen3_engine *engine, const void *handles, uint32_t count) {
+  return guarded([&] {
+    if (!handles) throw xpu::InvalidArg("xpu_qwen3_tp_connect: null pointer");
+    eng(engine).tp_connect(static_cast<const uint8_t *>(handles), count);
+  });
 }
 
 int xpu_qwen3_init_synthetic(xpu_qwen3_engine *engine, uint64_t seed, float stddev) {

@@ -25,6 +25,16 @@ def shape_struct(shape: Qwen3Shape) -> _lib.Qwen3ShapeC:
                             shape.rope_theta)
 
 
+def exchange_handles(handle: bytes, group=None) -> list[bytes]:
+    """All-gather one bytes object per rank over torch.distributed, in rank order."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    out: list = [None] * world
+    dist.all_gather_object(out, handle, group=group)
+    return [bytes(h) for h in out]
+
+
 class Qwen3Engine:
     def __init__(self, shape: Qwen3Shape, max_seq: int, device: int = 0, tp_rank: int = 0,
                  tp_size: int = 1, mode: str | None = None):
@@ -65,6 +75,27 @@ class Qwen3Engine:
     def load_weights(self, weights: dict[str, np.ndarray]) -> None:
         for name, bits in weights.items():
             self.set_tensor(name, bits)
+
+    # ---------------------------------------------------- tensor parallel ----
+    TP_HANDLE_BYTES = 64
+
+    def tp_handle(self) -> bytes:
+        """This rank's exchange-region handle (CUDA IPC), to be all-gathered."""
+        buf = ctypes.create_string_buffer(self.TP_HANDLE_BYTES)
+        _lib.check(self.lib.xpu_qwen3_tp_handle(self._h, buf))
+        return buf.raw
+
+    def tp_connect(self, handles: list[bytes]) -> None:
+        """Maps the peers' exchange regions: handles[q] from rank q."""
+        if any(len(h) != self.TP_HANDLE_BYTES for h in handles):
+            raise ValueError("tp_connect: every handle is 64 bytes")
+        blob = b"".join(handles)
+        _lib.check(self.lib.xpu_qwen3_tp_connect(self._h, blob, len(handles)))
+
+    def connect_tensor_parallel(self, group=None) -> None:
+        """All-gathers the ranks' handles over a torch.distributed process
+        group (any backend) and connects."""
+        self.tp_connect(exchange_handles(self.tp_handle(), group))
 
     # ------------------------------------------------------------- decode ----
     def decode(self, token: int, position: int) -> int:
