@@ -512,10 +512,11 @@ class Qwen3Engine {
     logits_ = dev_alloc<uint16_t>(d_.V_l);
     b_.logits = logits_;
     const uint64_t heads_qkv = d_.QH_l + 2ull * d_.KVH_l;
-    unsigned *counters = dev_alloc<unsigned>(heads_qkv + d_.KVH_l + H / kTileRows + 1);
-    CK(cudaMemset(counters, 0, (heads_qkv + d_.KVH_l + H / kTileRows + 1) * sizeof(unsigned)));
-    b_.cnt_qkv = counters;
-    b_.cnt_attn = counters + heads_qkv;
+    n_counters_ = heads_qkv + d_.KVH_l + H / kTileRows + 1;
+    counters_ = dev_alloc<unsigned>(n_counters_);
+    CK(cudaMemset(counters_, 0, n_counters_ * sizeof(unsigned)));
+    b_.cnt_qkv = counters_;
+    b_.cnt_attn = counters_ + heads_qkv;
     b_.cnt_tile = b_.cnt_attn + d_.KVH_l;
     b_.cnt_lm = b_.cnt_tile + H / kTileRows;
     state_ = dev_alloc<DecodeState>(1);
@@ -587,7 +588,10 @@ class Qwen3Engine {
       check_state_error(err);
     }
     if (err & 4u) {
+      // Re-arm the grid barrier and every arrival counter (a step that gave
+      // up can leave any of them mid-count).
       if (plan_) CK(step_reset(plan_, stream_));
+      CK(cudaMemsetAsync(counters_, 0, n_counters_ * sizeof(unsigned), stream_));
       host_state_->error = 0;
       write_state();
       CK(cudaStreamSynchronize(stream_));
@@ -651,6 +655,8 @@ class Qwen3Engine {
   uint64_t weights_bytes_ = 0, embed_bytes_ = 0;
   size_t tensors_set_ = 0;
   bool loaded_ = false;
+  unsigned *counters_ = nullptr;          // every arrival counter of the decode step
+  uint64_t n_counters_ = 0;
   uint8_t *xregion_ = nullptr;            // this rank's exchange region (tp_size > 1)
   std::vector<void *> peer_regions_;      // peers' regions mapped through CUDA IPC
   bool connected_ = false, broken_ = false;
