@@ -297,11 +297,12 @@ cudaError_t step_plan_create(const DecodeDims &d, const DecodeBuffers &b, const 
   g.gu = make_geom(layers[0].wgu, d.H, 0, 2 * d.I_l, d.H, 1);
   g.down = make_geom(layers[0].wd, d.I_l, 0, d.H, d.I_l / d.chunks_l, d.chunks_l);
   g.lm = make_geom(b.lm_head, d.H, 0, d.V_l, d.H, 1);
-  // One ring for every matrix: slot = the largest stage, 128 KB in all.
+  // One ring for every matrix: slot = the largest stage, as many slots (2-8)
+  // as the per-CTA shared memory leaves after the activation/attention
+  // region. The ring is how far the producer can run ahead while the
+  // consumers are in attention or a barrier, so it gets all the room.
   uint32_t slot = 0;
   for (const StreamGeom *x : {&g.qkv, &g.o, &g.gu, &g.down, &g.lm}) slot = std::max(slot, stage_bytes(*x));
-  const uint32_t nslots = std::max(2u, std::min(8u, (128u * 1024u) / slot));
-  for (StreamGeom *x : {&g.qkv, &g.o, &g.gu, &g.down, &g.lm}) { x->slot = slot; x->stages = nslots; }
   plan->group = static_cast<int>(d.QH_l / d.KVH_l);
   size_t attn_bytes = 0;
   switch (plan->group) {
@@ -313,13 +314,25 @@ cudaError_t step_plan_create(const DecodeDims &d, const DecodeBuffers &b, const 
   }
   const uint32_t stage_elems = std::max(std::max(d.H, K_o), d.I_l);
   p.x_elems = std::max<uint32_t>(stage_elems, static_cast<uint32_t>((attn_bytes + 1) / 2));
+
+  int dev = 0, sms = 0, smem_optin = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) { delete plan; return e; }
+  // Static shared memory of k_step (s_last, LmShared, flags) stays under 1 KB.
+  const size_t budget = static_cast<size_t>(smem_optin) - 1024;
+  uint32_t nslots = 8;
+  while (nslots > 2) {
+    g.qkv.slot = slot;
+    g.qkv.stages = nslots;
+    if (stream_smem_bytes(g.qkv, p.x_elems) <= budget) break;
+    --nslots;
+  }
+  for (StreamGeom *x : {&g.qkv, &g.o, &g.gu, &g.down, &g.lm}) { x->slot = slot; x->stages = nslots; }
   plan->smem = stream_smem_bytes(g.qkv, p.x_elems);
 
   // Items a CTA owns in one phase must fit the deferred-arrival table.
-  int dev = 0, sms = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (e != cudaSuccess) { delete plan; return e; }
   plan->grid = static_cast<uint32_t>(sms);
   for (const StreamGeom *x : {&g.qkv, &g.o, &g.down})
     if ((x->items() + plan->grid - 1) / plan->grid > kMaxLocalItems) { delete plan; return cudaErrorInvalidConfiguration; }
