@@ -7,6 +7,11 @@
       (the reference's host-primitive test; prints "... PASS")
     - libref_model.so     <- qwen3/model.cpp + oracle/ref_model_shim.cpp
       (its bf16 codec and config/checkpoint validator behind a C shim)
+    - test_gpu_dispatch_cuda <- qwen3/tests/test_gpu_dispatch.cpp + qwen3/model.cpp,
+      unchanged, against the reference's own runtime header, with the CUDA
+      implementation of that runtime (xpu_playground_b200/host/qwen3/
+      level_zero_runtime_cuda.cpp, Level Zero handle types from host/ze_shim)
+      and libxpu_cuda: the reference's kernel-dispatch test run on a B200.
   The GPU box has no reference tree; it uses the files built here.
 """
 
@@ -63,6 +68,21 @@ def build_reference() -> list[Path]:
         _run(["g++", "-std=c++17", "-O2", "-fPIC", "-shared", f"-I{qwen3}", str(shim),
               str(qwen3 / "model.cpp"), "-o", str(lib)])
     outs.append(lib)
+
+    repo = HERE.parent
+    pkg = repo / "xpu_playground_b200"
+    runtime_src = pkg / "host" / "qwen3" / "level_zero_runtime_cuda.cpp"
+    libdir = pkg / "lib"
+    cuda = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+    dispatch = REF_OUT / "test_gpu_dispatch_cuda"
+    srcs = [qwen3 / "tests" / "test_gpu_dispatch.cpp", qwen3 / "model.cpp", runtime_src]
+    if (libdir / "libxpu_cuda.so").exists() and _stale(dispatch, srcs + [Path(__file__), libdir / "libxpu_cuda.so"]):
+        _run(["g++", "-std=c++17", "-O2", f"-I{qwen3}", f"-I{pkg / 'host' / 'ze_shim'}", f"-I{repo / 'include'}",
+              f"-I{cuda / 'include'}", *map(str, srcs), "-o", str(dispatch), f"-L{libdir}", "-lxpu_cuda",
+              f"-L{cuda / 'lib64'}", "-lcudart_static", "-ldl", "-lpthread", "-lrt",
+              f"-Wl,-rpath,{libdir}", "-Wl,-rpath,$ORIGIN/../../xpu_playground_b200/lib"])
+    if dispatch.exists():
+        outs.append(dispatch)
     return outs
 
 

@@ -62,3 +62,20 @@ def test_attention_group_sizes():
 def test_check_raises_with_message():
     with pytest.raises(_lib.XpuError, match="XPU_ERR_INVALID"):
         _lib.call("xpu_gemv", 0, None, None, None, 1, 1, None)
+
+
+def test_runtime_library_exports_the_reference_class_api():
+    """libxpu_qwen3_runtime.so defines qwen3::LevelZeroRuntime's members
+    (qwen3/level_zero_runtime.hpp:19-32)."""
+    import subprocess
+    from xpu_playground_b200 import build
+    out = subprocess.run(["nm", "-DC", "--defined-only", str(build.RUNTIME_LIB)], capture_output=True,
+                         text=True, check=True).stdout
+    for sym in ("qwen3::LevelZeroRuntime::LevelZeroRuntime(std::__cxx11::basic_string",
+                "qwen3::LevelZeroRuntime::~LevelZeroRuntime()",
+                "qwen3::LevelZeroRuntime::require_bmg_and_memory(unsigned long) const",
+                "qwen3::LevelZeroRuntime::allocate_device(unsigned long, unsigned long)",
+                "qwen3::LevelZeroRuntime::copy_to_device(void*, void const*, unsigned long)",
+                "qwen3::LevelZeroRuntime::copy_from_device(void*, void const*, unsigned long)",
+                "qwen3::LevelZeroRuntime::launch(std::__cxx11::basic_string"):
+        assert sym in out, sym

@@ -56,12 +56,18 @@ BENCH_PROGRAMS: dict[str, str] = {
 # Other C++ host programs: name -> sources under host/ (all link libxpu_cuda.so).
 HOST_PROGRAMS: dict[str, list[str]] = {
     "peak_sycl": ["peak_sycl.cpp"],
+    "runtime_selftest": ["qwen3/runtime_selftest.cpp", "qwen3/level_zero_runtime_cuda.cpp"],
 }
+# The reference's Qwen3 kernel runtime API on CUDA (class qwen3::LevelZeroRuntime,
+# declared in host/qwen3_api/level_zero_runtime.hpp).
+RUNTIME_LIB = LIB_DIR / "libxpu_qwen3_runtime.so"
+RUNTIME_SRC = HOST / "qwen3" / "level_zero_runtime_cuda.cpp"
+QWEN3_API = HOST / "qwen3_api"
 
 
 def _headers() -> list[Path]:
     return sorted(list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h")) +
-                  list(HOST.glob("*.hpp")))
+                  list(HOST.glob("**/*.hpp")) + list(HOST.glob("**/*.h")))
 
 
 def _stale(target: Path, sources: list[Path]) -> bool:
@@ -116,12 +122,16 @@ def build_programs() -> list[Path]:
         outputs.append(out)
         if _stale(out, [HOST / src, LIB, Path(__file__), *headers]):
             _run([CXX, *CXX_FLAGS, "-DXPU_STANDALONE_HOST", str(HOST / src), "-o", str(out), *link, rpath])
+    if _stale(RUNTIME_LIB, [RUNTIME_SRC, LIB, Path(__file__), *headers]):
+        _run([CXX, *CXX_FLAGS, f"-I{QWEN3_API}", "-shared", str(RUNTIME_SRC), "-o", str(RUNTIME_LIB), *link,
+              "-Wl,-rpath,$ORIGIN"])
+    outputs.append(RUNTIME_LIB)
     for name, files in HOST_PROGRAMS.items():
         srcs = [HOST / f for f in files]
         out = BIN_DIR / name
         outputs.append(out)
         if _stale(out, [*srcs, LIB, Path(__file__), *headers]):
-            _run([CXX, *CXX_FLAGS, *map(str, srcs), "-o", str(out), *link, rpath])
+            _run([CXX, *CXX_FLAGS, f"-I{QWEN3_API}", *map(str, srcs), "-o", str(out), *link, rpath])
     return outputs
 
 
