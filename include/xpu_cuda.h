@@ -211,6 +211,24 @@ typedef struct {
 int xpu_qwen3_create(const xpu_qwen3_shape *shape, uint32_t maximum_sequence, int device,
                      uint32_t tp_rank, uint32_t tp_size, xpu_qwen3_engine **out);
 int xpu_qwen3_destroy(xpu_qwen3_engine *engine);
+/* ------------------------------------------------------- checkpoints --
+ * Replace load_and_validate_config / load_and_validate_checkpoint
+ * (qwen3/model.cpp:376-495) for any Qwen3 shape with head_dim 128, tied or
+ * untied, sharded (model.safetensors.index.json) or single-file
+ * (model.safetensors). Checks: model_type qwen3, silu, bfloat16, no
+ * rope_scaling; BF16 tensors with exactly the shapes the config implies,
+ * every expected tensor and nothing else, payloads inside their shard and
+ * not overlapping, the index's total_size equal to the payload bytes.
+ *
+ * xpu_qwen3_read_config: <model_dir>/config.json -> *shape.
+ * xpu_qwen3_validate_checkpoint: config + every tensor header, no GPU needed;
+ *   *payload_bytes (optional) = total tensor bytes.
+ * xpu_qwen3_load_checkpoint: validates against the engine's shape and streams
+ *   this rank's part of every tensor to the GPU (pinned double buffering). */
+int xpu_qwen3_read_config(const char *model_dir, xpu_qwen3_shape *shape);
+int xpu_qwen3_validate_checkpoint(const char *model_dir, xpu_qwen3_shape *shape, uint64_t *payload_bytes);
+int xpu_qwen3_load_checkpoint(xpu_qwen3_engine *engine, const char *model_dir);
+
 /* Tensor-parallel rendezvous (tp_size > 1; ranks are processes, one GPU
  * each, on one NVLink/NVSwitch node). Each rank writes its exchange-region
  * handle (XPU_TP_HANDLE_BYTES bytes, a CUDA IPC handle) with

@@ -30,13 +30,16 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_generate(rank, world, port, preset, prompt, n_new, q):
+def _rank_generate(rank, world, port, preset, prompt, n_new, q, ckpt=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
     try:
         eng = Qwen3Engine(PRESETS[preset], MAX_SEQ, device=rank, tp_rank=rank, tp_size=world)
-        eng.init_synthetic(SEED)
+        if ckpt:
+            eng.load_checkpoint(ckpt)  # each rank streams its own shards from the files
+        else:
+            eng.init_synthetic(SEED)
         eng.connect_tensor_parallel()
         toks = eng.generate(prompt, n_new)
         q.put((rank, toks, eng.logits()))
@@ -49,11 +52,11 @@ def _rank_generate(rank, world, port, preset, prompt, n_new, q):
         dist.destroy_process_group()
 
 
-def _run_ranks(target, world, *args):
+def _run_ranks(target, world, *args, **kwargs):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=target, args=(r, world, port, *args, q)) for r in range(world)]
+    procs = [ctx.Process(target=target, args=(r, world, port, *args, q), kwargs=kwargs) for r in range(world)]
     for p in procs:
         p.start()
     try:
@@ -91,6 +94,26 @@ def test_tp_matches_single_gpu(preset, world):
         assert not isinstance(toks, str), toks
         assert toks == ref_toks, f"rank {rank} tokens differ from tp=1"
         assert np.array_equal(logits, ref_logits[rank * shard:(rank + 1) * shard]), f"rank {rank} logits differ"
+
+
+def test_tp_loads_checkpoint_shards(tmp_path):
+    """Each rank streams only its shards of a sharded safetensors checkpoint;
+    tp=2 then matches one GPU on the same weights."""
+    if NGPU < 2:
+        pytest.skip("needs 2 GPUs")
+    from oracle.qwen3_ref import seeded_weights
+    from tests._ckpt import write_checkpoint
+    shape = PRESETS["qwen3-0.6b"]
+    d = write_checkpoint(tmp_path / "m", shape, seeded_weights(shape, SEED), shards=2)
+    prompt = prompt_ids(16, shape.vocab, seed=6)
+    ref_toks, ref_logits = _single_gpu("qwen3-0.6b", prompt, 16)
+    results = _run_ranks(_rank_generate, 2, "qwen3-0.6b", prompt, 16, ckpt=str(d))
+    shard = shape.vocab // 2
+    for rank in range(2):
+        toks, logits = results[rank]
+        assert not isinstance(toks, str), toks
+        assert toks == ref_toks
+        assert np.array_equal(logits, ref_logits[rank * shard:(rank + 1) * shard])
 
 
 def _rank_absent_peer(rank, world, port, q):

@@ -36,6 +36,18 @@ class XpuError(RuntimeError):
 vp, sz = ctypes.c_void_p, ctypes.c_size_t
 u32, u64, i32, f32, f64 = ctypes.c_uint32, ctypes.c_uint64, ctypes.c_int, ctypes.c_float, ctypes.c_double
 
+class Qwen3ShapeC(ctypes.Structure):
+    """xpu_qwen3_shape."""
+    _fields_ = [("hidden_size", u32), ("intermediate_size", u32), ("num_hidden_layers", u32),
+                ("num_attention_heads", u32), ("num_key_value_heads", u32), ("vocab_size", u32),
+                ("tie_word_embeddings", u32), ("rms_norm_eps", f32), ("rope_theta", f64)]
+
+
+class Qwen3InfoC(ctypes.Structure):
+    """xpu_qwen3_info_t."""
+    _fields_ = [("weight_bytes", u64), ("kernels_per_step", u32), ("vocab_rows", u32),
+                ("vocab_offset", u32), ("stream", vp)]
+
 # name -> (restype, argtypes). Keep in step with include/xpu_cuda.h.
 SIGNATURES: dict[str, tuple] = {
     "xpu_last_error": (ctypes.c_char_p, []),
@@ -60,6 +72,9 @@ SIGNATURES: dict[str, tuple] = {
     "xpu_fill_normal_bf16": (i32, [vp, u64, u64, u64, f32, vp]),
     "xpu_qwen3_create": (i32, [vp, u32, i32, u32, u32, vp]),
     "xpu_qwen3_destroy": (i32, [vp]),
+    "xpu_qwen3_read_config": (i32, [ctypes.c_char_p, ctypes.POINTER(Qwen3ShapeC)]),
+    "xpu_qwen3_validate_checkpoint": (i32, [ctypes.c_char_p, ctypes.POINTER(Qwen3ShapeC), ctypes.POINTER(u64)]),
+    "xpu_qwen3_load_checkpoint": (i32, [vp, ctypes.c_char_p]),
     "xpu_qwen3_tp_handle": (i32, [vp, vp]),
     "xpu_qwen3_tp_connect": (i32, [vp, vp, u32]),
     "xpu_qwen3_init_synthetic": (i32, [vp, u64, f32]),
@@ -77,18 +92,6 @@ SIGNATURES: dict[str, tuple] = {
     "xpu_qwen3_bytes_per_token": (u64, [vp, u32]),
 }
 
-
-class Qwen3ShapeC(ctypes.Structure):
-    """xpu_qwen3_shape."""
-    _fields_ = [("hidden_size", u32), ("intermediate_size", u32), ("num_hidden_layers", u32),
-                ("num_attention_heads", u32), ("num_key_value_heads", u32), ("vocab_size", u32),
-                ("tie_word_embeddings", u32), ("rms_norm_eps", f32), ("rope_theta", f64)]
-
-
-class Qwen3InfoC(ctypes.Structure):
-    """xpu_qwen3_info_t."""
-    _fields_ = [("weight_bytes", u64), ("kernels_per_step", u32), ("vocab_rows", u32),
-                ("vocab_offset", u32), ("stream", vp)]
 
 _lib = None
 

@@ -215,6 +215,83 @@ class Qwen3Engine {
 
   void mark_loaded() { loaded_ = true; }
 
+  // Streams this rank's part of every tensor of a safetensors checkpoint
+  // directory (validated against the engine's shape) to the GPU: file reads
+  // into two pinned 64 MiB staging buffers alternate with their host->device
+  // copies, so reading and copying overlap.
+  void load_checkpoint(const std::string &dir) {
+    xpu_qwen3_shape cfg{};
+    read_qwen3_config(dir, &cfg, nullptr);
+    auto same = [&](const char *what, double a, double b) {
+      if (a != b)
+        throw InvalidArg(std::string("checkpoint config does not match the engine: ") + what + " is " +
+                         std::to_string(a) + ", engine has " + std::to_string(b));
+    };
+    same("hidden_size", cfg.hidden_size, shape_.hidden_size);
+    same("intermediate_size", cfg.intermediate_size, shape_.intermediate_size);
+    same("num_hidden_layers", cfg.num_hidden_layers, shape_.num_hidden_layers);
+    same("num_attention_heads", cfg.num_attention_heads, shape_.num_attention_heads);
+    same("num_key_value_heads", cfg.num_key_value_heads, shape_.num_key_value_heads);
+    same("vocab_size", cfg.vocab_size, shape_.vocab_size);
+    same("tie_word_embeddings", cfg.tie_word_embeddings, shape_.tie_word_embeddings);
+    same("rms_norm_eps", cfg.rms_norm_eps, shape_.rms_norm_eps);
+    same("rope_theta", cfg.rope_theta, shape_.rope_theta);
+    std::vector<CkptTensor> tensors;
+    try {
+      tensors = index_qwen3_checkpoint(dir, shape_);
+    } catch (const std::runtime_error &e) {
+      throw InvalidArg(e.what());
+    }
+    CK(cudaSetDevice(device_));
+    constexpr uint64_t kStaging = 64ull << 20;
+    struct Staging {
+      uint8_t *buf = nullptr;
+      cudaEvent_t done = nullptr;
+    } st[2];
+    auto release = [&] {
+      for (Staging &x : st) {
+        if (x.done) cudaEventSynchronize(x.done), cudaEventDestroy(x.done);
+        if (x.buf) cudaFreeHost(x.buf);
+      }
+    };
+    try {
+      for (Staging &x : st) {
+        CK(cudaMallocHost(&x.buf, kStaging));
+        CK(cudaEventCreateWithFlags(&x.done, cudaEventDisableTiming));
+        CK(cudaEventRecord(x.done, stream_));
+      }
+      int k = 0;
+      for (const CkptTensor &t : tensors) {
+        FileReader file(t.path);
+        for (const Placement &p : placements(t.name)) {
+          const uint64_t row_bytes = p.cols * 2;
+          const bool whole_rows = p.c0 == 0 && p.nc == p.cols && p.pitch == p.cols;
+          const uint64_t rows_per = std::max<uint64_t>(1, kStaging / row_bytes);
+          if (row_bytes > kStaging) throw InvalidArg("tensor row larger than the staging buffer: " + t.name);
+          for (uint64_t r = 0; r < p.nr; r += rows_per) {
+            const uint64_t rows = std::min(rows_per, p.nr - r);
+            Staging &x = st[k];
+            k ^= 1;
+            CK(cudaEventSynchronize(x.done));  // the buffer's previous copy has finished
+            file.read(x.buf, rows * row_bytes, t.offset + (p.r0 + r) * row_bytes);
+            if (whole_rows)
+              CK(cudaMemcpyAsync(p.dst + r * p.cols, x.buf, rows * row_bytes, cudaMemcpyHostToDevice, stream_));
+            else
+              CK(cudaMemcpy2DAsync(p.dst + r * p.pitch, p.pitch * 2, x.buf + p.c0 * 2, row_bytes, p.nc * 2, rows,
+                                   cudaMemcpyHostToDevice, stream_));
+            CK(cudaEventRecord(x.done, stream_));
+          }
+        }
+      }
+      CK(cudaStreamSynchronize(stream_));
+    } catch (...) {
+      release();
+      throw;
+    }
+    release();
+    loaded_ = true;
+  }
+
   // 0 = persistent single kernel per step (default), 1 = CUDA graph of
   // per-phase kernels. Both compute identical bits.
   void set_mode(int mode) {
@@ -726,6 +803,13 @@ int xpu_qwen3_tp_connect(xpu_qwen3_engine *engine, const void *handles, uint32_t
   return guarded([&] {
     if (!handles) throw xpu::InvalidArg("xpu_qwen3_tp_connect: null pointer");
     eng(engine).tp_connect(static_cast<const uint8_t *>(handles), count);
+  });
+}
+
+int xpu_qwen3_load_checkpoint(xpu_qwen3_engine *engine, const char *model_dir) {
+  return guarded([&] {
+    if (!model_dir) throw xpu::InvalidArg("xpu_qwen3_load_checkpoint: null pointer");
+    eng(engine).load_checkpoint(model_dir);
   });
 }
 

@@ -9,6 +9,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <vector>
 
 #include "../../include/xpu_cuda.h"
 
@@ -64,5 +65,34 @@ cudaError_t qwen_silu_multiply_launch(uint16_t *gate, const uint16_t *up, uint32
                                       cudaStream_t stream);
 cudaError_t qwen_argmax_launch(const uint16_t *values, uint32_t *token, uint32_t width,
                                cudaStream_t stream);
+
+// ---- Qwen3 checkpoints (loader.cpp) ----
+struct CkptTensor {
+  std::string name, path;       // tensor name, shard file
+  uint64_t offset = 0, bytes = 0;  // payload position in the file
+  std::vector<uint64_t> shape;
+};
+// Reads <dir>/config.json into a shape (throws std::runtime_error on anything
+// this engine cannot run).
+void read_qwen3_config(const std::string &dir, xpu_qwen3_shape *out, uint32_t *eos_token_id);
+// Every tensor the shape needs, located and validated in <dir>'s safetensors.
+std::vector<CkptTensor> index_qwen3_checkpoint(const std::string &dir, const xpu_qwen3_shape &shape);
+std::vector<std::string> qwen3_tensor_names(const xpu_qwen3_shape &s);
+std::vector<uint64_t> qwen3_tensor_shape(const xpu_qwen3_shape &s, const std::string &name);
+
+// Positional reads (pread) of one open file.
+class FileReader {
+ public:
+  explicit FileReader(const std::string &path);
+  ~FileReader();
+  FileReader(const FileReader &) = delete;
+  FileReader &operator=(const FileReader &) = delete;
+  uint64_t size() const;
+  void read(void *dst, uint64_t bytes, uint64_t offset) const;
+
+ private:
+  int fd_;
+  std::string path_;
+};
 
 }  // namespace xpu

@@ -35,6 +35,30 @@ def exchange_handles(handle: bytes, group=None) -> list[bytes]:
     return [bytes(h) for h in out]
 
 
+def _shape_from_c(c: _lib.Qwen3ShapeC) -> Qwen3Shape:
+    return Qwen3Shape(hidden=c.hidden_size, intermediate=c.intermediate_size, layers=c.num_hidden_layers,
+                      q_heads=c.num_attention_heads, kv_heads=c.num_key_value_heads, vocab=c.vocab_size,
+                      tied=bool(c.tie_word_embeddings),
+                      # the C field is float32: print it back at float32 precision (1e-06, not 9.99e-07)
+                      eps=float(f"{c.rms_norm_eps:.7g}"), rope_theta=c.rope_theta)
+
+
+def read_config(model_dir: str) -> Qwen3Shape:
+    """<model_dir>/config.json as a validated shape (xpu_qwen3_read_config)."""
+    c = _lib.Qwen3ShapeC()
+    _lib.check(_lib.load().xpu_qwen3_read_config(str(model_dir).encode(), ctypes.byref(c)))
+    return _shape_from_c(c)
+
+
+def validate_checkpoint(model_dir: str) -> tuple[Qwen3Shape, int]:
+    """Config and every tensor header of a safetensors checkpoint directory,
+    validated without a GPU; returns the shape and the payload bytes."""
+    c = _lib.Qwen3ShapeC()
+    n = ctypes.c_uint64()
+    _lib.check(_lib.load().xpu_qwen3_validate_checkpoint(str(model_dir).encode(), ctypes.byref(c), ctypes.byref(n)))
+    return _shape_from_c(c), n.value
+
+
 class Qwen3Engine:
     def __init__(self, shape: Qwen3Shape, max_seq: int, device: int = 0, tp_rank: int = 0,
                  tp_size: int = 1, mode: str | None = None):
@@ -71,6 +95,10 @@ class Qwen3Engine:
     def set_tensor(self, name: str, bits: np.ndarray) -> None:
         a = np.ascontiguousarray(bits, dtype=np.uint16)
         _lib.check(self.lib.xpu_qwen3_set_tensor(self._h, name.encode(), a.ctypes.data, a.size))
+
+    def load_checkpoint(self, model_dir: str) -> None:
+        """Streams (this rank's part of) a safetensors checkpoint directory."""
+        _lib.check(self.lib.xpu_qwen3_load_checkpoint(self._h, str(model_dir).encode()))
 
     def load_weights(self, weights: dict[str, np.ndarray]) -> None:
         for name, bits in weights.items():
