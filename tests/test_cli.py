@@ -61,3 +61,31 @@ def test_bench_library_exports_run_entries():
     argv = (ctypes.c_char_p * 3)(b"gemm", b"--size", b"0")
     lib.run_gemm.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_char_p)]
     assert lib.run_gemm(3, argv) == 1
+
+
+def test_qwen3_cli_arguments(tmp_path):
+    """qwen3/main.cpp:15-67 option rules, checked before any GPU work."""
+    q = BIN / "qwen3"
+    r = run(q, "--help")
+    assert r.returncode == 0 and r.stdout.startswith("Usage: qwen3 --model-dir DIR")
+    r = run(q, "--model-dir", str(tmp_path), "--input-ids", "-")
+    assert r.returncode == 1 and r.stderr.startswith("qwen3: --max-new-tokens is required")
+    r = run(q, "--model-dir", str(tmp_path), "--input-ids", "-", "--max-new-tokens", "x")
+    assert r.returncode == 1 and "invalid value for --max-new-tokens: x" in r.stderr
+    r = run(q, "--model-dir", str(tmp_path), "--input-ids", "-", "--max-new-tokens", "4", "--max-seq-len", "50000")
+    assert r.returncode == 1 and "--max-seq-len cannot exceed 40960" in r.stderr
+    r = run(q, "--model-dir", str(tmp_path), "--input-ids", "-", "--max-new-tokens", "4")
+    assert r.returncode == 1 and "config.json" in r.stderr  # no checkpoint there
+
+
+def test_qwen3_cli_rejects_bad_token_ids(tmp_path):
+    import json
+    from tests._ckpt import config_dict
+    from xpu_playground_b200.qwen3_config import PRESETS
+    (tmp_path / "config.json").write_text(json.dumps(config_dict(PRESETS["tiny"])))
+    ids = tmp_path / "ids.txt"
+    for text, needle in (("1 2 4096", "outside [0, 4095]: 4096"), ("1 x", "invalid input token ID: x"),
+                         ("", "at least one input token ID is required")):
+        ids.write_text(text)
+        r = run(BIN / "qwen3", "--model-dir", str(tmp_path), "--input-ids", str(ids), "--max-new-tokens", "2")
+        assert r.returncode == 1 and needle in r.stderr, r.stderr

@@ -33,3 +33,22 @@ def test_load_rejects_a_checkpoint_of_another_shape(tmp_path):
     with Qwen3Engine(PRESETS["tiny-tied"], 16) as e:
         with pytest.raises(XpuError, match="checkpoint config does not match the engine"):
             e.load_checkpoint(d)
+
+
+def test_qwen3_cli_generates_like_the_engine(tmp_path):
+    """The qwen3 program (reference main.cpp's flags and JSON output) on a
+    checkpoint directory gives the engine's greedy tokens."""
+    import json
+    import subprocess
+    from xpu_playground_b200 import build
+    shape = PRESETS["tiny-tied"]
+    d = write_checkpoint(tmp_path / "m", shape, seeded_weights(shape, 5), shards=2)
+    prompt = prompt_ids(12, shape.vocab, seed=9)
+    (tmp_path / "ids.txt").write_text(" ".join(map(str, prompt)) + "\n")
+    r = subprocess.run([str(build.BIN_DIR / "qwen3"), "--model-dir", str(d), "--input-ids", str(tmp_path / "ids.txt"),
+                        "--max-new-tokens", "20", "--max-seq-len", "64"], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    out = json.loads(r.stdout)
+    with Qwen3Engine(shape, 64) as e:
+        e.load_checkpoint(d)
+        assert out["generated_ids"] == e.generate(prompt, 20, stop_at_eos=True)

@@ -56,6 +56,7 @@ BENCH_PROGRAMS: dict[str, str] = {
 # Other C++ host programs: name -> sources under host/ (all link libxpu_cuda.so).
 HOST_PROGRAMS: dict[str, list[str]] = {
     "peak_sycl": ["peak_sycl.cpp"],
+    "qwen3": ["qwen3_cli.cpp"],
     "runtime_selftest": ["qwen3/runtime_selftest.cpp", "qwen3/level_zero_runtime_cuda.cpp"],
 }
 # The reference's Qwen3 kernel runtime API on CUDA (class qwen3::LevelZeroRuntime,
