@@ -9,6 +9,11 @@ and runs `--warm` + 1 decode steps, so that the step to capture under
 `ncu -k regex:k_step -s <warm> -c 1` is the last one. Weight initialisation
 launches one fill kernel per tensor before that.
 
+Under torchrun the ranks run one tensor-parallel engine and rank 0 reports:
+
+    python -m torch.distributed.run --nproc-per-node 8 --master-addr 127.0.0.1 \
+        -m xpu_playground_b200.profile_step --preset qwen3-8b --trace
+
 --trace re-runs with XPU_STEP_TRACE=1 and prints, per phase of the persistent
 step, the mean/max over CTAs of the time spent staging the activation,
 streaming its items, finishing (arrivals and epilogues) and in the grid
@@ -43,15 +48,37 @@ def main() -> None:
     from .qwen3_config import PRESETS
 
     shape = PRESETS[args.preset]
-    eng = Qwen3Engine(shape, args.context + args.warm + 8, mode=args.mode)
+    # Under torchrun (WORLD_SIZE > 1) the ranks run one tensor-parallel
+    # engine (one GPU each) and rank 0 reports.
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    eng = Qwen3Engine(shape, args.context + args.warm + 8, device=local, tp_rank=rank, tp_size=world,
+                      mode=args.mode if world == 1 else "persistent")
     eng.init_synthetic(1)
+    if world > 1:
+        eng.connect_tensor_parallel()
     eng.set_state(5, args.context)
     eng.enqueue_steps(args.warm + 1)
     eng.synchronize()
     tok, pos, err = eng.state()
-    print(f"{args.preset}: position {pos}, last token {tok}, error {err}, "
+    if world > 1:
+        dist.barrier()
+        if rank != 0:
+            dist.barrier()
+            eng.close()
+            dist.destroy_process_group()
+            return
+    print(f"{args.preset}: position {pos}, last token {tok}, error {err}, tp {world}, "
           f"kernels/step {eng.info().kernels_per_step}, fill launches {len(shape.tensor_names())}")
     if not args.trace:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
         return
     n = ctypes.c_uint32()
     _lib.check(eng.lib.xpu_qwen3_trace(eng._h, None, 0, ctypes.byref(n)))
@@ -72,6 +99,10 @@ def main() -> None:
         print(f"{PHASES[ph]:8s} " + "  ".join(cells))
     lm = t[:, -1] - t[:, -3]
     print(f"lm_head  total {lm.mean() / 1e3:.1f}/{lm.max() / 1e3:.1f} us (mean/max over CTAs)")
+    if world > 1:
+        dist.barrier()
+        eng.close()
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":
