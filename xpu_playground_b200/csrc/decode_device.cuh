@@ -111,15 +111,19 @@ __device__ inline bool arrive_one(unsigned *counter, unsigned total, int *flag) 
 
 __device__ __forceinline__ void flag_error(DecodeState *st, uint32_t bits) { atomicOr(&st->error, bits); }
 
-// System-scope release store / acquire load (cross-GPU exchange flags).
-__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+// Cross-GPU exchange flags: published with relaxed system-scope stores after
+// one system-scope fence, polled with relaxed system-scope loads and followed
+// by one acquire fence (a release/acquire pattern per flag without a fence in
+// every store and every poll).
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long *p) {
   unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 // Waits (bounded) until every rank's flag in this rank's region reaches
 // epoch; false on a timeout (error bit 4 set) or when another waiter failed.
@@ -127,7 +131,7 @@ __device__ inline bool wait_rank_flags(const DecodeDims &d, const DecodeBuffers 
   const unsigned long long *own = b.tp.flag[d.tp_rank];
   const long long start = clock64();
   for (uint32_t q = 0; q < d.tp_size; ++q) {
-    while (ld_acquire_sys(own + q) < epoch) {
+    while (ld_relaxed_sys(own + q) < epoch) {
       if (*reinterpret_cast<volatile uint32_t *>(&b.state->error) & kErrPipelineTimeout) return false;
       if (clock64() - start > kWaitCycles) {
         flag_error(b.state, kErrPipelineTimeout);
@@ -135,6 +139,7 @@ __device__ inline bool wait_rank_flags(const DecodeDims &d, const DecodeBuffers 
       }
     }
   }
+  fence_acq_rel_sys();
   return true;
 }
 
@@ -416,14 +421,15 @@ __device__ inline bool lm_items_and_argmax(const DecodeDims &d, const DecodeBuff
           slot->bad = fbad;
         }
         __threadfence_system();
-        for (uint32_t q = 0; q < d.tp_size; ++q) st_release_sys(&(b.tp.lm[q] + d.tp_rank)->epoch, lm_epoch);
+        for (uint32_t q = 0; q < d.tp_size; ++q) st_relaxed_sys(&(b.tp.lm[q] + d.tp_rank)->epoch, lm_epoch);
         const LmSlot *own = b.tp.lm[d.tp_rank];
         bool ok = true;
         const long long start = clock64();
         for (uint32_t q = 0; ok && q < d.tp_size; ++q)
-          while (ld_acquire_sys(&own[q].epoch) < lm_epoch) {
+          while (ld_relaxed_sys(&own[q].epoch) < lm_epoch) {
             if (clock64() - start > kWaitCycles) { ok = false; break; }
           }
+        fence_acq_rel_sys();
         if (!ok) {
           flag_error(st, kErrPipelineTimeout);
         } else {

@@ -84,10 +84,13 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
+// The consumer barrier orders every consumer thread's earlier writes before
+// the arriving thread, whose fence is cumulative over them: one fence per CTA
+// instead of one per thread.
 __device__ bool grid_barrier(unsigned long long *counter, unsigned long long target, DecodeState *st, int *flag) {
-  __threadfence();
   consumer_sync();
   if (ctid() == 0) {
+    __threadfence();
     atomicAdd(counter, 1ull);
     bool ok = false;
     const long long start = clock64();
@@ -109,13 +112,13 @@ __device__ bool grid_barrier(unsigned long long *counter, unsigned long long tar
 // every CTA then waits until all ranks' flags reach epoch, which makes every
 // rank's remote stores issued before the barrier visible here.
 __device__ bool tp_barrier(const StepParams &p, unsigned long long target, unsigned long long epoch, int *flag) {
-  __threadfence_system();
   consumer_sync();
   if (ctid() == 0) {
+    __threadfence_system();  // cumulative over the CTA's peer stores (ordered by the consumer barrier)
     const unsigned long long old = atomicAdd(p.bar, 1ull);
     if (old + 1 == target) {
       __threadfence_system();
-      for (uint32_t q = 0; q < p.d.tp_size; ++q) st_release_sys(p.b.tp.flag[q] + p.d.tp_rank, epoch);
+      for (uint32_t q = 0; q < p.d.tp_size; ++q) st_relaxed_sys(p.b.tp.flag[q] + p.d.tp_rank, epoch);
     }
     *flag = wait_rank_flags(p.d, p.b, epoch);
   }
