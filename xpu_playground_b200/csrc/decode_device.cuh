@@ -164,42 +164,66 @@ __device__ inline bool qkv_items(const DecodeDims &d, const DecodeBuffers &b, co
 // l, l+32, l+64, l+96, so both rotate-half pairs sit in one lane): sum the
 // splits, then q/k RMSNorm + RoPE (transformers rounding) into the q buffer /
 // key cache, or v into the value cache, at `pos`.
+constexpr uint32_t kMaxQkvSplits = 8;  // split partials held in registers by the head epilogue
+
 __device__ inline void qkv_head_warp(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w,
                                      uint32_t head, uint32_t pos) {
   const uint32_t lane = lane_id();
   const uint32_t rows_total = (d.QH_l + 2 * d.KVH_l) * kHD;
+  const bool is_v = head >= d.QH_l + d.KVH_l, is_q = head < d.QH_l;
+  // Every input of the epilogue is loaded before any is used (one memory
+  // round trip): the split partials, and for q/k the norm weight and the
+  // RoPE table entries of this lane's four dimensions l + 32 j.
+  float part[kMaxQkvSplits][4];
+  const uint32_t splits = d.qkv_splits < kMaxQkvSplits ? d.qkv_splits : kMaxQkvSplits;
+#pragma unroll
+  for (uint32_t s = 0; s < kMaxQkvSplits; ++s)
+    if (s < splits)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        part[s][j] = __ldcg(b.part_qkv + static_cast<size_t>(s) * rows_total + head * kHD + lane + 32 * j);
+  float nwv[4] = {0.f, 0.f, 0.f, 0.f}, cv[4] = {0.f, 0.f, 0.f, 0.f}, sv[4] = {0.f, 0.f, 0.f, 0.f};
+  if (!is_v) {
+    const bf16 *nw = is_q ? w.q_norm : w.k_norm;
+    const bf16 *cr = b.cos_t + static_cast<size_t>(pos) * kHD, *sr = b.sin_t + static_cast<size_t>(pos) * kHD;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      nwv[j] = bf(nw, lane + 32 * j);
+      cv[j] = bf(cr, lane + 32 * j);
+      sv[j] = bf(sr, lane + 32 * j);
+    }
+  }
   float v[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     float y = 0.f;
-    for (uint32_t s = 0; s < d.qkv_splits; ++s)
+#pragma unroll
+    for (uint32_t s = 0; s < kMaxQkvSplits; ++s)
+      if (s < splits) y += part[s][j];
+    for (uint32_t s = kMaxQkvSplits; s < d.qkv_splits; ++s)
       y += __ldcg(b.part_qkv + static_cast<size_t>(s) * rows_total + head * kHD + lane + 32 * j);
     v[j] = round_bf16(y);
   }
-  if (head >= d.QH_l + d.KVH_l) {  // value head: straight into the cache
+  if (is_v) {  // value head: straight into the cache
     const size_t slot = (static_cast<size_t>(pos) * d.KVH_l + (head - d.QH_l - d.KVH_l)) * kHD;
 #pragma unroll
     for (int j = 0; j < 4; ++j) put(w.vcache, slot + lane + 32 * j, v[j]);
     return;
   }
-  const bool is_q = head < d.QH_l;
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < 4; ++j) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
   ss = warp_sum(ss);
   const float r = 1.0f / sqrtf(ss / static_cast<float>(kHD) + d.eps);
-  const bf16 *nw = is_q ? w.q_norm : w.k_norm;
   float nv[4];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) nv[j] = round_bf16(__fmul_rn(bf(nw, lane + 32 * j), round_bf16(__fmul_rn(v[j], r))));
-  const bf16 *cr = b.cos_t + static_cast<size_t>(pos) * kHD, *sr = b.sin_t + static_cast<size_t>(pos) * kHD;
+  for (int j = 0; j < 4; ++j) nv[j] = round_bf16(__fmul_rn(nwv[j], round_bf16(__fmul_rn(v[j], r))));
   float out[4];
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const uint32_t i = lane + 32 * j;  // pairs (i, i + 64): rotate_half
+  for (int j = 0; j < 2; ++j) {  // pairs (i, i + 64): rotate_half
     const float a = nv[j], c = nv[j + 2];
-    out[j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(a, bf(cr, i))), round_bf16(__fmul_rn(-c, bf(sr, i)))));
-    out[j + 2] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(c, bf(cr, i + 64))), round_bf16(__fmul_rn(a, bf(sr, i + 64)))));
+    out[j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(a, cv[j])), round_bf16(__fmul_rn(-c, sv[j]))));
+    out[j + 2] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(c, cv[j + 2])), round_bf16(__fmul_rn(a, sv[j + 2]))));
   }
   bf16 *dst = is_q ? b.q + static_cast<size_t>(head) * kHD
                    : w.kcache + (static_cast<size_t>(pos) * d.KVH_l + (head - d.QH_l)) * kHD;
@@ -208,6 +232,21 @@ __device__ inline void qkv_head_warp(const DecodeDims &d, const DecodeBuffers &b
 }
 
 // Deferred arrivals of this CTA's QKV items; every head it completed is
+// Persistent step: the head epilogues of one attention item's kv group, run
+// by the item's CTA itself (so no separate finishing phase): the group's q
+// heads, and for the item holding the newest position also its k and v
+// heads (into the cache at pos). Every CTA of the group computes the same q
+// bits, so their duplicate stores to b.q are harmless.
+__device__ inline void attn_group_heads(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w,
+                                        uint32_t kvh, bool newest, uint32_t pos) {
+  const uint32_t G = d.QH_l / d.KVH_l, n = G + (newest ? 2 : 0);
+  for (uint32_t h = cwarp(); h < n; h += kConsumerWarps) {
+    const uint32_t head = h < G ? kvh * G + h : (h == G ? d.QH_l + kvh : d.QH_l + d.KVH_l + kvh);
+    qkv_head_warp(d, b, w, head, pos);
+  }
+  consumer_sync();
+}
+
 // finished by one warp (heads spread over the 8 consumer warps).
 __device__ inline void qkv_finish(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w,
                                   const StreamGeom &g, uint32_t pos, uint8_t *s_last) {

@@ -194,13 +194,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constan
     stamp();
     if (!qkv_items(d, b, sm, p.g.qkv, it)) { flag_error(st, kErrPipelineTimeout); return; }
     stamp();
-    qkv_finish(d, b, w, p.g.qkv, pos, s_last);
-    stamp();
+    stamp();  // (no finishing phase: each attention item finishes its group's heads)
     if (!barrier()) return;
     stamp();
     stamp();
-    for (uint32_t item = blockIdx.x; item < attn_items; item += gridDim.x)
+    for (uint32_t item = blockIdx.x; item < attn_items; item += gridDim.x) {
+      attn_group_heads(d, b, w, item / nch, item % nch == nch - 1, pos);
       scores_item<G>(d, b, w, item / nch, item % nch, npc, n, as);
+    }
     stamp();
     stamp();
     if (!barrier()) return;
