@@ -513,16 +513,31 @@ struct AttnShared {
 // s = bf16(bf16(q.k) * scale) for the chunk's positions; chunk max and sum of
 // exp(s - max) into stats.
 template <int G>
+// finish_heads (persistent step): the item also runs its group's head
+// epilogues (attn_group_heads) - after issuing the loads of every cached K
+// row except the newest, whose row the epilogue writes, so the two memory
+// round trips overlap.
 __device__ inline void scores_item(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w, uint32_t kvh,
-                                   uint32_t chunk, uint32_t nchunks, uint32_t n, AttnShared<G> &as) {
+                                   uint32_t chunk, uint32_t nchunks, uint32_t n, AttnShared<G> &as,
+                                   bool finish_heads = false) {
   const uint32_t lane = lane_id(), cw = cwarp();
   const uint32_t p0 = chunk * kPosChunk, p1 = min(p0 + kPosChunk, n);
   const uint32_t pw = p0 + cw * kPosPerWarp;
+  const uint32_t newest = n - 1;
   uint2 kr[kPosPerWarp];
 #pragma unroll
   for (uint32_t i = 0; i < kPosPerWarp; ++i) {
     const uint32_t p = pw + i;
-    kr[i] = p < p1 ? ldcg8(w.kcache + (static_cast<size_t>(p) * d.KVH_l + kvh) * kHD + lane * 4) : make_uint2(0, 0);
+    kr[i] = p < p1 && !(finish_heads && p == newest)
+                ? ldcg8(w.kcache + (static_cast<size_t>(p) * d.KVH_l + kvh) * kHD + lane * 4)
+                : make_uint2(0, 0);
+  }
+  if (finish_heads) {
+    attn_group_heads(d, b, w, kvh, chunk == newest / kPosChunk, newest);
+    if (newest >= pw && newest < pw + kPosPerWarp)
+#pragma unroll
+      for (uint32_t i = 0; i < kPosPerWarp; ++i)
+        if (pw + i == newest) kr[i] = ldcg8(w.kcache + (static_cast<size_t>(newest) * d.KVH_l + kvh) * kHD + lane * 4);
   }
   float q[G][4];
 #pragma unroll

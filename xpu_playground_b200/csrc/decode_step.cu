@@ -198,10 +198,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constan
     if (!barrier()) return;
     stamp();
     stamp();
-    for (uint32_t item = blockIdx.x; item < attn_items; item += gridDim.x) {
-      attn_group_heads(d, b, w, item / nch, item % nch == nch - 1, pos);
-      scores_item<G>(d, b, w, item / nch, item % nch, npc, n, as);
-    }
+    for (uint32_t item = blockIdx.x; item < attn_items; item += gridDim.x)
+      scores_item<G>(d, b, w, item / nch, item % nch, npc, n, as, true);
     stamp();
     stamp();
     if (!barrier()) return;
