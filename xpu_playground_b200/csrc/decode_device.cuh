@@ -164,7 +164,7 @@ __device__ inline bool qkv_items(const DecodeDims &d, const DecodeBuffers &b, co
 // l, l+32, l+64, l+96, so both rotate-half pairs sit in one lane): sum the
 // splits, then q/k RMSNorm + RoPE (transformers rounding) into the q buffer /
 // key cache, or v into the value cache, at `pos`.
-constexpr uint32_t kMaxQkvSplits = 8;  // split partials held in registers by the head epilogue
+constexpr uint32_t kMaxQkvSplits = 4;  // split partials held in registers by the head epilogue
 
 __device__ inline void qkv_head_warp(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w,
                                      uint32_t head, uint32_t pos) {
@@ -592,23 +592,37 @@ __device__ inline void pv_item(const DecodeDims &d, const DecodeBuffers &b, cons
     const uint32_t p = pw + i;
     vr[i] = p < p1 ? ldcg8(w.vcache + (static_cast<size_t>(p) * d.KVH_l + kvh) * kHD + lane * 4) : make_uint2(0, 0);
   }
+  // This thread's scores of the chunk, loaded now with the V rows (they do
+  // not depend on the softmax statistics).
+  constexpr uint32_t kScPerThread = (G * kPosChunk + kConsumerThreads - 1) / kConsumerThreads;
+  float sreg[kScPerThread];
+#pragma unroll
+  for (uint32_t k = 0; k < kScPerThread; ++k) {
+    const uint32_t i = t + k * kConsumerThreads, g = i / kPosChunk, p = p0 + i % kPosChunk;
+    sreg[k] = (i < G * kPosChunk && p < p1) ? __ldcg(b.scores + static_cast<size_t>(kvh * G + g) * d.max_seq + p) : 0.f;
+  }
   for (uint32_t g = cw; g < static_cast<uint32_t>(G); g += kConsumerWarps) {
     const float *st = b.stats + static_cast<size_t>(kvh * G + g) * nchunks * 2;
-    float m = -INFINITY;
-    for (uint32_t c = lane; c < nch; c += 32) m = fmaxf(m, __ldcg(st + 2 * c));
+    // this lane's first chunk statistics, read once (up to 32 chunks, 4096
+    // positions, without a second read)
+    const float cm = lane < nch ? __ldcg(st + 2 * lane) : -INFINITY;
+    const float cl = lane < nch ? __ldcg(st + 2 * lane + 1) : 0.f;
+    float m = cm;
+    for (uint32_t c = lane + 32; c < nch; c += 32) m = fmaxf(m, __ldcg(st + 2 * c));
     m = warp_max(m);
-    float sum = 0.f;
-    for (uint32_t c = lane; c < nch; c += 32) sum += __ldcg(st + 2 * c + 1) * expf(__ldcg(st + 2 * c) - m);
+    float sum = lane < nch ? cl * expf(cm - m) : 0.f;
+    for (uint32_t c = lane + 32; c < nch; c += 32) sum += __ldcg(st + 2 * c + 1) * expf(__ldcg(st + 2 * c) - m);
     sum = warp_sum(sum);
     if (lane == 0) { as.sM[g] = m; as.sInv[g] = 1.0f / sum; }
   }
   consumer_sync();
-  for (uint32_t i = t; i < G * kPosChunk; i += kConsumerThreads) {
-    const uint32_t g = i / kPosChunk, j = i % kPosChunk, p = p0 + j;
-    as.sc[g][j] = p < p1 ? round_bf16(__fmul_rn(
-                               expf(__ldcg(b.scores + static_cast<size_t>(kvh * G + g) * d.max_seq + p) - as.sM[g]),
-                               as.sInv[g]))
-                         : 0.f;
+#pragma unroll
+  for (uint32_t k = 0; k < kScPerThread; ++k) {
+    const uint32_t i = t + k * kConsumerThreads;
+    if (i < G * kPosChunk) {
+      const uint32_t g = i / kPosChunk, j = i % kPosChunk;
+      as.sc[g][j] = p0 + j < p1 ? round_bf16(__fmul_rn(expf(sreg[k] - as.sM[g]), as.sInv[g])) : 0.f;
+    }
   }
   consumer_sync();
   float acc[G][4];
