@@ -581,7 +581,8 @@ __device__ inline void scores_item(const DecodeDims &d, const DecodeBuffers &b, 
 // chunks into the attention output.
 template <int G>
 __device__ inline void pv_item(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w, uint32_t kvh,
-                               uint32_t chunk, uint32_t nchunks, uint32_t n, AttnShared<G> &as) {
+                               uint32_t chunk, uint32_t nchunks, uint32_t n, AttnShared<G> &as,
+                               bool defer_combine = false) {
   const uint32_t lane = lane_id(), cw = cwarp(), t = ctid();
   const uint32_t nch = (n + kPosChunk - 1) / kPosChunk;
   const uint32_t p0 = chunk * kPosChunk, p1 = min(p0 + kPosChunk, n);
@@ -652,6 +653,10 @@ __device__ inline void pv_item(const DecodeDims &d, const DecodeBuffers &b, cons
     for (uint32_t ww = 0; ww < static_cast<uint32_t>(kConsumerWarps); ++ww) tot += as.sacc[ww][g][dd];
     b.attn_part[(static_cast<size_t>(kvh * G + g) * nchunks + chunk) * kHD + dd] = tot;
   }
+  if (defer_combine) {  // persistent step: the o_proj staging combines the chunks (stage_attn_parts)
+    consumer_sync();
+    return;
+  }
   if (arrive_one(b.cnt_attn + kvh, nch, &as.flag)) {
     for (uint32_t e = t; e < G * kHD; e += kConsumerThreads) {
       const uint32_t g = e / kHD, dd = e % kHD;
@@ -661,6 +666,43 @@ __device__ inline void pv_item(const DecodeDims &d, const DecodeBuffers &b, cons
       put(b.attn, static_cast<size_t>(kvh * G + g) * kHD + dd, o);
     }
     if (t == 0) b.cnt_attn[kvh] = 0;
+  }
+  consumer_sync();
+}
+
+// Persistent step, o_proj input: for each K part that this CTA's o_proj
+// items use, the attention output of those dimensions, combined here from
+// the position-chunk partials (chunks in order, then bf16: the arithmetic of
+// pv_item's combine) and staged into xs at the part's offset.
+__device__ inline void stage_attn_parts(const DecodeDims &d, const DecodeBuffers &b, const StreamGeom &g,
+                                        uint32_t nchunks, uint32_t n, uint4 *xs) {
+  constexpr uint32_t kHeld = 24;  // chunk partials loaded before the in-order sum (3072 positions)
+  const uint32_t nch = (n + kPosChunk - 1) / kPosChunk;
+  uint32_t list[8], nparts = 0;
+  uint32_t seen = 0;
+  for (uint32_t item = blockIdx.x; item < g.items(); item += gridDim.x) {
+    const uint32_t part = item % g.kparts;
+    if (!((seen >> part) & 1u) && nparts < 8) { seen |= 1u << part; list[nparts++] = part; }
+  }
+  const uint32_t quads = g.kt / 4;  // 4 dimensions per thread and pass
+  for (uint32_t q = ctid(); q < nparts * quads; q += kConsumerThreads) {
+    const uint32_t e0 = list[q / quads] * g.kt + 4 * (q % quads);
+    const uint32_t h = e0 / kHD, dd = e0 % kHD;
+    const float *src = b.attn_part + static_cast<size_t>(h) * nchunks * kHD + dd;
+    float4 v[kHeld];
+#pragma unroll
+    for (uint32_t c = 0; c < kHeld; ++c)
+      v[c] = c < nch ? __ldcg(reinterpret_cast<const float4 *>(src + static_cast<size_t>(c) * kHD))
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+#pragma unroll
+    for (uint32_t c = 0; c < kHeld; ++c)
+      if (c < nch) { o0 += v[c].x; o1 += v[c].y; o2 += v[c].z; o3 += v[c].w; }
+    for (uint32_t c = kHeld; c < nch; ++c) {
+      const float4 x = __ldcg(reinterpret_cast<const float4 *>(src + static_cast<size_t>(c) * kHD));
+      o0 += x.x; o1 += x.y; o2 += x.z; o3 += x.w;
+    }
+    reinterpret_cast<uint2 *>(xs)[e0 / 4] = make_uint2(pack_bf16x2(o0, o1), pack_bf16x2(o2, o3));
   }
   consumer_sync();
 }

@@ -206,12 +206,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constan
     stamp();
     stamp();
     for (uint32_t item = blockIdx.x; item < attn_items; item += gridDim.x)
-      pv_item<G>(d, b, w, item / nch, item % nch, npc, n, as);
+      pv_item<G>(d, b, w, item / nch, item % nch, npc, n, as, true);
     stamp();
     stamp();
     if (!barrier()) return;
     stamp();
-    stage_copy(b.attn, d.QH_l * kHD, sm.xs);
+    stage_attn_parts(d, b, p.g.o, npc, n, sm.xs);
     stamp();
     if (tp) {
       if (!rowpar_items_tp(d, b, sm, p.g.o, it, 0)) { flag_error(st, kErrPipelineTimeout); return; }
