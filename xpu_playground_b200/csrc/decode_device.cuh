@@ -87,26 +87,30 @@ __device__ inline uint32_t arrive_items(unsigned *counters, uint32_t items, uint
                                         uint8_t *s_last) {
   const uint32_t mine = items > blockIdx.x ? (items - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
   const uint32_t n = mine < kMaxLocalItems ? mine : kMaxLocalItems;
-  __threadfence();
+  // The consumer barrier orders every consumer's stores before the arriving
+  // threads, whose fences (release before, acquire after the atomic) are
+  // cumulative over them; the second barrier hands the acquire to everyone.
   consumer_sync();
   for (uint32_t j = ctid(); j < n; j += kConsumerThreads) {
     const uint32_t item = blockIdx.x + j * gridDim.x;
+    __threadfence();
     s_last[j] = atomicAdd(counters + item / per_counter, 1u) == total - 1u;
+    __threadfence();
   }
   consumer_sync();
-  __threadfence();
   return n;
 }
 
 // Whole-CTA (consumer warps) publish-then-count on one counter.
 __device__ inline bool arrive_one(unsigned *counter, unsigned total, int *flag) {
-  __threadfence();
+  consumer_sync();  // as arrive_items: one arriving thread fences for the CTA
+  if (ctid() == 0) {
+    __threadfence();
+    *flag = (atomicAdd(counter, 1u) == total - 1u);
+    __threadfence();
+  }
   consumer_sync();
-  if (ctid() == 0) *flag = (atomicAdd(counter, 1u) == total - 1u);
-  consumer_sync();
-  const bool last = *flag != 0;
-  if (last) __threadfence();
-  return last;
+  return *flag != 0;
 }
 
 __device__ __forceinline__ void flag_error(DecodeState *st, uint32_t bits) { atomicOr(&st->error, bits); }
@@ -358,9 +362,14 @@ __device__ inline void rowpar_finish(const DecodeDims &d, const DecodeBuffers &b
     if (j < n && s_last[j]) {
       const uint32_t tile = (blockIdx.x + j * gridDim.x) / g.kparts;
       const uint32_t r = tile * kStageRows + t % kStageRows;
+      float v[kCanonChunks];  // every chunk's partial in flight before the in-order sum
+#pragma unroll
+      for (uint32_t c = 0; c < kCanonChunks; ++c) v[c] = __ldcg(b.part + static_cast<size_t>(c) * d.H + r);
+      const float xr = bfcg(b.x, r);
       float y = 0.f;
-      for (uint32_t c = 0; c < kCanonChunks; ++c) y += __ldcg(b.part + static_cast<size_t>(c) * d.H + r);
-      put(b.x, r, __fadd_rn(bfcg(b.x, r), round_bf16(y)));
+#pragma unroll
+      for (uint32_t c = 0; c < kCanonChunks; ++c) y += v[c];
+      put(b.x, r, __fadd_rn(xr, round_bf16(y)));
       if (t % kStageRows == 0) b.cnt_tile[tile] = 0;
     }
   }
