@@ -69,6 +69,8 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemv", action="store_true")
+    ap.add_argument("--batch", type=int, default=16,
+                    help="sequences of the batched-decode measurement in extra (0: skip)")
     return ap.parse_args()
 
 
@@ -234,6 +236,49 @@ def gemm_extra(torch, device, peak_tflops: float) -> dict:
     return out
 
 
+def batch_extra(torch, device, shape, context: int, batch: int, steps: int, warmup: int) -> dict:
+    """Batched decode (BASELINE configs[4] at batch 16): `batch` sequences,
+    each after its own seeded `context`-token prompt (prefilled by batched
+    steps), timed over `steps` device-resident batched steps with CUDA
+    events; roofline = weights once + every sequence's K/V per step."""
+    from xpu_playground_b200.qwen3 import Qwen3Engine
+
+    max_seq = context + warmup + steps + 8
+    eng = Qwen3Engine(shape, max_seq, device=device.index or 0, max_batch=batch)
+    eng.init_synthetic(2026)
+    prompts = [seeded_prompt(context, shape.vocab, seed=7 + s) for s in range(batch)]
+    eng.batch_generate(prompts, 1)  # prefill: context batched steps
+    stream = torch.cuda.ExternalStream(eng.info().stream, device=device)
+    eng.batch_enqueue_steps(warmup)
+    eng.synchronize()
+    _, pos0, err = eng.batch_state(batch)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    eng.batch_enqueue_steps(steps)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    _, pos1, err = eng.batch_state(batch)
+    if err:
+        raise SystemExit(f"batched decode error word {err}")
+    mid = (pos0[0] + pos1[0]) // 2
+    nbytes = eng.batch_bytes_per_step(batch, mid)
+    peak, kind = measured_peaks()
+    out = {
+        "workload": f"{shape.layers}-layer {shape.hidden}-hidden greedy decode, batch {batch}, "
+                    f"{context}-token prompt per sequence",
+        "value": round(batch * 1000.0 / ms, 1), "unit": "tok/s", "ms_per_step": round(ms, 4),
+        "steps": steps, "context_tokens": [pos0[0], pos1[0]],
+        "kernels_per_step": eng.batch_kernels_per_step(),
+        "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": nbytes,
+                     "achieved": round(nbytes / (ms * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4),
+                     "peak_source": f"{kind} HBM copy bandwidth"},
+    }
+    eng.close()
+    return out
+
+
 def measured_tflops() -> float:
     try:
         return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
@@ -312,6 +357,10 @@ def run_ours(args) -> None:
     peak, peak_kind = measured_peaks()
 
     extra = {}
+    if args.batch and world == 1:
+        eng.synchronize()
+        extra["batch_decode"] = batch_extra(torch, device, shape, args.context, args.batch,
+                                            steps=min(K, 64), warmup=max(W, 3))
     if not args.no_gemv:
         eng.synchronize()
         extra.update(gemv_extra(torch, device, rank, world))

@@ -285,6 +285,44 @@ int xpu_qwen3_info(xpu_qwen3_engine *engine, xpu_qwen3_info_t *info);
  * every weight streamed once (one embedding row) plus K/V reads. */
 uint64_t xpu_qwen3_bytes_per_token(xpu_qwen3_engine *engine, uint32_t context);
 
+/* ------------------------------------------------------ batched decode --
+ * Up to XPU_MAX_BATCH sequences per step on one GPU (the reference decodes
+ * one sequence per Engine; qwen3/main.cpp:159-226 per sequence). Each step
+ * streams the weights once for every sequence (tcgen05 GEMMs with N = 16);
+ * norms, RoPE, the KV cache, attention and argmax are per sequence with the
+ * batch-1 arithmetic. xpu_qwen3_create_batched makes a single-GPU engine
+ * whose KV cache holds max_batch sequences (sequence 0 is the one the
+ * batch-1 calls above use); every engine accepts batch 1.
+ *
+ * xpu_qwen3_batch_decode: one synchronous step of sequences 0..batch-1,
+ *   tokens[s] at positions[s] -> next_tokens[s]; XPU_ERR_NONFINITE if any
+ *   sequence's logits held a NaN/Inf (its token is 0xffffffff).
+ * xpu_qwen3_batch_generate: prompts (back to back, prompt_lens[s] tokens
+ *   each) fed token by token, then up to max_new_tokens greedy tokens per
+ *   sequence into out_tokens[s * max_new_tokens + i], out_counts[s] as
+ *   xpu_qwen3_generate; all sequences advance together, one host sync.
+ * xpu_qwen3_batch_set_state / _enqueue_steps / _get_state: device-resident
+ *   stepping of the batch set up by the last batched call.
+ * xpu_qwen3_batch_logits: bf16 logits of sequence `sequence` of the last step. */
+#define XPU_MAX_BATCH 16
+int xpu_qwen3_create_batched(const xpu_qwen3_shape *shape, uint32_t maximum_sequence, int device,
+                             uint32_t max_batch, xpu_qwen3_engine **out);
+int xpu_qwen3_batch_decode(xpu_qwen3_engine *engine, uint32_t batch, const uint32_t *tokens,
+                           const uint32_t *positions, uint32_t *next_tokens);
+int xpu_qwen3_batch_generate(xpu_qwen3_engine *engine, uint32_t batch, const uint32_t *prompts,
+                             const uint32_t *prompt_lens, uint32_t max_new_tokens, int stop_at_eos,
+                             uint32_t *out_tokens, uint32_t *out_counts);
+int xpu_qwen3_batch_set_state(xpu_qwen3_engine *engine, uint32_t batch, const uint32_t *tokens,
+                              const uint32_t *positions);
+int xpu_qwen3_batch_enqueue_steps(xpu_qwen3_engine *engine, uint32_t steps, void *stream);
+int xpu_qwen3_batch_get_state(xpu_qwen3_engine *engine, uint32_t batch, uint32_t *last_tokens,
+                              uint32_t *next_positions, uint32_t *error);
+int xpu_qwen3_batch_logits(xpu_qwen3_engine *engine, uint32_t sequence, uint16_t *host_out, uint32_t count);
+/* Algorithmic HBM bytes of one batched step: the weights once plus every
+ * sequence's K/V over `context` positions. */
+uint64_t xpu_qwen3_batch_bytes_per_step(xpu_qwen3_engine *engine, uint32_t batch, uint32_t context);
+uint32_t xpu_qwen3_batch_kernels_per_step(xpu_qwen3_engine *engine);
+
 #ifdef __cplusplus
 }
 #endif

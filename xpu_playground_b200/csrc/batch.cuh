@@ -1,0 +1,99 @@
+// Batched Qwen3 decode: up to 16 sequences advance one position per step.
+//
+// The reference engine decodes one sequence (qwen3/main.cpp:159-226); at
+// batch 1 every weight byte feeds one multiply-add, at batch B it feeds B.
+// A step streams the weights once for all sequences: each projection is a
+// skinny GEMM Y[16 x rows] = X[16 x K] . W^T on the tensor cores
+// (tcgen05.mma, M = 128 weight rows, N = 16 sequences, accumulators in
+// TMEM), so 16 sequences cost little more HBM time than one. Everything
+// that is per sequence (norms, RoPE, the KV cache, attention, argmax) runs
+// per sequence with the batch-1 arithmetic.
+//
+// One step is this CUDA graph (programmatic dependent launch between
+// kernels; the GEMMs prefetch weights before waiting on their input):
+//   embed_norm                 x[s] = embed[token s], xn[s] = RMSNorm(x[s])
+//   per layer:
+//     (norm)                   xn = RMSNorm(x) with input_layernorm (l > 0)
+//     gemm qkv                 per head tile: q/k RMSNorm + RoPE at the
+//                              sequence's position -> q, key cache; v -> value cache
+//     scores, pv               per (chunk, kv head, sequence) as batch 1
+//     gemm o_proj              x = bf16(x + bf16(attn . Wo^T))
+//     norm                     xn = RMSNorm(x) with post_attention_layernorm
+//     gemm gate/up             h = bf16(bf16(silu(bf16 g)) * bf16 u)
+//     gemm down                x = bf16(x + bf16(h . Wd^T))
+//   norm                       xn = RMSNorm(x) with the final norm
+//   gemm lm_head               bf16 logits, per-tile (max, lowest index)
+//   argmax                     per sequence: greedy token, state update
+//
+// HBM layout: weights are the batch-1 engine's (one arena). Activations are
+// [16][n] row-major bf16 (row s = sequence s; rows >= batch are never
+// written and their GEMM columns never read). The KV cache of layer l is
+// [batch capacity][max_seq][kv heads][128]: sequence s at s * max_seq *
+// kv_heads * 128 elements from the layer's base, sequence 0 being the
+// batch-1 engine's cache.
+#pragma once
+
+#include <stdint.h>
+
+#include "decode.cuh"
+
+namespace xpu {
+
+constexpr uint32_t kMaxBatch = 16;  // sequences per step: the N of one tcgen05 MMA
+
+// Per-sequence step state (host writes it for synchronous calls; the argmax
+// kernel advances it for device-resident generation).
+struct SeqState {
+  uint32_t token;       // input token of the next step (unless position < prompt_len)
+  uint32_t position;    // position of the next step
+  uint32_t prompt_len;  // positions below this read their token from prompt[s][]
+  uint32_t next;        // greedy token of the last step (0xffffffff on NaN/Inf)
+};
+
+struct BatchDims {
+  uint32_t H, I, QH, KVH;  // hidden, intermediate, query heads, kv heads
+  uint32_t vocab;
+  uint32_t max_seq;
+  uint32_t nchunks;        // attention position chunks of max_seq
+  uint32_t batch;          // active sequences (1..16)
+  float eps;
+};
+
+struct BatchBuffers {
+  bf16 *x;              // [16][H] residual stream
+  bf16 *xn;             // [16][H] normalised activations (GEMM operand)
+  bf16 *q;              // [16][QH * 128]
+  bf16 *attn;           // [16][QH * 128] attention output (GEMM operand)
+  bf16 *h;              // [16][I] SwiGLU output (GEMM operand)
+  uint16_t *logits;     // [16][vocab] bf16 bits
+  float *scores;        // [16][QH][max_seq]
+  float *stats;         // [16][QH][nchunks][2]
+  float *attn_part;     // [16][QH][nchunks][128]
+  float *gemm_part;     // [grid][2][16][128] split-tile partial sums
+  unsigned *cnt_tile;   // [max tiles] split-tile arrival counters
+  unsigned *cnt_attn;   // [16][KVH] attention chunk arrivals
+  ArgBest *cand;        // [16][lm tiles] per-tile argmax candidates
+  uint32_t *cand_bad;   // [16][lm tiles] NaN/Inf seen in the tile
+  SeqState *seq;        // [16]
+  uint32_t *error;      // sticky: 1 = NaN/Inf logits or bad token, 4 = wait timeout
+  const uint32_t *prompt;  // [16][max_seq]
+  uint32_t *log;           // [16][max_seq] greedy token per position
+  const bf16 *cos_t, *sin_t;  // [max_seq][128]
+  const bf16 *embed;       // [vocab][H]
+  const bf16 *final_norm;  // [H]
+  const bf16 *lm_head;     // [vocab][H]
+  uint64_t kv_seq_stride;  // elements between two sequences' caches of one layer
+};
+
+// Number of 128-row tiles of the lm_head GEMM (sizes cand / cand_bad).
+inline uint32_t batch_lm_tiles(uint32_t vocab) { return (vocab + 127) / 128; }
+// Most tiles of any GEMM of the step (sizes cnt_tile).
+uint32_t batch_max_tiles(const BatchDims &d);
+// CTAs of the GEMMs (sizes gemm_part: grid * 2 * 16 * 128 floats).
+uint32_t batch_gemm_grid();
+
+// Records one batched step (d.batch sequences) on `s` (graph capture).
+cudaError_t record_batch_step(const BatchDims &d, const BatchBuffers &b, const LayerWeights *layers,
+                              uint32_t n_layers, cudaStream_t s);
+
+}  // namespace xpu

@@ -1,0 +1,972 @@
+// Kernels and graph recording of the batched decode step (batch.cuh).
+//
+// The projections are one kernel, k_bgemm: a persistent skinny GEMM
+// Y[16 x rows] = X[16 x K] . W^T on tcgen05 with the weights W ([rows][K]
+// row-major, as the checkpoint stores them) as the 128-row A operand and the
+// 16 sequences' activations as the N = 16 B operand, both K-major and
+// 128-byte swizzled straight from their row-major layouts by TMA.
+//
+// Work split (stream-K): the (128-row tile, 64-column K block) grid of a
+// GEMM is one list of tiles * K/64 blocks in tile-major order, cut into
+// `grid` equal contiguous ranges, one per CTA (one CTA per SM). Every SM thus
+// streams the same number of weight bytes to within one 16 KB block, where
+// a fixed split-K would leave up to 13% of the SMs idle. A CTA's range
+// covers whole tiles, whose accumulators go straight to the epilogue, and at
+// most two partial tiles at its ends, whose FP32 accumulators it publishes
+// to gemm_part (slot 0: its first tile, slot 1: its last); the CTA that
+// completes a partial tile's arrivals sums the tile's slots in CTA order
+// (results do not depend on arrival order) and runs the epilogue.
+//
+// 192 threads per CTA:
+//   warp 0     TMA producer: a stage is up to 4 consecutive K blocks of one
+//              tile (split at tile and range ends), i.e. per block a 128 x 64
+//              weight box (16 KB) and a 16 x 64 activation box (2 KB), into
+//              a 3-stage ring of 72 KB stages. The 4 boxes of a stage cover
+//              512 contiguous bytes of each weight row, requested back to
+//              back (one-box stages, 128 bytes per row at a time, left HBM at
+//              two thirds of its copy bandwidth). Weights do not depend on
+//              the previous kernel: the first ring's worth is requested
+//              before griddepcontrol.wait, so it streams while the previous
+//              kernel drains.
+//   warp 1     TMEM owner (2 x 4 x 16 columns: a double-buffered set of 4
+//              accumulators); its elected lane issues 4 MMAs (M128 N16 K16)
+//              per K block, the j-th into accumulator j, so consecutive MMAs
+//              never wait on each other's accumulation (at N = 16 one MMA's
+//              math is a few cycles; a chain through one accumulator would
+//              be bound by the accumulate latency), and commits the stage
+//              back to the producer and each finished segment to the
+//              epilogue.
+//   warps 2-5  epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31, i.e.
+//              weight rows, and all 16 sequence columns of the 4
+//              accumulators, summed in accumulator order.
+//
+// Waits are bounded; a timeout sets bit 4 of the batch error word and every
+// role leaves its loop, waiting (bounded) for its own copies and MMAs.
+#include <cuda.h>
+
+#include <algorithm>
+#include <cmath>
+
+#include "batch.cuh"
+#include "decode_device.cuh"
+#include "tcgen05.cuh"
+#include "xpu_internal.h"
+
+namespace xpu {
+
+namespace {
+
+using dec::AttnShared;
+using dec::pv_item;
+using dec::scores_item;
+
+constexpr uint32_t kTileM = 128;                       // weight rows per tile (MMA M, TMEM lanes)
+constexpr uint32_t kSeqN = kMaxBatch;                  // MMA N
+constexpr uint32_t kKb = 64;                           // K per block: one 128-byte swizzled row
+constexpr uint32_t kWBytes = kTileM * kKb * 2;         // 16 KB
+constexpr uint32_t kXBytes = kSeqN * kKb * 2;          // 2 KB
+constexpr uint32_t kBoxes = 4;                         // K blocks per stage (at most)
+constexpr uint32_t kStageW = kBoxes * kWBytes;          // 64 KB
+constexpr uint32_t kStageBytes = kStageW + kBoxes * kXBytes;  // 72 KB (1024-byte multiple)
+constexpr uint32_t kRing = 3;
+constexpr uint32_t kGemmThreads = 192;
+constexpr uint32_t kAccs = kKb / 16;                   // accumulators per buffer: one per MMA of a K block
+constexpr uint32_t kAccCols = kSeqN;                   // TMEM columns of one accumulator
+constexpr uint32_t kBufCols = kAccs * kAccCols;        // 64 columns per buffer
+constexpr uint32_t kTmemCols = 2 * kBufCols;           // double buffered: 128 columns
+// kind::f16 instruction descriptor: FP32 D, BF16 A and B, both K-major, N, M.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((kSeqN >> 3) << 17) | ((kTileM >> 4) << 24);
+
+static_assert(kStageBytes % 1024 == 0, "swizzled stages stay 1024-byte aligned");
+
+enum Epi : int { kEpiQkv = 0, kEpiResid = 1, kEpiGateUp = 2, kEpiLm = 3 };
+
+struct BGemm {
+  uint32_t rows, nk, tiles, total;  // weight rows, K blocks per tile, tiles, tiles * nk
+  BatchDims d;
+  BatchBuffers b;
+  bf16 *out;                    // residual x (kEpiResid) or h (kEpiGateUp)
+  const bf16 *q_norm, *k_norm;  // kEpiQkv
+  bf16 *kcache, *vcache;        // kEpiQkv: this layer's caches (sequence 0)
+};
+
+struct EpiShared {
+  uint16_t vals[kSeqN][kTileM];  // bf16 bits
+  float red[4][kSeqN];
+  ArgBest best[4][kSeqN];
+  uint32_t bad[4][kSeqN];
+};
+
+__host__ __device__ inline uint32_t range_start(uint32_t c, uint32_t total, uint32_t grid) {
+  return static_cast<uint32_t>(static_cast<uint64_t>(c) * total / grid);
+}
+// The CTA whose range holds K block kb (the largest c with range_start(c) <= kb).
+__host__ __device__ inline uint32_t range_owner(uint32_t kb, uint32_t total, uint32_t grid) {
+  return static_cast<uint32_t>((static_cast<uint64_t>(kb + 1) * grid + total - 1) / total) - 1;
+}
+
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
+
+__device__ __forceinline__ float bfv(const bf16 *p, size_t i) {
+  return bf16_bits_to_float(reinterpret_cast<const uint16_t *>(p)[i]);
+}
+__device__ __forceinline__ void putv(bf16 *p, size_t i, float v) {
+  reinterpret_cast<uint16_t *>(p)[i] = float_to_bf16_bits(v);
+}
+
+// ---- epilogues: thread = weight row r of tile t, v[s] = FP32 sum for sequence s ----
+
+// Tile t is head t of [q; k; v]: q/k RMSNorm (weight, eps) and RoPE at each
+// sequence's position into q / the key cache, v into the value cache
+// (transformers rounding points, as the batch-1 head epilogue).
+__device__ inline void epi_qkv(const BGemm &p, uint32_t t, uint32_t r, const float (&v)[kSeqN], EpiShared &es) {
+  const BatchDims &d = p.d;
+  const uint32_t lane = threadIdx.x & 31, quarter = (threadIdx.x >> 5) & 3;
+  const bool is_q = t < d.QH, is_v = t >= d.QH + d.KVH;
+  // Every input of the epilogue is loaded before any store (one round trip).
+  uint32_t pos[kSeqN];
+#pragma unroll
+  for (uint32_t s = 0; s < kSeqN; ++s) pos[s] = s < d.batch ? p.b.seq[s].position : 0u;
+  if (is_v) {
+    const uint32_t kvh = t - d.QH - d.KVH;
+#pragma unroll
+    for (uint32_t s = 0; s < kSeqN; ++s)
+      if (s < d.batch)
+        putv(p.vcache + s * p.b.kv_seq_stride, (static_cast<size_t>(pos[s]) * d.KVH + kvh) * kHD + r, v[s]);
+    return;
+  }
+  float cs[kSeqN], sn[kSeqN];
+#pragma unroll
+  for (uint32_t s = 0; s < kSeqN; ++s) {
+    cs[s] = s < d.batch ? bfv(p.b.cos_t, static_cast<size_t>(pos[s]) * kHD + r) : 0.f;
+    sn[s] = s < d.batch ? bfv(p.b.sin_t, static_cast<size_t>(pos[s]) * kHD + r) : 0.f;
+  }
+  float val[kSeqN];
+#pragma unroll
+  for (uint32_t s = 0; s < kSeqN; ++s) {
+    val[s] = round_bf16(v[s]);
+    const float sq = warp_sum(__fmul_rn(val[s], val[s]));
+    if (lane == 0) es.red[quarter][s] = sq;
+  }
+  epi_sync();
+  const float nw = bfv(is_q ? p.q_norm : p.k_norm, r);
+#pragma unroll
+  for (uint32_t s = 0; s < kSeqN; ++s) {
+    const float ss = ((es.red[0][s] + es.red[1][s]) + es.red[2][s]) + es.red[3][s];
+    const float rs = 1.0f / sqrtf(ss / static_cast<float>(kHD) + d.eps);
+    es.vals[s][r] = float_to_bf16_bits(__fmul_rn(nw, round_bf16(__fmul_rn(val[s], rs))));
+  }
+  epi_sync();
+#pragma unroll
+  for (uint32_t s = 0; s < kSeqN; ++s) {
+    if (s >= d.batch) break;
+    const float a = bf16_bits_to_float(es.vals[s][r]), o = bf16_bits_to_float(es.vals[s][r ^ 64]);
+    const float rot = r < 64 ? round_bf16(__fmul_rn(-o, sn[s])) : round_bf16(__fmul_rn(o, sn[s]));
+    const float out = round_bf16(__fadd_rn(round_bf16(__fmul_rn(a, cs[s])), rot));
+    bf16 *dst = is_q ? p.b.q + (static_cast<size_t>(s) * d.QH + t) * kHD
+                     : p.kcache + s * p.b.kv_seq_stride + (static_cast<size_t>(pos[s]) * d.KVH + (t - d.QH)) * kHD;
+    putv(dst, r, out);
+  }
+  epi_sync();  // es is reused by the next tile
+}
+
+// x[s][row] = bf16(x[s][row] + bf16(sum)).
+__device__ inline void epi_resid(const BGemm &p, uint32_t row, const float (&v)[kSeqN]) {
+  if (row >= p.rows) return;
+  float x[kSeqN];  // every residual loaded before any store (one round trip)
+#pragma unroll
+  for (uint32_t s = 0; s < kSeqN; ++s) x[s] = s < p.d.batch ? bfv(p.out, static_cast<size_t>(s) * p.rows + row) : 0.f;
+#pragma unroll
+  for (uint32_t s = 0; s < kSeqN; ++s)
+    if (s < p.d.batch) putv(p.out, static_cast<size_t>(s) * p.rows + row, __fadd_rn(x[s], round_bf16(v[s])));
+}
+
+// Rows 2i, 2i + 1 are gate and up of unit i (adjacent lanes of one warp):
+// h[s][i] = bf16(bf16(silu(bf16 g)) * bf16 u).
+__device__ inline void epi_gateup(const BGemm &p, uint32_t row, const float (&v)[kSeqN]) {
+  const uint32_t lane = threadIdx.x & 31, units = p.rows / 2;
+#pragma unroll
+  for (uint32_t s = 0; s < kSeqN; ++s) {
+    const float gv = round_bf16(v[s]);
+    const float uv = __shfl_down_sync(kFullMask, gv, 1);
+    if (!(lane & 1) && s < p.d.batch && row < p.rows) {
+      const float act = round_bf16(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))));
+      putv(p.out, static_cast<size_t>(s) * units + row / 2, __fmul_rn(act, uv));
+    }
+  }
+}
+
+// bf16 logits and the tile's (max, lowest index) candidate per sequence;
+// NaN/Inf logits mark the tile bad.
+__device__ inline void epi_lm(const BGemm &p, uint32_t t, uint32_t row, const float (&v)[kSeqN], EpiShared &es) {
+  const uint32_t lane = threadIdx.x & 31, quarter = (threadIdx.x >> 5) & 3, et = threadIdx.x - 64;
+  const bool ok = row < p.rows;
+#pragma unroll
+  for (uint32_t s = 0; s < kSeqN; ++s) {
+    const float lv = round_bf16(v[s]);
+    if (ok && s < p.d.batch) p.b.logits[static_cast<size_t>(s) * p.rows + row] = float_to_bf16_bits(lv);
+    const bool bad = ok && not_finite(lv);
+    ArgBest cb = (ok && !bad) ? ArgBest{lv, row} : ArgBest{-INFINITY, 0xffffffffu};
+    cb = warp_argbest(cb);
+    const uint32_t anybad = __any_sync(kFullMask, bad) ? 1u : 0u;
+    if (lane == 0) { es.best[quarter][s] = cb; es.bad[quarter][s] = anybad; }
+  }
+  epi_sync();
+  if (et < p.d.batch) {
+    ArgBest cb = es.best[0][et];
+    uint32_t bad = es.bad[0][et];
+    for (uint32_t qq = 1; qq < 4; ++qq) { cb = arg_better(cb, es.best[qq][et]); bad |= es.bad[qq][et]; }
+    p.b.cand[static_cast<size_t>(et) * p.tiles + t] = cb;
+    p.b.cand_bad[static_cast<size_t>(et) * p.tiles + t] = bad;
+  }
+  epi_sync();
+}
+
+template <int EPI>
+__device__ __forceinline__ void run_epilogue(const BGemm &p, uint32_t t, uint32_t r, const float (&v)[kSeqN],
+                                             EpiShared &es) {
+  const uint32_t row = t * kTileM + r;
+  if (EPI == kEpiQkv) epi_qkv(p, t, r, v, es);
+  if (EPI == kEpiResid) epi_resid(p, row, v);
+  if (EPI == kEpiGateUp) epi_gateup(p, row, v);
+  if (EPI == kEpiLm) epi_lm(p, t, row, v, es);
+}
+
+__device__ __forceinline__ bool failed_now(const int *f) { return *reinterpret_cast<const volatile int *>(f) != 0; }
+
+// End of the stage that starts at K block kb: up to kBoxes blocks, not past
+// the tile or the CTA's range.
+__device__ __forceinline__ uint32_t stage_end(uint32_t kb, uint32_t kb1, uint32_t nk) {
+  const uint32_t tile_end = (kb / nk + 1) * nk;
+  return min(min(kb + kBoxes, kb1), tile_end);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, const BGemm p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ uint64_t full[kRing], empty[kRing], acc_full[2], acc_empty[2], mma_done;
+  __shared__ uint32_t tmem_base, consumed, issued_count;
+  __shared__ int failed, last_flag;
+  __shared__ EpiShared es;
+  const uint32_t a0 = smem_addr(smem_raw);
+  uint8_t *ring = smem_raw + ((a0 + 1023u) / 1024u * 1024u - a0);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t G = gridDim.x, c = blockIdx.x, nk = p.nk;
+  const uint32_t kb0 = range_start(c, p.total, G), kb1 = range_start(c + 1, p.total, G);
+  const uint32_t n = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < kRing; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (uint32_t i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(&mma_done, 1);
+    fence_mbar_init();
+    failed = 0;
+    consumed = 0;
+    issued_count = 0;
+  }
+  if (warp == 1) tmem_alloc1(&tmem_base, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  grid_dep_launch();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t pol = evict_first_policy();
+      uint32_t issued = 0, kb = kb0;
+      // Weights first (independent of the previous kernel), then, once it
+      // has finished, the activations of those stages and the rest.
+      uint32_t pre_end[kRing];
+      for (; issued < kRing && kb < kb1; ++issued) {
+        const uint32_t e = stage_end(kb, kb1, nk);
+        uint8_t *st = ring + issued * kStageBytes;
+        mbar_expect_tx(&full[issued], (e - kb) * (kWBytes + kXBytes));
+        for (uint32_t j = 0; j < e - kb; ++j)
+          tma_load_2d(st + j * kWBytes, &map_w, static_cast<int32_t>(((kb + j) % nk) * kKb),
+                      static_cast<int32_t>((kb / nk) * kTileM), &full[issued], pol);
+        pre_end[issued] = e;
+        kb = e;
+      }
+      grid_dep_wait();
+      for (uint32_t i = 0, b = kb0; i < issued; b = pre_end[i], ++i)
+        for (uint32_t j = 0; j < pre_end[i] - b; ++j)
+          tma_load_2d_plain(ring + i * kStageBytes + kStageW + j * kXBytes, &map_x,
+                            static_cast<int32_t>(((b + j) % nk) * kKb), 0, &full[i]);
+      for (uint32_t i = issued; kb < kb1; ++i) {
+        const uint32_t s = i % kRing, use = i / kRing;
+        if (failed_now(&failed) || !mbar_wait(&empty[s], (use - 1) & 1)) { failed = 1; break; }
+        const uint32_t e = stage_end(kb, kb1, nk);
+        uint8_t *st = ring + s * kStageBytes;
+        mbar_expect_tx(&full[s], (e - kb) * (kWBytes + kXBytes));
+        for (uint32_t j = 0; j < e - kb; ++j)
+          tma_load_2d(st + j * kWBytes, &map_w, static_cast<int32_t>(((kb + j) % nk) * kKb),
+                      static_cast<int32_t>((kb / nk) * kTileM), &full[s], pol);
+        for (uint32_t j = 0; j < e - kb; ++j)
+          tma_load_2d_plain(st + kStageW + j * kXBytes, &map_x, static_cast<int32_t>(((kb + j) % nk) * kKb), 0,
+                            &full[s]);
+        issued = i + 1;
+        kb = e;
+      }
+      issued_count = issued;  // copies not consumed by the MMAs are drained at exit
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      uint32_t seg = 0, i = 0;
+      for (uint32_t kb = kb0; kb < kb1; ++i) {
+        const uint32_t e = stage_end(kb, kb1, nk);
+        const bool first = kb == kb0 || kb % nk == 0, last = e == kb1 || e % nk == 0;
+        const uint32_t buf = seg & 1;
+        if (first && seg >= 2) {
+          if (!mbar_wait(&acc_empty[buf], ((seg >> 1) - 1) & 1)) { failed = 1; break; }
+          tc_fence_after();
+        }
+        const uint32_t s = i % kRing;
+        if (failed_now(&failed) || !mbar_wait(&full[s], (i / kRing) & 1)) { failed = 1; break; }
+        tc_fence_after();
+        const uint32_t sa = smem_addr(ring + s * kStageBytes), sx = sa + kStageW;
+        for (uint32_t j = 0; j < e - kb; ++j)
+#pragma unroll
+          for (uint32_t k16 = 0; k16 < kAccs; ++k16)
+            mma1_f16(tmem + buf * kBufCols + k16 * kAccCols, smem_desc(sa + j * kWBytes + 32 * k16, 16, 1024),
+                     smem_desc(sx + j * kXBytes + 32 * k16, 16, 1024), kIdesc, (first && j == 0) ? 0u : 1u);
+        mma1_commit(&empty[s]);
+        if (last) {
+          mma1_commit(&acc_full[buf]);
+          ++seg;
+        }
+        kb = e;
+      }
+      consumed = i;
+      // Every MMA this thread issued has completed before TMEM is freed.
+      mma1_commit(&mma_done);
+      if (!mbar_wait(&mma_done, 0)) failed = 1;
+    }
+  } else {
+    // Epilogue warps: inputs of the epilogue (residual, positions, caches)
+    // come from earlier kernels.
+    grid_dep_wait();
+    const uint32_t quarter = warp & 3, r = quarter * 32 + lane, et = threadIdx.x - 64;
+    // A warp that gives up waiting stays in the loop (every epilogue warp
+    // must reach the same named barriers) and computes on zeros from then on.
+    bool dead = false;
+    uint32_t seg = 0;
+    for (uint32_t kb = kb0; kb < kb1; ++seg) {
+      const uint32_t t = kb / nk, end = min(kb1, (t + 1) * nk);
+      const bool whole = kb == t * nk && end == (t + 1) * nk;
+      const uint32_t buf = seg & 1;
+      if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&acc_full[buf], (seg >> 1) & 1));
+      if (dead) failed = 1;
+      float v[kSeqN];
+#pragma unroll
+      for (uint32_t s = 0; s < kSeqN; ++s) v[s] = 0.f;
+      if (!dead) {
+        tc_fence_after();
+        uint32_t a[kAccs][kSeqN];
+        const uint32_t base = tmem + ((quarter * 32u) << 16) + buf * kBufCols;
+#pragma unroll
+        for (uint32_t j = 0; j < kAccs; ++j) tmem_ld16_nowait(base + j * kAccCols, a[j]);
+        tmem_wait_ld();
+#pragma unroll
+        for (uint32_t s = 0; s < kSeqN; ++s) {
+          float sum = __uint_as_float(a[0][s]);
+#pragma unroll
+          for (uint32_t j = 1; j < kAccs; ++j) sum += __uint_as_float(a[j][s]);
+          v[s] = sum;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      bool run = true;
+      if (!whole) {
+        const uint32_t slot = t == kb0 / nk ? 0u : 1u;
+        float *dst = p.b.gemm_part + (static_cast<size_t>(c) * 2 + slot) * (kSeqN * kTileM) + r;
+#pragma unroll
+        for (uint32_t s = 0; s < kSeqN; ++s) dst[s * kTileM] = v[s];
+        const uint32_t c0 = range_owner(t * nk, p.total, G), c1 = range_owner((t + 1) * nk - 1, p.total, G);
+        epi_sync();  // the tile's partial is complete in this CTA; one thread fences for all
+        if (et == 0) {
+          __threadfence();
+          last_flag = atomicAdd(p.b.cnt_tile + t, 1u) == c1 - c0;
+          __threadfence();
+        }
+        epi_sync();
+        run = last_flag != 0;
+        if (run) {
+          float w[kSeqN];
+#pragma unroll
+          for (uint32_t s = 0; s < kSeqN; ++s) w[s] = 0.f;
+          // Slots in CTA order, four at a time with all their loads in flight.
+          for (uint32_t c4 = c0; c4 <= c1; c4 += 4) {
+            float x[4][kSeqN];
+#pragma unroll
+            for (uint32_t j = 0; j < 4; ++j) {
+              const uint32_t cc = c4 + j;
+              if (cc > c1) break;
+              const uint32_t sl = t == range_start(cc, p.total, G) / nk ? 0u : 1u;
+              const float *src = p.b.gemm_part + (static_cast<size_t>(cc) * 2 + sl) * (kSeqN * kTileM) + r;
+#pragma unroll
+              for (uint32_t s = 0; s < kSeqN; ++s) x[j][s] = __ldcg(src + s * kTileM);
+            }
+#pragma unroll
+            for (uint32_t j = 0; j < 4; ++j) {
+              if (c4 + j > c1) break;
+#pragma unroll
+              for (uint32_t s = 0; s < kSeqN; ++s) w[s] += x[j][s];
+            }
+          }
+#pragma unroll
+          for (uint32_t s = 0; s < kSeqN; ++s) v[s] = w[s];
+          if (et == 0) p.b.cnt_tile[t] = 0;
+        }
+      }
+      if (run) run_epilogue<EPI>(p, t, r, v, es);
+      kb = end;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // Copies still in flight after a failure: wait (bounded) for each issued
+    // stage that the MMA thread did not consume.
+    for (uint32_t i = consumed; i < issued_count; ++i)
+      if (!mbar_wait(&full[i % kRing], (i / kRing) & 1)) break;
+    if (failed) atomicOr(p.b.error, kErrPipelineTimeout);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc1(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- norms ----
+// xn[s] = RMSNorm(x[s]) * w (transformers rounding, the batch-1 arithmetic
+// and summation order); with `embed`, x[s] = embed[token s] first.
+__global__ void __launch_bounds__(256) k_bnorm(BatchDims d, BatchBuffers b, const bf16 *w, int embed) {
+  __shared__ float scratch[8];
+  grid_dep_launch();
+  grid_dep_wait();
+  const uint32_t s = blockIdx.x, t = threadIdx.x, H = d.H;
+  uint4 *x4 = reinterpret_cast<uint4 *>(b.x + static_cast<size_t>(s) * H);
+  uint4 *xn4 = reinterpret_cast<uint4 *>(b.xn + static_cast<size_t>(s) * H);
+  const uint4 *src = x4;
+  if (embed) {
+    const SeqState st = b.seq[s];
+    uint32_t tok = st.position < st.prompt_len ? b.prompt[static_cast<size_t>(s) * d.max_seq + st.position] : st.token;
+    if (tok >= d.vocab) {  // a NaN step's sentinel or a bad id: read row 0, flag the batch
+      if (t == 0) atomicOr(b.error, 1u);
+      tok = 0;
+    }
+    src = reinterpret_cast<const uint4 *>(b.embed) + static_cast<size_t>(tok) * (H / 8);
+  }
+  float ss = 0.f;
+  for (uint32_t c = t; c < H / 8; c += 256) {
+    const uint4 v = src[c];
+    if (embed) x4[c] = v;
+    ss = dec::sq8(v, ss);
+  }
+  ss = block_sum<8>(ss, scratch);
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(H) + d.eps);
+  const uint4 *w4 = reinterpret_cast<const uint4 *>(w);
+  for (uint32_t c = t; c < H / 8; c += 256) {
+    const uint4 xv = src[c], wv = w4[c];
+    const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lo = round_bf16(__fmul_rn(bf16_lo(wa[j]), round_bf16(__fmul_rn(bf16_lo(xa[j]), r))));
+      const float hi = round_bf16(__fmul_rn(bf16_hi(wa[j]), round_bf16(__fmul_rn(bf16_hi(xa[j]), r))));
+      o[j] = pack_bf16x2(lo, hi);
+    }
+    xn4[c] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ------------------------------------------------------------ attention ----
+// Per (position chunk, kv head, sequence): the batch-1 scores and p.v items
+// on sequence s's views of q, the caches and the attention scratch.
+__device__ inline void seq_views(const BatchDims &bd, const BatchBuffers &bb, const LayerWeights &w, uint32_t s,
+                                 DecodeDims &d, DecodeBuffers &b, LayerWeights &ws) {
+  d = DecodeDims{};
+  d.H = bd.H;
+  d.QH_l = bd.QH;
+  d.KVH_l = bd.KVH;
+  d.max_seq = bd.max_seq;
+  b = DecodeBuffers{};
+  const size_t qs = static_cast<size_t>(s) * bd.QH;
+  b.q = bb.q + qs * kHD;
+  b.attn = bb.attn + qs * kHD;
+  b.scores = bb.scores + qs * bd.max_seq;
+  b.stats = bb.stats + qs * bd.nchunks * 2;
+  b.attn_part = bb.attn_part + qs * bd.nchunks * kHD;
+  b.cnt_attn = bb.cnt_attn + static_cast<size_t>(s) * bd.KVH;
+  ws = w;
+  ws.kcache = w.kcache + s * bb.kv_seq_stride;
+  ws.vcache = w.vcache + s * bb.kv_seq_stride;
+}
+
+template <int G>
+__global__ void __launch_bounds__(kStreamThreads) k_bscores(BatchDims bd, BatchBuffers bb, LayerWeights w) {
+  __shared__ AttnShared<G> as;
+  grid_dep_launch();
+  grid_dep_wait();
+  if (threadIdx.x < 32) return;
+  const uint32_t s = blockIdx.z, n = bb.seq[s].position + 1;
+  if (blockIdx.x * kPosChunk >= n) return;
+  DecodeDims d;
+  DecodeBuffers b;
+  LayerWeights ws;
+  seq_views(bd, bb, w, s, d, b, ws);
+  scores_item<G>(d, b, ws, blockIdx.y, blockIdx.x, bd.nchunks, n, as);
+}
+
+template <int G>
+__global__ void __launch_bounds__(kStreamThreads) k_bpv(BatchDims bd, BatchBuffers bb, LayerWeights w) {
+  __shared__ AttnShared<G> as;
+  grid_dep_launch();
+  grid_dep_wait();
+  if (threadIdx.x < 32) return;
+  const uint32_t s = blockIdx.z, n = bb.seq[s].position + 1;
+  if (blockIdx.x * kPosChunk >= n) return;
+  DecodeDims d;
+  DecodeBuffers b;
+  LayerWeights ws;
+  seq_views(bd, bb, w, s, d, b, ws);
+  pv_item<G>(d, b, ws, blockIdx.y, blockIdx.x, bd.nchunks, n, as);
+}
+
+// ------------------------------------------------- fused attention (one CTA) ----
+// One CTA per (kv head h, sequence s) runs the whole decode attention of the
+// head group over positions [0, n): pass 1 streams K (TMA, 64-position
+// stages of the head's 256-byte rows) and stores s = bf16(bf16(q.k) * scale)
+// for the group's G query heads in shared memory - exactly, as bf16; then
+// per head M = max s, S = sum exp(s - M) (fixed order) and the scores become
+// p = bf16(exp(s - M) * (1 / S)) in place (the rounding points of the
+// batch-1 path); pass 2 streams V and accumulates p * v, and the CTA writes
+// the bf16 output of its G heads. Nothing crosses CTAs, so there is no
+// score scratch, statistics exchange or chunk combine in global memory.
+// Warp 0 is the TMA producer; the 8 consumer warps take 8 positions each of
+// every stage, lane l dimensions 4l .. 4l + 3. K stages that hold only
+// positions below n - 1 (rows written by earlier steps) are requested before
+// griddepcontrol.wait; the newest row comes from the previous kernel.
+constexpr uint32_t kAttnPos = 64;                       // positions per stage
+constexpr uint32_t kAttnStageBytes = kAttnPos * kHD * 2;  // 16 KB
+constexpr uint32_t kAttnStages = 6;
+constexpr uint32_t kAttnPosPerWarp = kAttnPos / kConsumerWarps;  // 8
+
+__host__ __device__ inline size_t attn_scores_bytes(uint32_t G, uint32_t max_seq) {
+  return (static_cast<size_t>(G) * max_seq * 2 + 15) / 16 * 16;
+}
+__host__ __device__ inline size_t attn_smem_bytes(uint32_t G, uint32_t max_seq) {
+  return 1024 + static_cast<size_t>(kAttnStages) * kAttnStageBytes + attn_scores_bytes(G, max_seq);
+}
+
+// Transpose reduction: lane l holds V = 8 G partial sums; afterwards lane l
+// holds the warp-wide sums of values [l V / 32, (l + 1) V / 32) in val[0..]
+// (for V < 32 lanes that share a value hold identical sums).
+template <int V>
+__device__ __forceinline__ void warp_transpose_sum(float (&val)[V], uint32_t lane) {
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    const int o = 16 >> k, half = V >> (k + 1);
+    if (half >= 1) {
+      const bool upper = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = upper ? val[i] : val[i + half];
+        const float keep = upper ? val[i + half] : val[i];
+        val[i] = keep + __shfl_xor_sync(kFullMask, send, o);
+      }
+    } else {
+      val[0] += __shfl_xor_sync(kFullMask, val[0], o);
+    }
+  }
+}
+
+template <int G>
+__global__ void __launch_bounds__(kStreamThreads, 1)
+k_battn(BatchDims bd, BatchBuffers bb, const __grid_constant__ CUtensorMap map_k,
+        const __grid_constant__ CUtensorMap map_v) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ uint64_t full[kAttnStages], empty[kAttnStages];
+  __shared__ float red_m[kConsumerWarps][G], red_s[kConsumerWarps][G];
+  __shared__ float sM[G], sInv[G];
+  __shared__ int failed;
+  __shared__ uint32_t issued_n;
+  const uint32_t a0 = smem_addr(smem_raw);
+  uint8_t *ring = smem_raw + ((a0 + 1023u) / 1024u * 1024u - a0);
+  uint16_t *sc = reinterpret_cast<uint16_t *>(ring + kAttnStages * kAttnStageBytes);  // [G][max_seq] bf16
+  const uint32_t h = blockIdx.x, s = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t ms = bd.max_seq;
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < kAttnStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kConsumerWarps);
+    }
+    fence_mbar_init();
+    failed = 0;
+    issued_n = 0;
+  }
+  __syncthreads();
+  grid_dep_launch();
+  // Positions: the newest row (n - 1) is written by the previous kernel, so
+  // the position is read only after waiting - except by the producer, which
+  // needs it before: it reads the state, which no kernel of the step writes
+  // before the argmax.
+  const uint32_t n = bb.seq[s].position + 1;
+  const uint32_t nst = (n + kAttnPos - 1) / kAttnPos;  // stages per pass
+  const int32_t y0 = static_cast<int32_t>(s * ms), xh = static_cast<int32_t>(h * kHD);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // K stages entirely below the newest row may be fetched before the wait.
+      uint32_t early = (n - 1) / kAttnPos;
+      if (early > kAttnStages) early = kAttnStages;
+      for (uint32_t i = 0; i < early; ++i) {
+        mbar_expect_tx(&full[i], kAttnStageBytes);
+        tma_load_2d_plain(ring + i * kAttnStageBytes, &map_k, xh, y0 + static_cast<int32_t>(i * kAttnPos), &full[i]);
+      }
+      grid_dep_wait();
+      asm volatile("fence.proxy.async.global;" ::: "memory");  // the new row, written by generic stores
+      uint32_t i = early;
+      for (; i < 2 * nst; ++i) {
+        const uint32_t slot = i % kAttnStages, use = i / kAttnStages;
+        if (use > 0 && (failed_now(&failed) || !mbar_wait(&empty[slot], (use - 1) & 1))) { failed = 1; break; }
+        mbar_expect_tx(&full[slot], kAttnStageBytes);
+        const bool is_v = i >= nst;
+        const int32_t y = y0 + static_cast<int32_t>((is_v ? i - nst : i) * kAttnPos);
+        tma_load_2d_plain(ring + slot * kAttnStageBytes, is_v ? &map_v : &map_k, xh, y, &full[slot]);
+      }
+      issued_n = i;
+    }
+    __syncwarp();
+  } else {
+    grid_dep_wait();
+    const uint32_t cw = warp - 1, t = threadIdx.x - 32;
+    bool dead = false;
+    // q of the group's heads, this lane's 4 dimensions
+    float q[G][4];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const uint2 raw = *reinterpret_cast<const uint2 *>(bb.q + (static_cast<size_t>(s) * bd.QH + h * G + g) * kHD + lane * 4);
+      q[g][0] = bf16_lo(raw.x); q[g][1] = bf16_hi(raw.x); q[g][2] = bf16_lo(raw.y); q[g][3] = bf16_hi(raw.y);
+    }
+    // ---- pass 1: scores
+    for (uint32_t i = 0; i < nst; ++i) {
+      const uint32_t slot = i % kAttnStages;
+      if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&full[slot], (i / kAttnStages) & 1));
+      const uint8_t *st = ring + slot * kAttnStageBytes;
+      float val[kAttnPosPerWarp * G];
+#pragma unroll
+      for (uint32_t pp = 0; pp < kAttnPosPerWarp; ++pp) {
+        const uint2 kr = dead ? make_uint2(0, 0)
+                              : *reinterpret_cast<const uint2 *>(st + (cw * kAttnPosPerWarp + pp) * (kHD * 2) + lane * 8);
+        const float k4[4] = {bf16_lo(kr.x), bf16_hi(kr.x), bf16_lo(kr.y), bf16_hi(kr.y)};
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float a = 0.f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) a = fmaf(q[g][j], k4[j], a);
+          val[pp * G + g] = a;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+      warp_transpose_sum<kAttnPosPerWarp * G>(val, lane);
+      constexpr uint32_t kVals = kAttnPosPerWarp * G;               // sums per warp and stage
+      constexpr uint32_t kPer = kVals >= 32 ? kVals / 32 : 1;         // sums held per lane
+      constexpr uint32_t kShare = kVals >= 32 ? 1 : 32 / kVals;       // lanes holding the same sum
+#pragma unroll
+      for (uint32_t k = 0; k < kPer; ++k) {
+        const uint32_t idx = lane / kShare * kPer + k;
+        const uint32_t pp = idx / G, g = idx % G, pos = i * kAttnPos + cw * kAttnPosPerWarp + pp;
+        if (lane % kShare == 0 && pos < n)
+          sc[g * ms + pos] = float_to_bf16_bits(round_bf16(__fmul_rn(round_bf16(val[k]), kAttnScale)));
+      }
+    }
+    consumer_sync();
+    // ---- per head: max, sum of exp, then probabilities in place
+    float m[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) m[g] = -INFINITY;
+    for (uint32_t pos = t; pos < n; pos += kConsumerThreads)
+#pragma unroll
+      for (int g = 0; g < G; ++g) m[g] = fmaxf(m[g], bf16_bits_to_float(sc[g * ms + pos]));
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float wm = warp_max(m[g]);
+      if (lane == 0) red_m[cw][g] = wm;
+    }
+    consumer_sync();
+    if (t < static_cast<uint32_t>(G)) {
+      float mm = red_m[0][t];
+      for (int w = 1; w < kConsumerWarps; ++w) mm = fmaxf(mm, red_m[w][t]);
+      sM[t] = mm;
+    }
+    consumer_sync();
+    float l[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) l[g] = 0.f;
+    for (uint32_t pos = t; pos < n; pos += kConsumerThreads)
+#pragma unroll
+      for (int g = 0; g < G; ++g) l[g] += expf(bf16_bits_to_float(sc[g * ms + pos]) - sM[g]);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float ws = warp_sum(l[g]);
+      if (lane == 0) red_s[cw][g] = ws;
+    }
+    consumer_sync();
+    if (t < static_cast<uint32_t>(G)) {
+      float ss = 0.f;
+      for (int w = 0; w < kConsumerWarps; ++w) ss += red_s[w][t];
+      sInv[t] = 1.0f / ss;
+    }
+    consumer_sync();
+    for (uint32_t pos = t; pos < n; pos += kConsumerThreads)
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float sv = bf16_bits_to_float(sc[g * ms + pos]);
+        sc[g * ms + pos] = float_to_bf16_bits(__fmul_rn(expf(sv - sM[g]), sInv[g]));
+      }
+    consumer_sync();
+    // ---- pass 2: p . v
+    float acc[G][4];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[g][j] = 0.f;
+    for (uint32_t i = 0; i < nst; ++i) {
+      const uint32_t gi = nst + i, slot = gi % kAttnStages;
+      if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&full[slot], (gi / kAttnStages) & 1));
+      const uint8_t *st = ring + slot * kAttnStageBytes;
+#pragma unroll
+      for (uint32_t pp = 0; pp < kAttnPosPerWarp; ++pp) {
+        const uint32_t pos = i * kAttnPos + cw * kAttnPosPerWarp + pp;
+        if (pos >= n || dead) continue;
+        const uint2 vr = *reinterpret_cast<const uint2 *>(st + (cw * kAttnPosPerWarp + pp) * (kHD * 2) + lane * 8);
+        const float v4[4] = {bf16_lo(vr.x), bf16_hi(vr.x), bf16_lo(vr.y), bf16_hi(vr.y)};
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float pr = bf16_bits_to_float(sc[g * ms + pos]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[g][j] = fmaf(pr, v4[j], acc[g][j]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    if (dead) failed = 1;
+    consumer_sync();  // every stage consumed: the ring is free for the warp partials
+    float *part = reinterpret_cast<float *>(ring);  // [8 warps][G][128]
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      *reinterpret_cast<float4 *>(part + (cw * G + g) * kHD + lane * 4) =
+          make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+    consumer_sync();
+    for (uint32_t e = t; e < G * kHD; e += kConsumerThreads) {
+      float o = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) o += part[w * G * kHD + e];
+      const uint32_t g = e / kHD, dd = e % kHD;
+      putv(bb.attn, (static_cast<size_t>(s) * bd.QH + h * G + g) * kHD + dd, o);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && failed) {
+    // After a failure copies may still be in flight: wait (bounded) for the
+    // last ring's worth that was issued.
+    const uint32_t from = issued_n > kAttnStages ? issued_n - kAttnStages : 0;
+    for (uint32_t i = from; i < issued_n; ++i)
+      if (!mbar_wait(&full[i % kAttnStages], (i / kAttnStages) & 1)) break;
+    atomicOr(bb.error, kErrPipelineTimeout);
+  }
+}
+
+// --------------------------------------------------------------- argmax ----
+// Per sequence: the lm tiles' candidates in tile order -> greedy token
+// (lowest index on ties; 0xffffffff when any logit was NaN/Inf), then the
+// state advances one position.
+__global__ void __launch_bounds__(256) k_bargmax(BatchDims d, BatchBuffers b, uint32_t tiles) {
+  __shared__ ArgBest wb[8];
+  __shared__ uint32_t wbad[8];
+  grid_dep_launch();
+  grid_dep_wait();
+  const uint32_t s = blockIdx.x, t = threadIdx.x;
+  ArgBest best{-INFINITY, 0xffffffffu};
+  uint32_t bad = 0;
+  for (uint32_t i = t; i < tiles; i += 256) {
+    best = arg_better(best, b.cand[static_cast<size_t>(s) * tiles + i]);
+    bad |= b.cand_bad[static_cast<size_t>(s) * tiles + i];
+  }
+  best = warp_argbest(best);
+  bad = __reduce_or_sync(kFullMask, bad);
+  if ((t & 31) == 0) { wb[t >> 5] = best; wbad[t >> 5] = bad; }
+  __syncthreads();
+  if (t == 0) {
+    ArgBest fb = wb[0];
+    uint32_t fbad = wbad[0];
+    for (int i = 1; i < 8; ++i) { fb = arg_better(fb, wb[i]); fbad |= wbad[i]; }
+    const uint32_t next = (fbad || fb.index == 0xffffffffu) ? 0xffffffffu : fb.index;
+    if (next == 0xffffffffu) atomicOr(b.error, 1u);
+    SeqState &st = b.seq[s];
+    const uint32_t pos = st.position;
+    st.next = next;
+    st.token = next;
+    if (pos < d.max_seq) b.log[static_cast<size_t>(s) * d.max_seq + pos] = next;
+    st.position = pos + 1;
+  }
+}
+
+// ------------------------------------------------------------- launches ----
+uint32_t sm_count() {
+  static int count = 0;
+  if (count == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || count <= 0)
+      count = 148;
+  }
+  return static_cast<uint32_t>(count);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args... args) {
+  if (smem > 48 * 1024) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+constexpr size_t kGemmSmem = static_cast<size_t>(kRing) * kStageBytes + 1024;
+
+// Y = X . W^T for W [rows][K] and X [16][K] (K a multiple of 64, both 16-byte
+// aligned with 16-byte row pitches), with epilogue EPI.
+template <int EPI>
+cudaError_t launch_bgemm(const bf16 *W, uint32_t rows, uint32_t K, const bf16 *X, BGemm p, cudaStream_t s) {
+  if (K % kKb) return cudaErrorInvalidValue;
+  CUtensorMap mw, mx;
+  cudaError_t e = make_tmap_2d_u16_swizzled(&mw, W, K, rows, K, kKb, kTileM);
+  if (e != cudaSuccess) return e;
+  e = make_tmap_2d_u16_swizzled(&mx, X, K, kSeqN, K, kKb, kSeqN);
+  if (e != cudaSuccess) return e;
+  p.rows = rows;
+  p.nk = K / kKb;
+  p.tiles = (rows + kTileM - 1) / kTileM;
+  p.total = p.tiles * p.nk;
+  const uint32_t grid = std::min(sm_count(), p.total);
+  return launch_pdl(k_bgemm<EPI>, dim3(grid), dim3(kGemmThreads), kGemmSmem, s, mw, mx, p);
+}
+
+int smem_optin() {
+  static int bytes = 0;
+  if (bytes == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&bytes, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || bytes <= 0)
+      bytes = 227 * 1024;
+  }
+  return bytes;
+}
+
+// Fused one-CTA-per-(head, sequence) attention when the group's scores for
+// max_seq positions fit in shared memory next to the K/V ring and the cache
+// spans at least one stage; otherwise the batch-1 chunked kernels
+// (scores, then p.v with a last-CTA combine) per (chunk, head, sequence).
+template <int G>
+cudaError_t launch_battention(const BatchDims &d, const BatchBuffers &b, const LayerWeights &w, cudaStream_t s) {
+  const size_t smem = attn_smem_bytes(G, d.max_seq);
+  const uint64_t rows = static_cast<uint64_t>(d.batch) * d.max_seq;
+  if (smem + 4096 <= static_cast<size_t>(smem_optin()) && rows >= kAttnPos) {
+    CUtensorMap mk, mv;
+    cudaError_t e = make_tmap_2d_u16(&mk, w.kcache, static_cast<uint64_t>(d.KVH) * kHD, rows,
+                                     static_cast<uint64_t>(d.KVH) * kHD, kHD, kAttnPos);
+    if (e != cudaSuccess) return e;
+    e = make_tmap_2d_u16(&mv, w.vcache, static_cast<uint64_t>(d.KVH) * kHD, rows, static_cast<uint64_t>(d.KVH) * kHD,
+                         kHD, kAttnPos);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(k_battn<G>, dim3(d.KVH, d.batch), dim3(kStreamThreads), smem, s, d, b, mk, mv);
+  }
+  const dim3 grid(d.nchunks, d.KVH, d.batch), block(kStreamThreads);
+  const cudaError_t e = launch_pdl(k_bscores<G>, grid, block, 0, s, d, b, w);
+  return e != cudaSuccess ? e : launch_pdl(k_bpv<G>, grid, block, 0, s, d, b, w);
+}
+
+}  // namespace
+
+uint32_t batch_gemm_grid() { return sm_count(); }
+
+uint32_t batch_max_tiles(const BatchDims &d) {
+  const uint32_t qkv = d.QH + 2 * d.KVH, o = (d.H + kTileM - 1) / kTileM, gu = (2 * d.I + kTileM - 1) / kTileM;
+  return std::max({qkv, o, gu, batch_lm_tiles(d.vocab)});
+}
+
+cudaError_t record_batch_step(const BatchDims &d, const BatchBuffers &b, const LayerWeights *layers,
+                              uint32_t n_layers, cudaStream_t s) {
+  if (d.batch < 1 || d.batch > kMaxBatch) return cudaErrorInvalidValue;
+  const uint32_t G = d.QH / d.KVH;
+  BGemm base{};
+  base.d = d;
+  base.b = b;
+#define XPU_TRY(expr)                        \
+  do {                                       \
+    const cudaError_t e_ = (expr);           \
+    if (e_ != cudaSuccess) return e_;        \
+  } while (0)
+  XPU_TRY(launch_pdl(k_bnorm, dim3(d.batch), dim3(256), 0, s, d, b, layers[0].in_norm, 1));
+  for (uint32_t l = 0; l < n_layers; ++l) {
+    const LayerWeights &w = layers[l];
+    if (l > 0) XPU_TRY(launch_pdl(k_bnorm, dim3(d.batch), dim3(256), 0, s, d, b, w.in_norm, 0));
+    BGemm pq = base;
+    pq.q_norm = w.q_norm;
+    pq.k_norm = w.k_norm;
+    pq.kcache = w.kcache;
+    pq.vcache = w.vcache;
+    XPU_TRY(launch_bgemm<kEpiQkv>(w.wqkv, (d.QH + 2 * d.KVH) * kHD, d.H, b.xn, pq, s));
+    switch (G) {
+      case 1: XPU_TRY(launch_battention<1>(d, b, w, s)); break;
+      case 2: XPU_TRY(launch_battention<2>(d, b, w, s)); break;
+      case 4: XPU_TRY(launch_battention<4>(d, b, w, s)); break;
+      case 8: XPU_TRY(launch_battention<8>(d, b, w, s)); break;
+      default: return cudaErrorInvalidValue;
+    }
+    BGemm po = base;
+    po.out = b.x;
+    XPU_TRY(launch_bgemm<kEpiResid>(w.wo, d.H, d.QH * kHD, b.attn, po, s));
+    XPU_TRY(launch_pdl(k_bnorm, dim3(d.batch), dim3(256), 0, s, d, b, w.post_norm, 0));
+    BGemm pg = base;
+    pg.out = b.h;
+    XPU_TRY(launch_bgemm<kEpiGateUp>(w.wgu, 2 * d.I, d.H, b.xn, pg, s));
+    BGemm pd = base;
+    pd.out = b.x;
+    XPU_TRY(launch_bgemm<kEpiResid>(w.wd, d.H, d.I, b.h, pd, s));
+  }
+  XPU_TRY(launch_pdl(k_bnorm, dim3(d.batch), dim3(256), 0, s, d, b, b.final_norm, 0));
+  XPU_TRY(launch_bgemm<kEpiLm>(b.lm_head, d.vocab, d.H, b.xn, base, s));
+  XPU_TRY(launch_pdl(k_bargmax, dim3(d.batch), dim3(256), 0, s, d, b, batch_lm_tiles(d.vocab)));
+#undef XPU_TRY
+  return cudaSuccess;
+}
+
+}  // namespace xpu

@@ -14,6 +14,10 @@
 // all-gathers the handles over its host process group and hands them to
 // tp_connect, which maps the peers' regions (NVLink peer access). The
 // persistent step kernel then exchanges partials through them.
+//
+// Batched decode (single GPU): an engine created with a batch capacity B
+// holds B sequences' KV caches and steps up to B of them at once through a
+// second CUDA graph (batch.cuh) over the same weights.
 #include <algorithm>
 #include <cmath>
 #include <stdexcept>
@@ -23,6 +27,7 @@
 #include <string>
 #include <vector>
 
+#include "batch.cuh"
 #include "decode.cuh"
 #include "xpu_internal.h"
 
@@ -83,8 +88,8 @@ struct Placement {
 class Qwen3Engine {
  public:
   Qwen3Engine(const xpu_qwen3_shape &shape, uint32_t max_seq, int device, uint32_t tp_rank,
-              uint32_t tp_size)
-      : shape_(shape), max_seq_(max_seq), device_(device), rank_(tp_rank), tp_(tp_size) {
+              uint32_t tp_size, uint32_t max_batch = 1)
+      : shape_(shape), max_seq_(max_seq), device_(device), rank_(tp_rank), tp_(tp_size), batch_cap_(max_batch) {
     validate();
     CK(cudaSetDevice(device_));
     CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
@@ -96,11 +101,13 @@ class Qwen3Engine {
   ~Qwen3Engine() {
     cudaSetDevice(device_);
     if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
+    if (batch_exec_) cudaGraphExecDestroy(batch_exec_);
     if (plan_) step_plan_destroy(plan_);
     if (stream_) cudaStreamSynchronize(stream_);
     for (void *p : peer_regions_) cudaIpcCloseMemHandle(p);
     for (void *p : allocations_) cudaFree(p);
     if (host_state_) cudaFreeHost(host_state_);
+    if (host_seq_) cudaFreeHost(host_seq_);
     if (stream_) cudaStreamDestroy(stream_);
   }
 
@@ -443,7 +450,236 @@ class Qwen3Engine {
     return w + kv * context;
   }
 
+  // ------------------------------------------------------ batched decode ----
+  uint32_t batch_capacity() const { return batch_cap_; }
+
+  // One step of sequences 0..n-1: tokens[s] at positions[s] (each sequence
+  // reads and writes its own KV cache); next[s] = its greedy token.
+  void batch_decode(uint32_t n, const uint32_t *tokens, const uint32_t *positions, uint32_t *next) {
+    check_batch(n);
+    for (uint32_t s = 0; s < n; ++s) {
+      if (positions[s] >= max_seq_)
+        throw InvalidArg("position " + std::to_string(positions[s]) + " >= maximum sequence " + std::to_string(max_seq_));
+      if (tokens[s] >= shape_.vocab_size) throw InvalidArg("token id outside the vocabulary");
+    }
+    ensure_batch(n);
+    for (uint32_t s = 0; s < n; ++s) host_seq_[s] = SeqState{tokens[s], positions[s], 0, 0};
+    write_batch_state(n);
+    CK(cudaGraphLaunch(batch_exec_, stream_));
+    read_batch_state(n);
+    after_batch_check();
+    for (uint32_t s = 0; s < n; ++s) next[s] = host_seq_[s].next;
+  }
+
+  // Device-resident prompts + greedy generation for n sequences: prompt s
+  // is lens[s] tokens (prompts holds them back to back); every step advances
+  // every sequence one position, for max(lens) + n_new - 1 steps, with one
+  // host synchronisation at the end. out[s * n_new + i] = generated token i
+  // of sequence s; counts[s] as generate() (stops after EOS when asked).
+  void batch_generate(uint32_t n, const uint32_t *prompts, const uint32_t *lens, uint32_t n_new, uint32_t *out,
+                      uint32_t *counts, bool stop_at_eos) {
+    check_batch(n);
+    uint32_t steps = 0;
+    uint64_t total = 0;
+    for (uint32_t s = 0; s < n; ++s) {
+      if (lens[s] == 0) throw InvalidArg("at least one prompt token is required per sequence");
+      if (static_cast<uint64_t>(lens[s]) + n_new > max_seq_)
+        throw InvalidArg("prompt plus generation exceeds the maximum sequence");
+      for (uint32_t i = 0; i < lens[s]; ++i)
+        if (prompts[total + i] >= shape_.vocab_size) throw InvalidArg("prompt token id outside the vocabulary");
+      total += lens[s];
+      steps = std::max(steps, n_new ? lens[s] + n_new - 1 : lens[s]);
+    }
+    ensure_batch(n);
+    uint64_t off = 0;
+    for (uint32_t s = 0; s < n; ++s) {
+      CK(cudaMemcpyAsync(bprompt_ + static_cast<uint64_t>(s) * max_seq_, prompts + off, lens[s] * 4ull,
+                         cudaMemcpyHostToDevice, stream_));
+      off += lens[s];
+      host_seq_[s] = SeqState{0, 0, lens[s], 0};
+    }
+    write_batch_state(n);
+    for (uint32_t i = 0; i < steps; ++i) CK(cudaGraphLaunch(batch_exec_, stream_));
+    std::vector<uint32_t> log(static_cast<size_t>(n) * max_seq_);
+    for (uint32_t s = 0; s < n; ++s)
+      CK(cudaMemcpyAsync(log.data() + static_cast<size_t>(s) * max_seq_, blog_ + static_cast<size_t>(s) * max_seq_,
+                         (lens[s] + n_new) * 4ull, cudaMemcpyDeviceToHost, stream_));
+    read_batch_state(n);
+    after_batch_check();
+    for (uint32_t s = 0; s < n; ++s) {
+      uint32_t count = 0;
+      for (uint32_t i = 0; i < n_new; ++i) {
+        const uint32_t t = log[static_cast<size_t>(s) * max_seq_ + lens[s] - 1 + i];
+        out[static_cast<size_t>(s) * n_new + count++] = t;
+        if (t == 0xffffffffu) break;
+        if (stop_at_eos && (t == 151645u || t == 151643u)) break;
+      }
+      counts[s] = count;
+    }
+  }
+
+  // Set sequences 0..n-1 (token, position) without running; enqueue_steps
+  // then advances them device-resident.
+  void batch_set_state(uint32_t n, const uint32_t *tokens, const uint32_t *positions) {
+    check_batch(n);
+    for (uint32_t s = 0; s < n; ++s)
+      if (positions[s] >= max_seq_ || tokens[s] >= shape_.vocab_size) throw InvalidArg("token or position out of range");
+    ensure_batch(n);
+    for (uint32_t s = 0; s < n; ++s) host_seq_[s] = SeqState{tokens[s], positions[s], 0, 0};
+    write_batch_state(n);
+    CK(cudaStreamSynchronize(stream_));
+  }
+
+  // Sequences 0..n-1 of the current batch: last greedy token and next position.
+  uint32_t batch_get_state(uint32_t n, uint32_t *tokens, uint32_t *positions) {
+    if (!batch_exec_ || n > batch_n_) throw InvalidArg("no batch of that size is set up");
+    read_batch_state(n);
+    for (uint32_t s = 0; s < n; ++s) {
+      if (tokens) tokens[s] = host_seq_[s].next;
+      if (positions) positions[s] = host_seq_[s].position;
+    }
+    return *host_berr_;
+  }
+
+  void batch_enqueue_steps(uint32_t steps, cudaStream_t stream) {
+    if (!batch_exec_) throw InvalidArg("no batch set up: call batch_set_state, batch_decode or batch_generate first");
+    cudaStream_t s = stream ? stream : stream_;
+    for (uint32_t i = 0; i < steps; ++i) CK(cudaGraphLaunch(batch_exec_, s));
+  }
+
+  void batch_logits(uint32_t seq, uint16_t *host, uint32_t count) {
+    if (seq >= batch_cap_) throw InvalidArg("sequence index outside the batch capacity");
+    if (!bb_.logits) throw InvalidArg("no batched step has run");
+    if (count > shape_.vocab_size) throw InvalidArg("logit count exceeds the vocabulary");
+    CK(cudaMemcpyAsync(host, bb_.logits + static_cast<size_t>(seq) * shape_.vocab_size, count * 2ull,
+                       cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+  }
+
+  // embed + norm, 8 per layer (no input norm on layer 0), final norm, lm_head, argmax
+  uint32_t batch_kernels_per_step() const { return 8 * shape_.num_hidden_layers + 3; }
+
+  // Bytes one batched step of n sequences must move: the weights once, plus
+  // every sequence's K and V over `context` positions.
+  uint64_t batch_bytes_per_step(uint32_t n, uint32_t context) const {
+    const uint64_t kv = 2ull * shape_.num_hidden_layers * shape_.num_key_value_heads * 128 * 2;
+    return bytes_per_token(0) + static_cast<uint64_t>(n) * kv * context;
+  }
+
  private:
+  void check_batch(uint32_t n) const {
+    if (tp_ > 1) throw InvalidArg("batched decode runs on one GPU (tp_size 1)");
+    if (n < 1 || n > batch_cap_)
+      throw InvalidArg("batch of " + std::to_string(n) + " sequences outside [1, " + std::to_string(batch_cap_) +
+                       "] (the engine's batch capacity)");
+  }
+
+  void write_batch_state(uint32_t n) {
+    *host_berr_ = 0;
+    CK(cudaMemcpyAsync(bb_.seq, host_seq_, n * sizeof(SeqState), cudaMemcpyHostToDevice, stream_));
+    CK(cudaMemcpyAsync(bb_.error, host_berr_, sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
+  }
+
+  void read_batch_state(uint32_t n) {
+    CK(cudaMemcpyAsync(host_seq_, bb_.seq, n * sizeof(SeqState), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaMemcpyAsync(host_berr_, bb_.error, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+  }
+
+  // A timed-out wait leaves arrival counters mid-count: clear them (and the
+  // error word) before reporting, so the next call starts clean.
+  void after_batch_check() {
+    const uint32_t err = *host_berr_;
+    if (err & 4u) {
+      CK(cudaMemsetAsync(bb_.cnt_tile, 0, batch_max_tiles(bd_) * sizeof(unsigned), stream_));
+      CK(cudaMemsetAsync(bb_.cnt_attn, 0, kMaxBatch * bd_.KVH * sizeof(unsigned), stream_));
+      CK(cudaMemsetAsync(bb_.error, 0, sizeof(uint32_t), stream_));
+      CK(cudaStreamSynchronize(stream_));
+      check_state_error(err);
+    }
+  }
+
+  template <typename T>
+  T *dev_zeros(uint64_t count) {
+    T *p = dev_alloc<T>(count);
+    CK(cudaMemset(p, 0, std::max<uint64_t>(count * sizeof(T), 16)));
+    return p;
+  }
+
+  void allocate_batch() {
+    CK(cudaSetDevice(device_));
+    const auto &s = shape_;
+    bd_ = BatchDims{};
+    bd_.H = s.hidden_size;
+    bd_.I = s.intermediate_size;
+    bd_.QH = s.num_attention_heads;
+    bd_.KVH = s.num_key_value_heads;
+    bd_.vocab = s.vocab_size;
+    bd_.max_seq = max_seq_;
+    bd_.nchunks = pos_chunks(max_seq_);
+    bd_.batch = 1;
+    bd_.eps = s.rms_norm_eps;
+    const uint64_t B = kMaxBatch, H = bd_.H, Q = bd_.QH * 128ull;
+    BatchBuffers b{};
+    b.x = dev_zeros<bf16>(B * H);
+    b.xn = dev_zeros<bf16>(B * H);
+    b.q = dev_zeros<bf16>(B * Q);
+    b.attn = dev_zeros<bf16>(B * Q);
+    b.h = dev_zeros<bf16>(B * bd_.I);
+    b.logits = dev_zeros<uint16_t>(B * bd_.vocab);
+    b.scores = dev_zeros<float>(B * bd_.QH * max_seq_);
+    b.stats = dev_zeros<float>(B * bd_.QH * bd_.nchunks * 2);
+    b.attn_part = dev_zeros<float>(B * Q * bd_.nchunks);
+    b.gemm_part = dev_zeros<float>(static_cast<uint64_t>(batch_gemm_grid()) * 2 * B * 128);
+    b.cnt_tile = dev_zeros<unsigned>(batch_max_tiles(bd_));
+    b.cnt_attn = dev_zeros<unsigned>(B * bd_.KVH);
+    b.cand = dev_zeros<ArgBest>(B * batch_lm_tiles(bd_.vocab));
+    b.cand_bad = dev_zeros<uint32_t>(B * batch_lm_tiles(bd_.vocab));
+    b.seq = dev_zeros<SeqState>(B);
+    b.error = dev_zeros<uint32_t>(1);
+    bprompt_ = dev_zeros<uint32_t>(B * max_seq_);
+    blog_ = dev_zeros<uint32_t>(B * max_seq_);
+    b.prompt = bprompt_;
+    b.log = blog_;
+    b.cos_t = reinterpret_cast<const bf16 *>(cos_);
+    b.sin_t = reinterpret_cast<const bf16 *>(sin_);
+    b.embed = reinterpret_cast<const bf16 *>(embed_);
+    b.final_norm = reinterpret_cast<const bf16 *>(final_norm_);
+    b.lm_head = reinterpret_cast<const bf16 *>(lm_head_);
+    b.kv_seq_stride = static_cast<uint64_t>(max_seq_) * bd_.KVH * 128;
+    bb_ = b;
+    CK(cudaMallocHost(&host_seq_, kMaxBatch * sizeof(SeqState) + 16));
+    host_berr_ = reinterpret_cast<uint32_t *>(host_seq_ + kMaxBatch);
+  }
+
+  // Builds (once per batch size) the batched step graph for n sequences.
+  void ensure_batch(uint32_t n) {
+    if (!loaded_) throw InvalidArg("no weights: call init_synthetic, load a checkpoint or set every tensor");
+    if (!bb_.x) allocate_batch();
+    if (batch_exec_ && batch_n_ == n) return;
+    CK(cudaSetDevice(device_));
+    CK(cudaStreamSynchronize(stream_));
+    if (batch_exec_) {
+      CK(cudaGraphExecDestroy(batch_exec_));
+      batch_exec_ = nullptr;
+    }
+    bd_.batch = n;
+    std::vector<LayerWeights> lw(shape_.num_hidden_layers);
+    for (uint32_t l = 0; l < shape_.num_hidden_layers; ++l) lw[l] = layer_weights(l);
+    cudaGraph_t graph = nullptr;
+    CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    const cudaError_t rec = record_batch_step(bd_, bb_, lw.data(), shape_.num_hidden_layers, stream_);
+    const cudaError_t end = cudaStreamEndCapture(stream_, &graph);
+    if (rec != cudaSuccess || end != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      CK(rec != cudaSuccess ? rec : end);
+    }
+    const cudaError_t e = cudaGraphInstantiate(&batch_exec_, graph, 0);
+    cudaGraphDestroy(graph);
+    CK(e);
+    batch_n_ = n;
+  }
+
   struct Layer {
     uint16_t *in_norm, *post_norm, *q_norm, *k_norm, *wqkv, *wo, *wgu, *wd, *kcache, *vcache;
   };
@@ -486,6 +722,8 @@ class Qwen3Engine {
         "heads must divide evenly across tensor-parallel ranks");
     req(s.intermediate_size % (64 * tp_) == 0, "intermediate_size / tp must be a multiple of 64");
     req(s.vocab_size % tp_ == 0 && (s.vocab_size / tp_) % 2 == 0, "vocabulary must split evenly");
+    req(batch_cap_ >= 1 && batch_cap_ <= kMaxBatch, "batch capacity must be in [1, 16]");
+    req(tp_ == 1 || batch_cap_ == 1, "batched decode runs on one GPU (tp_size 1)");
   }
 
   void plan() {
@@ -551,7 +789,9 @@ class Qwen3Engine {
     for (size_t i = 0; i < items.size(); ++i) *items[i].slot = reinterpret_cast<uint16_t *>(arena + offsets[i]);
     if (s.tie_word_embeddings) lm_head_ = embed_ + static_cast<uint64_t>(d_.v_offset) * H;
 
-    const uint64_t cache_layer = static_cast<uint64_t>(max_seq_) * kvr;
+    // [batch capacity][max_seq][kv heads][128] per layer; sequence 0 is the
+    // batch-1 path's cache.
+    const uint64_t cache_layer = static_cast<uint64_t>(batch_cap_) * max_seq_ * kvr;
     uint16_t *kc = dev_alloc<uint16_t>(cache_layer * L), *vc = dev_alloc<uint16_t>(cache_layer * L);
     CK(cudaMemset(kc, 0, cache_layer * L * 2));
     CK(cudaMemset(vc, 0, cache_layer * L * 2));
@@ -737,6 +977,15 @@ class Qwen3Engine {
   uint8_t *xregion_ = nullptr;            // this rank's exchange region (tp_size > 1)
   std::vector<void *> peer_regions_;      // peers' regions mapped through CUDA IPC
   bool connected_ = false, broken_ = false;
+  // batched decode
+  uint32_t batch_cap_ = 1;
+  BatchDims bd_{};
+  BatchBuffers bb_{};
+  cudaGraphExec_t batch_exec_ = nullptr;
+  uint32_t batch_n_ = 0;
+  uint32_t *bprompt_ = nullptr, *blog_ = nullptr;
+  SeqState *host_seq_ = nullptr;
+  uint32_t *host_berr_ = nullptr;
 };
 
 }  // namespace xpu
@@ -784,6 +1033,17 @@ int xpu_qwen3_create(const xpu_qwen3_shape *shape, uint32_t maximum_sequence, in
     *out = nullptr;
     auto holder = std::make_unique<xpu_qwen3_engine>();
     holder->impl = std::make_unique<Qwen3Engine>(*shape, maximum_sequence, device, tp_rank, tp_size);
+    *out = holder.release();
+  });
+}
+
+int xpu_qwen3_create_batched(const xpu_qwen3_shape *shape, uint32_t maximum_sequence, int device,
+                             uint32_t max_batch, xpu_qwen3_engine **out) {
+  return guarded([&] {
+    if (!shape || !out) throw xpu::InvalidArg("xpu_qwen3_create_batched: null pointer");
+    *out = nullptr;
+    auto holder = std::make_unique<xpu_qwen3_engine>();
+    holder->impl = std::make_unique<Qwen3Engine>(*shape, maximum_sequence, device, 0, 1, max_batch);
     *out = holder.release();
   });
 }
@@ -902,6 +1162,72 @@ int xpu_qwen3_set_mode(xpu_qwen3_engine *engine, int mode) {
 
 int xpu_qwen3_synchronize(xpu_qwen3_engine *engine) {
   return guarded([&] { eng(engine).sync(); });
+}
+
+int xpu_qwen3_batch_decode(xpu_qwen3_engine *engine, uint32_t batch, const uint32_t *tokens,
+                           const uint32_t *positions, uint32_t *next_tokens) {
+  int status = guarded([&] {
+    if (!tokens || !positions || !next_tokens) throw xpu::InvalidArg("xpu_qwen3_batch_decode: null pointer");
+    eng(engine).batch_decode(batch, tokens, positions, next_tokens);
+  });
+  if (status == XPU_OK)
+    for (uint32_t s = 0; s < batch; ++s)
+      if (next_tokens[s] == 0xffffffffu)
+        return xpu::fail(XPU_ERR_NONFINITE, "model produced a NaN or infinity in vocabulary logits");
+  return status;
+}
+
+int xpu_qwen3_batch_generate(xpu_qwen3_engine *engine, uint32_t batch, const uint32_t *prompts,
+                             const uint32_t *prompt_lens, uint32_t max_new_tokens, int stop_at_eos,
+                             uint32_t *out_tokens, uint32_t *out_counts) {
+  int status = guarded([&] {
+    if (!prompts || !prompt_lens || !out_counts || (max_new_tokens && !out_tokens))
+      throw xpu::InvalidArg("xpu_qwen3_batch_generate: null pointer");
+    eng(engine).batch_generate(batch, prompts, prompt_lens, max_new_tokens, out_tokens, out_counts,
+                               stop_at_eos != 0);
+  });
+  if (status == XPU_OK)
+    for (uint32_t s = 0; s < batch; ++s)
+      if (out_counts[s] && out_tokens[static_cast<size_t>(s) * max_new_tokens + out_counts[s] - 1] == 0xffffffffu)
+        return xpu::fail(XPU_ERR_NONFINITE, "model produced a NaN or infinity in vocabulary logits");
+  return status;
+}
+
+int xpu_qwen3_batch_set_state(xpu_qwen3_engine *engine, uint32_t batch, const uint32_t *tokens,
+                              const uint32_t *positions) {
+  return guarded([&] {
+    if (!tokens || !positions) throw xpu::InvalidArg("xpu_qwen3_batch_set_state: null pointer");
+    eng(engine).batch_set_state(batch, tokens, positions);
+  });
+}
+
+int xpu_qwen3_batch_get_state(xpu_qwen3_engine *engine, uint32_t batch, uint32_t *tokens, uint32_t *positions,
+                              uint32_t *error) {
+  return guarded([&] {
+    const uint32_t e = eng(engine).batch_get_state(batch, tokens, positions);
+    if (error) *error = e;
+  });
+}
+
+int xpu_qwen3_batch_enqueue_steps(xpu_qwen3_engine *engine, uint32_t steps, void *stream) {
+  return guarded([&] { eng(engine).batch_enqueue_steps(steps, static_cast<cudaStream_t>(stream)); });
+}
+
+int xpu_qwen3_batch_logits(xpu_qwen3_engine *engine, uint32_t sequence, uint16_t *host_out, uint32_t count) {
+  return guarded([&] {
+    if (!host_out) throw xpu::InvalidArg("xpu_qwen3_batch_logits: null pointer");
+    eng(engine).batch_logits(sequence, host_out, count);
+  });
+}
+
+uint64_t xpu_qwen3_batch_bytes_per_step(xpu_qwen3_engine *engine, uint32_t batch, uint32_t context) {
+  if (!engine || !engine->impl) return 0;
+  return engine->impl->batch_bytes_per_step(batch, context);
+}
+
+uint32_t xpu_qwen3_batch_kernels_per_step(xpu_qwen3_engine *engine) {
+  if (!engine || !engine->impl) return 0;
+  return engine->impl->batch_kernels_per_step();
 }
 
 }  // extern "C"

@@ -40,6 +40,7 @@
 
 #include "common.cuh"
 #include "stream.cuh"
+#include "tcgen05.cuh"
 #include "xpu_internal.h"
 
 namespace xpu {
@@ -64,9 +65,6 @@ constexpr int kEpilogueWarps = 8;
 constexpr int kGemmThreads = 64 + 32 * kEpilogueWarps;
 constexpr unsigned kErrGemmTimeout = 1u;
 
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -86,17 +84,6 @@ __device__ __forceinline__ uint32_t cluster_addr(const void *p, uint32_t rank) {
 
 __device__ __forceinline__ void remote_arrive(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
-}
-
-// Shared-memory matrix descriptor: 128-byte swizzle, version 1 (sm_100).
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
-  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
-  d |= static_cast<uint64_t>(1) << 46;  // version
-  d |= static_cast<uint64_t>(2) << 61;  // SWIZZLE_128B
-  return d;
 }
 
 // Instruction descriptor, kind::f16: FP32 accumulator, A K-major, B MN-major.

@@ -61,13 +61,19 @@ def validate_checkpoint(model_dir: str) -> tuple[Qwen3Shape, int]:
 
 class Qwen3Engine:
     def __init__(self, shape: Qwen3Shape, max_seq: int, device: int = 0, tp_rank: int = 0,
-                 tp_size: int = 1, mode: str | None = None):
+                 tp_size: int = 1, mode: str | None = None, max_batch: int = 1):
         self.lib = _lib.load()
-        self.shape, self.max_seq = shape, max_seq
+        self.shape, self.max_seq, self.max_batch = shape, max_seq, max_batch
         self._h = ctypes.c_void_p()
         self._shape_c = shape_struct(shape)
-        _lib.check(self.lib.xpu_qwen3_create(ctypes.byref(self._shape_c), max_seq, device, tp_rank,
-                                             tp_size, ctypes.byref(self._h)))
+        if max_batch != 1:
+            if tp_size != 1:
+                raise ValueError("batched decode runs on one GPU (tp_size 1)")
+            _lib.check(self.lib.xpu_qwen3_create_batched(ctypes.byref(self._shape_c), max_seq, device,
+                                                         max_batch, ctypes.byref(self._h)))
+        else:
+            _lib.check(self.lib.xpu_qwen3_create(ctypes.byref(self._shape_c), max_seq, device, tp_rank,
+                                                 tp_size, ctypes.byref(self._h)))
         if mode is not None:
             self.set_mode(mode)
 
@@ -171,3 +177,57 @@ class Qwen3Engine:
 
     def bytes_per_token(self, context: int) -> int:
         return int(self.lib.xpu_qwen3_bytes_per_token(self._h, context))
+
+    # ----------------------------------------------------- batched decode ----
+    def batch_decode(self, tokens: list[int], positions: list[int]) -> list[int]:
+        """One step of len(tokens) sequences (xpu_qwen3_batch_decode)."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(positions, dtype=np.uint32)
+        if t.size != p.size:
+            raise ValueError("one position per token")
+        out = np.zeros(t.size, np.uint32)
+        _lib.check(self.lib.xpu_qwen3_batch_decode(self._h, t.size, t.ctypes.data, p.ctypes.data,
+                                                   out.ctypes.data))
+        return [int(x) for x in out]
+
+    def batch_generate(self, prompts: list[list[int]], max_new_tokens: int,
+                       stop_at_eos: bool = False) -> list[list[int]]:
+        """Device-resident prompts + greedy generation for len(prompts) sequences."""
+        lens = np.ascontiguousarray([len(p) for p in prompts], dtype=np.uint32)
+        flat = np.ascontiguousarray([t for p in prompts for t in p] or [0], dtype=np.uint32)
+        out = np.zeros(max(1, len(prompts) * max_new_tokens), np.uint32)
+        counts = np.zeros(len(prompts), np.uint32)
+        _lib.check(self.lib.xpu_qwen3_batch_generate(self._h, len(prompts), flat.ctypes.data, lens.ctypes.data,
+                                                     max_new_tokens, int(stop_at_eos), out.ctypes.data,
+                                                     counts.ctypes.data))
+        return [[int(x) for x in out[s * max_new_tokens: s * max_new_tokens + counts[s]]]
+                for s in range(len(prompts))]
+
+    def batch_set_state(self, tokens: list[int], positions: list[int]) -> None:
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(positions, dtype=np.uint32)
+        if t.size != p.size:
+            raise ValueError("one position per token")
+        _lib.check(self.lib.xpu_qwen3_batch_set_state(self._h, t.size, t.ctypes.data, p.ctypes.data))
+
+    def batch_enqueue_steps(self, steps: int, stream: int | None = None) -> None:
+        _lib.check(self.lib.xpu_qwen3_batch_enqueue_steps(self._h, steps, stream))
+
+    def batch_state(self, batch: int) -> tuple[list[int], list[int], int]:
+        tok = np.zeros(batch, np.uint32)
+        pos = np.zeros(batch, np.uint32)
+        err = ctypes.c_uint32()
+        _lib.check(self.lib.xpu_qwen3_batch_get_state(self._h, batch, tok.ctypes.data, pos.ctypes.data,
+                                                      ctypes.byref(err)))
+        return [int(x) for x in tok], [int(x) for x in pos], err.value
+
+    def batch_logits(self, sequence: int) -> np.ndarray:
+        out = np.empty(self.shape.vocab, np.uint16)
+        _lib.check(self.lib.xpu_qwen3_batch_logits(self._h, sequence, out.ctypes.data, out.size))
+        return out
+
+    def batch_bytes_per_step(self, batch: int, context: int) -> int:
+        return int(self.lib.xpu_qwen3_batch_bytes_per_step(self._h, batch, context))
+
+    def batch_kernels_per_step(self) -> int:
+        return int(self.lib.xpu_qwen3_batch_kernels_per_step(self._h))
