@@ -322,6 +322,14 @@ int xpu_qwen3_batch_logits(xpu_qwen3_engine *engine, uint32_t sequence, uint16_t
  * sequence's K/V over `context` positions. */
 uint64_t xpu_qwen3_batch_bytes_per_step(xpu_qwen3_engine *engine, uint32_t batch, uint32_t context);
 uint32_t xpu_qwen3_batch_kernels_per_step(xpu_qwen3_engine *engine);
+/* Batched-step tracing (when the process runs with XPU_BATCH_TRACE=1): per
+ * kernel of the step, in launch order, 8 globaltimer values (ns): first CTA
+ * start, last return from the wait on the previous kernel, last CTA end,
+ * first return from that wait, last CTA start, and for the GEMMs the last
+ * CTA's first landed stage, final accumulator and epilogue end; over all
+ * steps since the previous call, which it resets. *count = values written
+ * (0 when tracing is off). */
+int xpu_qwen3_batch_trace(xpu_qwen3_engine *engine, uint64_t *host_ns, uint32_t capacity, uint32_t *count);
 
 #ifdef __cplusplus
 }

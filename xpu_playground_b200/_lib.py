@@ -99,6 +99,7 @@ SIGNATURES: dict[str, tuple] = {
     "xpu_qwen3_batch_logits": (i32, [vp, u32, vp, u32]),
     "xpu_qwen3_batch_bytes_per_step": (u64, [vp, u32, u32]),
     "xpu_qwen3_batch_kernels_per_step": (u32, [vp]),
+    "xpu_qwen3_batch_trace": (i32, [vp, vp, u32, vp]),
 }
 
 

@@ -13,16 +13,17 @@
 // kernels; the GEMMs prefetch weights before waiting on their input):
 //   embed_norm                 x[s] = embed[token s], xn[s] = RMSNorm(x[s])
 //   per layer:
-//     (norm)                   xn = RMSNorm(x) with input_layernorm (l > 0)
-//     gemm qkv                 per head tile: q/k RMSNorm + RoPE at the
-//                              sequence's position -> q, key cache; v -> value cache
-//     scores, pv               per (chunk, kv head, sequence) as batch 1
-//     gemm o_proj              x = bf16(x + bf16(attn . Wo^T))
-//     norm                     xn = RMSNorm(x) with post_attention_layernorm
-//     gemm gate/up             h = bf16(bf16(silu(bf16 g)) * bf16 u)
-//     gemm down                x = bf16(x + bf16(h . Wd^T))
-//   norm                       xn = RMSNorm(x) with the final norm
-//   gemm lm_head               bf16 logits, per-tile (max, lowest index)
+//     gemm qkv                 operand RMSNorm(x) with input_layernorm (inside
+//                              the GEMM for l > 0) -> raw bf16 q/k/v
+//     attention                per (kv head, sequence): the group's q/k
+//                              RMSNorm + RoPE at the sequence's position, k/v
+//                              into the caches, scores, softmax, p.v
+//     gemm o_proj              x = bf16(x + bf16(attn . Wo^T)), per-tile sums of x^2
+//     gemm gate/up             operand RMSNorm(x) with post_attention_layernorm;
+//                              h = bf16(bf16(silu(bf16 g)) * bf16 u)
+//     gemm down                x = bf16(x + bf16(h . Wd^T)), per-tile sums of x^2
+//   gemm lm_head               operand RMSNorm(x) with the final norm; bf16
+//                              logits, per-tile (max, lowest index)
 //   argmax                     per sequence: greedy token, state update
 //
 // HBM layout: weights are the batch-1 engine's (one arena). Activations are
@@ -57,12 +58,14 @@ struct BatchDims {
   uint32_t nchunks;        // attention position chunks of max_seq
   uint32_t batch;          // active sequences (1..16)
   float eps;
+  uint32_t trace_slot;     // this launch's slot in BatchBuffers::trace
 };
 
 struct BatchBuffers {
   bf16 *x;              // [16][H] residual stream
   bf16 *xn;             // [16][H] normalised activations (GEMM operand)
-  bf16 *q;              // [16][QH * 128]
+  bf16 *qkv;            // [16][(QH + 2 KVH) * 128] raw q/k/v (QKV GEMM output)
+  bf16 *q;              // [16][QH * 128] finished q (chunked-attention path)
   bf16 *attn;           // [16][QH * 128] attention output (GEMM operand)
   bf16 *h;              // [16][I] SwiGLU output (GEMM operand)
   uint16_t *logits;     // [16][vocab] bf16 bits
@@ -70,6 +73,7 @@ struct BatchBuffers {
   float *stats;         // [16][QH][nchunks][2]
   float *attn_part;     // [16][QH][nchunks][128]
   float *gemm_part;     // [grid][2][16][128] split-tile partial sums
+  float *ssq;           // [H / 128][16] per-tile sums of x^2 of the residual (RMSNorm input)
   unsigned *cnt_tile;   // [max tiles] split-tile arrival counters
   unsigned *cnt_attn;   // [16][KVH] attention chunk arrivals
   ArgBest *cand;        // [16][lm tiles] per-tile argmax candidates
@@ -83,7 +87,13 @@ struct BatchBuffers {
   const bf16 *final_norm;  // [H]
   const bf16 *lm_head;     // [vocab][H]
   uint64_t kv_seq_stride;  // elements between two sequences' caches of one layer
+  // Step tracing (XPU_BATCH_TRACE=1, else null): per kernel of the step
+  // [slot][8] globaltimer ns (see trace_mark in batch_step.cu).
+  unsigned long long *trace;
 };
+
+constexpr uint32_t kBatchTraceSlots = 512;
+constexpr uint32_t kBatchTraceValues = 8;
 
 // Number of 128-row tiles of the lm_head GEMM (sizes cand / cand_bad).
 inline uint32_t batch_lm_tiles(uint32_t vocab) { return (vocab + 127) / 128; }

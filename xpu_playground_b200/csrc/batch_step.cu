@@ -39,6 +39,14 @@
 //   warps 2-5  epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31, i.e.
 //              weight rows, and all 16 sequence columns of the 4
 //              accumulators, summed in accumulator order.
+//   warps 6-7  (normalising GEMMs: QKV of layers > 0, gate/up, lm_head)
+//              RMSNorm of the activation operand in place: the operand is
+//              the raw residual x; per sequence r = 1/sqrt(mean(x^2) + eps)
+//              from the per-tile sums of squares the residual GEMM epilogue
+//              published (tiles in order), and every landed activation box
+//              becomes bf16(w * bf16(x * r)) (the transformers rounding)
+//              in its swizzled shared-memory place before the MMA warp may
+//              read it. This replaces a separate norm kernel per GEMM.
 //
 // Waits are bounded; a timeout sets bit 4 of the batch error word and every
 // role leaves its loop, waiting (bounded) for its own copies and MMAs.
@@ -69,7 +77,7 @@ constexpr uint32_t kBoxes = 4;                         // K blocks per stage (at
 constexpr uint32_t kStageW = kBoxes * kWBytes;          // 64 KB
 constexpr uint32_t kStageBytes = kStageW + kBoxes * kXBytes;  // 72 KB (1024-byte multiple)
 constexpr uint32_t kRing = 3;
-constexpr uint32_t kGemmThreads = 192;
+constexpr uint32_t kGemmThreads = 256;
 constexpr uint32_t kAccs = kKb / 16;                   // accumulators per buffer: one per MMA of a K block
 constexpr uint32_t kAccCols = kSeqN;                   // TMEM columns of one accumulator
 constexpr uint32_t kBufCols = kAccs * kAccCols;        // 64 columns per buffer
@@ -85,14 +93,14 @@ struct BGemm {
   uint32_t rows, nk, tiles, total;  // weight rows, K blocks per tile, tiles, tiles * nk
   BatchDims d;
   BatchBuffers b;
-  bf16 *out;                    // residual x (kEpiResid) or h (kEpiGateUp)
-  const bf16 *q_norm, *k_norm;  // kEpiQkv
-  bf16 *kcache, *vcache;        // kEpiQkv: this layer's caches (sequence 0)
+  bf16 *out;                    // residual x (kEpiResid), h (kEpiGateUp) or raw qkv (kEpiQkv)
+  const bf16 *norm_w;           // normalising GEMMs: the RMSNorm weight of the operand
 };
 
 struct EpiShared {
   uint16_t vals[kSeqN][kTileM];  // bf16 bits
   float red[4][kSeqN];
+  float ssq[2][4][kSeqN];        // residual epilogue, alternating per tile
   ArgBest best[4][kSeqN];
   uint32_t bad[4][kSeqN];
 };
@@ -107,6 +115,20 @@ __host__ __device__ inline uint32_t range_owner(uint32_t kb, uint32_t total, uin
 
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
 
+// Step tracing, per launch [slot][8] globaltimer ns: 0 first CTA start,
+// 1 last wait return, 2 last CTA end, 3 first wait return, 4 last CTA start,
+// 5 last first-stage arrival, 6 last final accumulator, 7 last epilogue end.
+// what: 0 start, 1 wait returned, 2 end, 5, 6, 7 as above (max over CTAs).
+__device__ __forceinline__ void trace_mark(const BatchDims &d, const BatchBuffers &b, int what) {
+  if (!b.trace) return;
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  unsigned long long *slot = b.trace + static_cast<size_t>(d.trace_slot) * kBatchTraceValues;
+  if (what == 0) { atomicMin(slot, t); atomicMax(slot + 4, t); }
+  if (what == 1) { atomicMax(slot + 1, t); atomicMin(slot + 3, t); }
+  if (what == 2 || what >= 5) atomicMax(slot + what, t);
+}
+
 __device__ __forceinline__ float bfv(const bf16 *p, size_t i) {
   return bf16_bits_to_float(reinterpret_cast<const uint16_t *>(p)[i]);
 }
@@ -114,71 +136,59 @@ __device__ __forceinline__ void putv(bf16 *p, size_t i, float v) {
   reinterpret_cast<uint16_t *>(p)[i] = float_to_bf16_bits(v);
 }
 
-// ---- epilogues: thread = weight row r of tile t, v[s] = FP32 sum for sequence s ----
-
-// Tile t is head t of [q; k; v]: q/k RMSNorm (weight, eps) and RoPE at each
-// sequence's position into q / the key cache, v into the value cache
-// (transformers rounding points, as the batch-1 head epilogue).
-__device__ inline void epi_qkv(const BGemm &p, uint32_t t, uint32_t r, const float (&v)[kSeqN], EpiShared &es) {
-  const BatchDims &d = p.d;
-  const uint32_t lane = threadIdx.x & 31, quarter = (threadIdx.x >> 5) & 3;
-  const bool is_q = t < d.QH, is_v = t >= d.QH + d.KVH;
-  // Every input of the epilogue is loaded before any store (one round trip).
-  uint32_t pos[kSeqN];
+// Transpose reduction: lane l holds V partial sums; afterwards lane l
+// holds the warp-wide sums of values [l V / 32, (l + 1) V / 32) in val[0..]
+// (for V < 32 lanes that share a value hold identical sums).
+template <int V>
+__device__ __forceinline__ void warp_transpose_sum(float (&val)[V], uint32_t lane) {
 #pragma unroll
-  for (uint32_t s = 0; s < kSeqN; ++s) pos[s] = s < d.batch ? p.b.seq[s].position : 0u;
-  if (is_v) {
-    const uint32_t kvh = t - d.QH - d.KVH;
+  for (int k = 0; k < 5; ++k) {
+    const int o = 16 >> k, half = V >> (k + 1);
+    if (half >= 1) {
+      const bool upper = (lane & o) != 0;
 #pragma unroll
-    for (uint32_t s = 0; s < kSeqN; ++s)
-      if (s < d.batch)
-        putv(p.vcache + s * p.b.kv_seq_stride, (static_cast<size_t>(pos[s]) * d.KVH + kvh) * kHD + r, v[s]);
-    return;
+      for (int i = 0; i < half; ++i) {
+        const float send = upper ? val[i] : val[i + half];
+        const float keep = upper ? val[i + half] : val[i];
+        val[i] = keep + __shfl_xor_sync(kFullMask, send, o);
+      }
+    } else {
+      val[0] += __shfl_xor_sync(kFullMask, val[0], o);
+    }
   }
-  float cs[kSeqN], sn[kSeqN];
-#pragma unroll
-  for (uint32_t s = 0; s < kSeqN; ++s) {
-    cs[s] = s < d.batch ? bfv(p.b.cos_t, static_cast<size_t>(pos[s]) * kHD + r) : 0.f;
-    sn[s] = s < d.batch ? bfv(p.b.sin_t, static_cast<size_t>(pos[s]) * kHD + r) : 0.f;
-  }
-  float val[kSeqN];
-#pragma unroll
-  for (uint32_t s = 0; s < kSeqN; ++s) {
-    val[s] = round_bf16(v[s]);
-    const float sq = warp_sum(__fmul_rn(val[s], val[s]));
-    if (lane == 0) es.red[quarter][s] = sq;
-  }
-  epi_sync();
-  const float nw = bfv(is_q ? p.q_norm : p.k_norm, r);
-#pragma unroll
-  for (uint32_t s = 0; s < kSeqN; ++s) {
-    const float ss = ((es.red[0][s] + es.red[1][s]) + es.red[2][s]) + es.red[3][s];
-    const float rs = 1.0f / sqrtf(ss / static_cast<float>(kHD) + d.eps);
-    es.vals[s][r] = float_to_bf16_bits(__fmul_rn(nw, round_bf16(__fmul_rn(val[s], rs))));
-  }
-  epi_sync();
-#pragma unroll
-  for (uint32_t s = 0; s < kSeqN; ++s) {
-    if (s >= d.batch) break;
-    const float a = bf16_bits_to_float(es.vals[s][r]), o = bf16_bits_to_float(es.vals[s][r ^ 64]);
-    const float rot = r < 64 ? round_bf16(__fmul_rn(-o, sn[s])) : round_bf16(__fmul_rn(o, sn[s]));
-    const float out = round_bf16(__fadd_rn(round_bf16(__fmul_rn(a, cs[s])), rot));
-    bf16 *dst = is_q ? p.b.q + (static_cast<size_t>(s) * d.QH + t) * kHD
-                     : p.kcache + s * p.b.kv_seq_stride + (static_cast<size_t>(pos[s]) * d.KVH + (t - d.QH)) * kHD;
-    putv(dst, r, out);
-  }
-  epi_sync();  // es is reused by the next tile
 }
 
-// x[s][row] = bf16(x[s][row] + bf16(sum)).
-__device__ inline void epi_resid(const BGemm &p, uint32_t row, const float (&v)[kSeqN]) {
+// ---- epilogues: thread = weight row r of tile t, v[s] = FP32 sum for sequence s ----
+
+// Raw q/k/v: qkv[s][row] = bf16(sum); the per-head RMSNorm, RoPE and
+// cache writes run in the attention kernel, whose CTA owns the head group.
+__device__ inline void epi_qkv(const BGemm &p, uint32_t row, const float (&v)[kSeqN]) {
   if (row >= p.rows) return;
-  float x[kSeqN];  // every residual loaded before any store (one round trip)
-#pragma unroll
-  for (uint32_t s = 0; s < kSeqN; ++s) x[s] = s < p.d.batch ? bfv(p.out, static_cast<size_t>(s) * p.rows + row) : 0.f;
 #pragma unroll
   for (uint32_t s = 0; s < kSeqN; ++s)
-    if (s < p.d.batch) putv(p.out, static_cast<size_t>(s) * p.rows + row, __fadd_rn(x[s], round_bf16(v[s])));
+    if (s < p.d.batch) putv(p.out, static_cast<size_t>(s) * p.rows + row, v[s]);
+}
+
+// x[s][row] = bf16(x[s][row] + bf16(sum)) with x[s][row] preloaded in xr;
+// the tile's sum of x^2 per sequence (lanes by a transpose reduction, then
+// quarters in order) goes to ssq[tile][s] for the next normalising GEMM.
+// `par` alternates per call so one barrier suffices.
+__device__ inline void epi_resid(const BGemm &p, uint32_t t, uint32_t row, const float (&v)[kSeqN],
+                                 const float (&xr)[kSeqN], EpiShared &es, uint32_t par) {
+  const uint32_t lane = threadIdx.x & 31, quarter = (threadIdx.x >> 5) & 3, et = threadIdx.x - 64;
+  const bool ok = row < p.rows;
+  float sq[kSeqN];
+#pragma unroll
+  for (uint32_t s = 0; s < kSeqN; ++s) {
+    const float xn = round_bf16(__fadd_rn(xr[s], round_bf16(v[s])));
+    if (ok && s < p.d.batch) putv(p.out, static_cast<size_t>(s) * p.rows + row, xn);
+    sq[s] = ok ? __fmul_rn(xn, xn) : 0.f;
+  }
+  warp_transpose_sum<kSeqN>(sq, lane);  // lanes 2s, 2s + 1: the warp's sum for sequence s
+  if ((lane & 1) == 0) es.ssq[par][quarter][lane / 2] = sq[0];
+  epi_sync();
+  if (et < kSeqN)
+    p.b.ssq[t * kSeqN + et] = ((es.ssq[par][0][et] + es.ssq[par][1][et]) + es.ssq[par][2][et]) + es.ssq[par][3][et];
 }
 
 // Rows 2i, 2i + 1 are gate and up of unit i (adjacent lanes of one warp):
@@ -224,10 +234,10 @@ __device__ inline void epi_lm(const BGemm &p, uint32_t t, uint32_t row, const fl
 
 template <int EPI>
 __device__ __forceinline__ void run_epilogue(const BGemm &p, uint32_t t, uint32_t r, const float (&v)[kSeqN],
-                                             EpiShared &es) {
+                                             const float (&xr)[kSeqN], EpiShared &es, uint32_t par) {
   const uint32_t row = t * kTileM + r;
-  if (EPI == kEpiQkv) epi_qkv(p, t, r, v, es);
-  if (EPI == kEpiResid) epi_resid(p, row, v);
+  if (EPI == kEpiQkv) epi_qkv(p, row, v);
+  if (EPI == kEpiResid) epi_resid(p, t, row, v, xr, es, par);
   if (EPI == kEpiGateUp) epi_gateup(p, row, v);
   if (EPI == kEpiLm) epi_lm(p, t, row, v, es);
 }
@@ -241,11 +251,54 @@ __device__ __forceinline__ uint32_t stage_end(uint32_t kb, uint32_t kb1, uint32_
   return min(min(kb + kBoxes, kb1), tile_end);
 }
 
-template <int EPI>
+// Round two floats to bf16 (RNE) and pack them: lo in the low half.
+__device__ __forceinline__ uint32_t pack2_rn(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+// bf16(w * bf16(x * r)) for the two bf16 of x and w in one word each.
+__device__ __forceinline__ uint32_t norm_word(uint32_t x, uint32_t w, float r) {
+  const uint32_t t = pack2_rn(__fmul_rn(bf16_lo(x), r), __fmul_rn(bf16_hi(x), r));
+  return pack2_rn(__fmul_rn(bf16_lo(w), bf16_lo(t)), __fmul_rn(bf16_hi(w), bf16_hi(t)));
+}
+
+// RMSNorm of the activation boxes of one stage in place (transform warps,
+// 64 threads): thread u owns logical 16-byte chunk u % 8 of rows 2 (u / 8)
+// and 2 (u / 8) + 1 of each box; the 128-byte swizzle stores chunk j of row
+// s at chunk j ^ (s % 8). Every load of the stage is issued before any math.
+__device__ inline void norm_stage(uint8_t *xs, uint32_t kb, uint32_t e, uint32_t nk, const bf16 *w, const float *rs,
+                                  uint32_t u) {
+  const uint32_t j = u % 8, s0 = 2 * (u / 8), nb = e - kb;
+  uint4 wv[kBoxes], xv[kBoxes][2];
+#pragma unroll
+  for (uint32_t b = 0; b < kBoxes; ++b)
+    if (b < nb) {
+      wv[b] = ld_ro16(w + ((kb + b) % nk) * kKb + j * 8);
+#pragma unroll
+      for (uint32_t q = 0; q < 2; ++q)
+        xv[b][q] = *reinterpret_cast<const uint4 *>(xs + b * kXBytes + (s0 + q) * 128 + ((j ^ ((s0 + q) & 7)) * 16));
+    }
+  const float r0 = rs[s0], r1 = rs[s0 + 1];
+#pragma unroll
+  for (uint32_t b = 0; b < kBoxes; ++b)
+    if (b < nb)
+#pragma unroll
+      for (uint32_t q = 0; q < 2; ++q) {
+        const float r = q ? r1 : r0;
+        const uint4 x = xv[b][q], wq = wv[b];
+        *reinterpret_cast<uint4 *>(xs + b * kXBytes + (s0 + q) * 128 + ((j ^ ((s0 + q) & 7)) * 16)) =
+            make_uint4(norm_word(x.x, wq.x, r), norm_word(x.y, wq.y, r), norm_word(x.z, wq.z, r),
+                       norm_word(x.w, wq.w, r));
+      }
+}
+
+template <int EPI, bool NORM>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, const BGemm p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  __shared__ uint64_t full[kRing], empty[kRing], acc_full[2], acc_empty[2], mma_done;
+  __shared__ uint64_t full[kRing], empty[kRing], xready[kRing], acc_full[2], acc_empty[2], mma_done;
+  __shared__ float s_rs[kSeqN];
   __shared__ uint32_t tmem_base, consumed, issued_count;
   __shared__ int failed, last_flag;
   __shared__ EpiShared es;
@@ -254,12 +307,12 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t G = gridDim.x, c = blockIdx.x, nk = p.nk;
   const uint32_t kb0 = range_start(c, p.total, G), kb1 = range_start(c + 1, p.total, G);
-  const uint32_t n = kb1 - kb0;
 
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < kRing; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
+      mbar_init(&xready[i], 2);  // one arrival per transform warp
     }
     for (uint32_t i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
@@ -277,6 +330,7 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
   tc_fence_after();
   const uint32_t tmem = tmem_base;
   grid_dep_launch();
+  if (threadIdx.x == 0) trace_mark(p.d, p.b, 0);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -329,7 +383,8 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
           tc_fence_after();
         }
         const uint32_t s = i % kRing;
-        if (failed_now(&failed) || !mbar_wait(&full[s], (i / kRing) & 1)) { failed = 1; break; }
+        if (failed_now(&failed) || !mbar_wait(NORM ? &xready[s] : &full[s], (i / kRing) & 1)) { failed = 1; break; }
+        if (i == 0) trace_mark(p.d, p.b, 5);
         tc_fence_after();
         const uint32_t sa = smem_addr(ring + s * kStageBytes), sx = sa + kStageW;
         for (uint32_t j = 0; j < e - kb; ++j)
@@ -349,11 +404,52 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
       mma1_commit(&mma_done);
       if (!mbar_wait(&mma_done, 0)) failed = 1;
     }
+  } else if (warp >= 6) {
+    if (NORM) {
+      // Transform warps: r per sequence from the residual GEMM's tile sums,
+      // then every stage's activation boxes normalised in place.
+      grid_dep_wait();
+      const uint32_t u = threadIdx.x - 192;
+      {
+        // Sequence u / 4: thread u % 4 sums tiles [q0, q0 + per) in order
+        // (all loads in flight at once), the four partials are added in
+        // quarter order: a fixed order for every H.
+        const uint32_t T = p.d.H / kTileM, per = (T + 3) / 4, s = u / 4, q0 = (u % 4) * per;
+        float part = 0.f;
+        if (per <= 16) {
+          float x[16];
+#pragma unroll
+          for (uint32_t k = 0; k < 16; ++k) x[k] = (k < per && q0 + k < T) ? __ldcg(p.b.ssq + (q0 + k) * kSeqN + s) : 0.f;
+#pragma unroll
+          for (uint32_t k = 0; k < 16; ++k) part += x[k];
+        } else {
+          for (uint32_t k = 0; k < per && q0 + k < T; ++k) part += __ldcg(p.b.ssq + (q0 + k) * kSeqN + s);
+        }
+        const float p1 = __shfl_down_sync(kFullMask, part, 1), p2 = __shfl_down_sync(kFullMask, part, 2),
+                    p3 = __shfl_down_sync(kFullMask, part, 3);
+        if (u % 4 == 0) s_rs[s] = 1.0f / sqrtf(((part + p1) + p2 + p3) / static_cast<float>(p.d.H) + p.d.eps);
+      }
+      asm volatile("bar.sync 3, 64;" ::: "memory");
+      bool dead = false;
+      uint32_t i = 0;
+      for (uint32_t kb = kb0; kb < kb1; ++i) {
+        const uint32_t e = stage_end(kb, kb1, nk), s = i % kRing;
+        if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&full[s], (i / kRing) & 1));
+        if (dead) { failed = 1; break; }
+        norm_stage(ring + s * kStageBytes + kStageW, kb, e, nk, p.norm_w, s_rs, u);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&xready[s]);
+        kb = e;
+      }
+    }
   } else {
     // Epilogue warps: inputs of the epilogue (residual, positions, caches)
     // come from earlier kernels.
     grid_dep_wait();
+    if (threadIdx.x == 64) trace_mark(p.d, p.b, 1);
     const uint32_t quarter = warp & 3, r = quarter * 32 + lane, et = threadIdx.x - 64;
+    uint32_t par = 0;
     // A warp that gives up waiting stays in the loop (every epilogue warp
     // must reach the same named barriers) and computes on zeros from then on.
     bool dead = false;
@@ -364,6 +460,7 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
       const uint32_t buf = seg & 1;
       if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&acc_full[buf], (seg >> 1) & 1));
       if (dead) failed = 1;
+      if (threadIdx.x == 64 && end == kb1) trace_mark(p.d, p.b, 6);
       float v[kSeqN];
 #pragma unroll
       for (uint32_t s = 0; s < kSeqN; ++s) v[s] = 0.f;
@@ -385,6 +482,13 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      // Residual epilogue input, loaded before the arrival round trips.
+      float xr[kSeqN];
+#pragma unroll
+      for (uint32_t s = 0; s < kSeqN; ++s)
+        xr[s] = (EPI == kEpiResid && t * kTileM + r < p.rows && s < p.d.batch)
+                    ? dec::bfcg(p.out, static_cast<size_t>(s) * p.rows + t * kTileM + r)
+                    : 0.f;
       bool run = true;
       if (!whole) {
         const uint32_t slot = t == kb0 / nk ? 0u : 1u;
@@ -394,9 +498,11 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
         const uint32_t c0 = range_owner(t * nk, p.total, G), c1 = range_owner((t + 1) * nk - 1, p.total, G);
         epi_sync();  // the tile's partial is complete in this CTA; one thread fences for all
         if (et == 0) {
-          __threadfence();
-          last_flag = atomicAdd(p.b.cnt_tile + t, 1u) == c1 - c0;
-          __threadfence();
+          // Release (cumulative over the barrier: every epilogue thread's
+          // partial) and acquire (the other CTAs' partials) in one atomic.
+          uint32_t old;
+          asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(p.b.cnt_tile + t) : "memory");
+          last_flag = old == c1 - c0;
         }
         epi_sync();
         run = last_flag != 0;
@@ -428,7 +534,11 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
           if (et == 0) p.b.cnt_tile[t] = 0;
         }
       }
-      if (run) run_epilogue<EPI>(p, t, r, v, es);
+      if (run) {
+        run_epilogue<EPI>(p, t, r, v, xr, es, par);
+        par ^= 1u;
+      }
+      if (threadIdx.x == 64 && end == kb1) trace_mark(p.d, p.b, 7);
       kb = end;
     }
   }
@@ -446,6 +556,7 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
     tc_fence_after();
     tmem_dealloc1(tmem, kTmemCols);
   }
+  if (threadIdx.x == 0) trace_mark(p.d, p.b, 2);
 }
 
 // ---------------------------------------------------------------- norms ----
@@ -454,7 +565,9 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
 __global__ void __launch_bounds__(256) k_bnorm(BatchDims d, BatchBuffers b, const bf16 *w, int embed) {
   __shared__ float scratch[8];
   grid_dep_launch();
+  if (threadIdx.x == 0) trace_mark(d, b, 0);
   grid_dep_wait();
+  if (threadIdx.x == 0) trace_mark(d, b, 1);
   const uint32_t s = blockIdx.x, t = threadIdx.x, H = d.H;
   uint4 *x4 = reinterpret_cast<uint4 *>(b.x + static_cast<size_t>(s) * H);
   uint4 *xn4 = reinterpret_cast<uint4 *>(b.xn + static_cast<size_t>(s) * H);
@@ -489,6 +602,8 @@ __global__ void __launch_bounds__(256) k_bnorm(BatchDims d, BatchBuffers b, cons
     }
     xn4[c] = make_uint4(o[0], o[1], o[2], o[3]);
   }
+  __syncthreads();
+  if (threadIdx.x == 0) trace_mark(d, b, 2);
 }
 
 // ------------------------------------------------------------ attention ----
@@ -544,6 +659,64 @@ __global__ void __launch_bounds__(kStreamThreads) k_bpv(BatchDims bd, BatchBuffe
   pv_item<G>(d, b, ws, blockIdx.y, blockIdx.x, bd.nchunks, n, as);
 }
 
+// ------------------------------------------------------ head epilogues ----
+// One warp finishes head `col` of sequence s's raw [q; k; v] (the QKV
+// GEMM's bf16 output) at position pos with the batch-1 arithmetic (lane l
+// owns dimensions l + 32 j, so both rotate-half partners sit in one lane):
+// q/k: RMSNorm with the head norm weight, then RoPE; v: unchanged. Returns
+// the lane's four finished values (dims l, l + 32, l + 64, l + 96).
+__device__ inline void head_finish(const BatchDims &bd, const BatchBuffers &bb, const LayerWeights &w, uint32_t s,
+                                   uint32_t col, uint32_t pos, float (&out)[4]) {
+  const uint32_t lane = threadIdx.x & 31, rows = (bd.QH + 2 * bd.KVH) * kHD;
+  const bf16 *raw = bb.qkv + static_cast<size_t>(s) * rows + static_cast<size_t>(col) * kHD;
+  const bool is_v = col >= bd.QH + bd.KVH, is_q = col < bd.QH;
+  float v[4], nwv[4], cv[4], sv[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[j] = bfv(raw, lane + 32 * j);
+    nwv[j] = is_v ? 0.f : bfv(is_q ? w.q_norm : w.k_norm, lane + 32 * j);
+    cv[j] = is_v ? 0.f : bfv(bb.cos_t, static_cast<size_t>(pos) * kHD + lane + 32 * j);
+    sv[j] = is_v ? 0.f : bfv(bb.sin_t, static_cast<size_t>(pos) * kHD + lane + 32 * j);
+  }
+  if (is_v) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[j] = v[j];
+    return;
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(kHD) + bd.eps);
+  float nv[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) nv[j] = round_bf16(__fmul_rn(nwv[j], round_bf16(__fmul_rn(v[j], r))));
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {  // pairs (i, i + 64): rotate_half
+    const float a = nv[j], c = nv[j + 2];
+    out[j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(a, cv[j])), round_bf16(__fmul_rn(-c, sv[j]))));
+    out[j + 2] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(c, cv[j + 2])), round_bf16(__fmul_rn(a, sv[j + 2]))));
+  }
+}
+
+// Chunked-attention path: the head epilogues of (kv head blockIdx.x,
+// sequence blockIdx.y) into q and the caches (one warp per head).
+__global__ void __launch_bounds__(256) k_bheads(BatchDims bd, BatchBuffers bb, LayerWeights w) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const uint32_t h = blockIdx.x, s = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t G = bd.QH / bd.KVH, pos = bb.seq[s].position;
+  for (uint32_t k = warp; k < G + 2; k += 8) {
+    const uint32_t col = k < G ? h * G + k : (k == G ? bd.QH + h : bd.QH + bd.KVH + h);
+    float out[4];
+    head_finish(bd, bb, w, s, col, pos, out);
+    bf16 *dst = k < G ? bb.q + (static_cast<size_t>(s) * bd.QH + col) * kHD
+                      : (k == G ? w.kcache : w.vcache) + s * bb.kv_seq_stride + (static_cast<size_t>(pos) * bd.KVH + h) * kHD;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) putv(dst, lane + 32 * j, out[j]);
+  }
+}
+
 // ------------------------------------------------- fused attention (one CTA) ----
 // One CTA per (kv head h, sequence s) runs the whole decode attention of the
 // head group over positions [0, n): pass 1 streams K (TMA, 64-position
@@ -554,14 +727,20 @@ __global__ void __launch_bounds__(kStreamThreads) k_bpv(BatchDims bd, BatchBuffe
 // batch-1 path); pass 2 streams V and accumulates p * v, and the CTA writes
 // the bf16 output of its G heads. Nothing crosses CTAs, so there is no
 // score scratch, statistics exchange or chunk combine in global memory.
-// Warp 0 is the TMA producer; the 8 consumer warps take 8 positions each of
-// every stage, lane l dimensions 4l .. 4l + 3. K stages that hold only
+// Warp 0 is the TMA producer; the 16 consumer warps take 4 positions each
+// of every stage, lane l dimensions 4l .. 4l + 3 (16 warps rather than 8:
+// a stage's dot products and reductions are short dependent chains, and
+// twice the warps hide their latency behind the stream). K stages that hold only
 // positions below n - 1 (rows written by earlier steps) are requested before
 // griddepcontrol.wait; the newest row comes from the previous kernel.
 constexpr uint32_t kAttnPos = 64;                       // positions per stage
 constexpr uint32_t kAttnStageBytes = kAttnPos * kHD * 2;  // 16 KB
 constexpr uint32_t kAttnStages = 6;
-constexpr uint32_t kAttnPosPerWarp = kAttnPos / kConsumerWarps;  // 8
+constexpr uint32_t kAttnWarps = 16;                             // consumer warps
+constexpr uint32_t kAttnThreads = 32 * (kAttnWarps + 1);
+constexpr uint32_t kAttnPosPerWarp = kAttnPos / kAttnWarps;     // 4
+
+__device__ __forceinline__ void attn_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kAttnWarps) : "memory"); }
 
 __host__ __device__ inline size_t attn_scores_bytes(uint32_t G, uint32_t max_seq) {
   return (static_cast<size_t>(G) * max_seq * 2 + 15) / 16 * 16;
@@ -570,36 +749,16 @@ __host__ __device__ inline size_t attn_smem_bytes(uint32_t G, uint32_t max_seq) 
   return 1024 + static_cast<size_t>(kAttnStages) * kAttnStageBytes + attn_scores_bytes(G, max_seq);
 }
 
-// Transpose reduction: lane l holds V = 8 G partial sums; afterwards lane l
-// holds the warp-wide sums of values [l V / 32, (l + 1) V / 32) in val[0..]
-// (for V < 32 lanes that share a value hold identical sums).
-template <int V>
-__device__ __forceinline__ void warp_transpose_sum(float (&val)[V], uint32_t lane) {
-#pragma unroll
-  for (int k = 0; k < 5; ++k) {
-    const int o = 16 >> k, half = V >> (k + 1);
-    if (half >= 1) {
-      const bool upper = (lane & o) != 0;
-#pragma unroll
-      for (int i = 0; i < half; ++i) {
-        const float send = upper ? val[i] : val[i + half];
-        const float keep = upper ? val[i + half] : val[i];
-        val[i] = keep + __shfl_xor_sync(kFullMask, send, o);
-      }
-    } else {
-      val[0] += __shfl_xor_sync(kFullMask, val[0], o);
-    }
-  }
-}
-
 template <int G>
-__global__ void __launch_bounds__(kStreamThreads, 1)
-k_battn(BatchDims bd, BatchBuffers bb, const __grid_constant__ CUtensorMap map_k,
+__global__ void __launch_bounds__(kAttnThreads, 1)
+k_battn(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant__ CUtensorMap map_k,
         const __grid_constant__ CUtensorMap map_v) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ uint64_t full[kAttnStages], empty[kAttnStages];
-  __shared__ float red_m[kConsumerWarps][G], red_s[kConsumerWarps][G];
+  __shared__ float red_m[kAttnWarps][G], red_s[kAttnWarps][G];
   __shared__ float sM[G], sInv[G];
+  __shared__ float q_s[G][kHD];                            // finished q of the group
+  __shared__ __align__(16) uint16_t knew[kHD], vnew[kHD];  // finished k, v of the newest position
   __shared__ int failed;
   __shared__ uint32_t issued_n;
   const uint32_t a0 = smem_addr(smem_raw);
@@ -610,7 +769,7 @@ k_battn(BatchDims bd, BatchBuffers bb, const __grid_constant__ CUtensorMap map_k
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < kAttnStages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kConsumerWarps);
+      mbar_init(&empty[i], kAttnWarps);
     }
     fence_mbar_init();
     failed = 0;
@@ -618,25 +777,24 @@ k_battn(BatchDims bd, BatchBuffers bb, const __grid_constant__ CUtensorMap map_k
   }
   __syncthreads();
   grid_dep_launch();
-  // Positions: the newest row (n - 1) is written by the previous kernel, so
-  // the position is read only after waiting - except by the producer, which
-  // needs it before: it reads the state, which no kernel of the step writes
-  // before the argmax.
+  if (threadIdx.x == 0) trace_mark(bd, bb, 0);
+  // The position comes from the step state, which no kernel of the step
+  // writes before the argmax, so it is read before waiting.
   const uint32_t n = bb.seq[s].position + 1;
   const uint32_t nst = (n + kAttnPos - 1) / kAttnPos;  // stages per pass
   const int32_t y0 = static_cast<int32_t>(s * ms), xh = static_cast<int32_t>(h * kHD);
 
   if (warp == 0) {
     if (lane == 0) {
-      // K stages entirely below the newest row may be fetched before the wait.
-      uint32_t early = (n - 1) / kAttnPos;
-      if (early > kAttnStages) early = kAttnStages;
+      // The cache rows below the newest were written by earlier steps, and
+      // the newest row is taken from shared memory (this CTA computes it):
+      // the first ring's worth of K stages is fetched before the wait.
+      uint32_t early = nst < kAttnStages ? nst : kAttnStages;
       for (uint32_t i = 0; i < early; ++i) {
         mbar_expect_tx(&full[i], kAttnStageBytes);
         tma_load_2d_plain(ring + i * kAttnStageBytes, &map_k, xh, y0 + static_cast<int32_t>(i * kAttnPos), &full[i]);
       }
       grid_dep_wait();
-      asm volatile("fence.proxy.async.global;" ::: "memory");  // the new row, written by generic stores
       uint32_t i = early;
       for (; i < 2 * nst; ++i) {
         const uint32_t slot = i % kAttnStages, use = i / kAttnStages;
@@ -651,15 +809,37 @@ k_battn(BatchDims bd, BatchBuffers bb, const __grid_constant__ CUtensorMap map_k
     __syncwarp();
   } else {
     grid_dep_wait();
+    if (threadIdx.x == 32) trace_mark(bd, bb, 1);
     const uint32_t cw = warp - 1, t = threadIdx.x - 32;
     bool dead = false;
-    // q of the group's heads, this lane's 4 dimensions
+    // Head epilogues of the group (warp g < G: q head h G + g; G: k; G + 1: v)
+    // at the newest position; k and v also go to the caches for later steps.
+    const uint32_t pos_new = n - 1;
+    if (cw < static_cast<uint32_t>(G) + 2) {
+      const uint32_t col = cw < G ? h * G + cw : (cw == G ? bd.QH + h : bd.QH + bd.KVH + h);
+      float out[4];
+      head_finish(bd, bb, w, s, col, pos_new, out);
+      if (cw < G) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) q_s[cw][lane + 32 * j] = out[j];
+      } else {
+        bf16 *cache = (cw == G ? w.kcache : w.vcache) + s * bb.kv_seq_stride +
+                      (static_cast<size_t>(pos_new) * bd.KVH + h) * kHD;
+        uint16_t *row = cw == G ? knew : vnew;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          row[lane + 32 * j] = float_to_bf16_bits(out[j]);
+          putv(cache, lane + 32 * j, out[j]);
+        }
+      }
+    }
+    attn_sync();
+    // q of the group's heads, this lane's 4 dimensions 4l .. 4l + 3
     float q[G][4];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const uint2 raw = *reinterpret_cast<const uint2 *>(bb.q + (static_cast<size_t>(s) * bd.QH + h * G + g) * kHD + lane * 4);
-      q[g][0] = bf16_lo(raw.x); q[g][1] = bf16_hi(raw.x); q[g][2] = bf16_lo(raw.y); q[g][3] = bf16_hi(raw.y);
-    }
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) q[g][j] = q_s[g][lane * 4 + j];
     // ---- pass 1: scores
     for (uint32_t i = 0; i < nst; ++i) {
       const uint32_t slot = i % kAttnStages;
@@ -668,8 +848,10 @@ k_battn(BatchDims bd, BatchBuffers bb, const __grid_constant__ CUtensorMap map_k
       float val[kAttnPosPerWarp * G];
 #pragma unroll
       for (uint32_t pp = 0; pp < kAttnPosPerWarp; ++pp) {
+        const uint32_t pos = i * kAttnPos + cw * kAttnPosPerWarp + pp;
         const uint2 kr = dead ? make_uint2(0, 0)
-                              : *reinterpret_cast<const uint2 *>(st + (cw * kAttnPosPerWarp + pp) * (kHD * 2) + lane * 8);
+                         : pos == pos_new ? *reinterpret_cast<const uint2 *>(knew + lane * 4)
+                                          : *reinterpret_cast<const uint2 *>(st + (cw * kAttnPosPerWarp + pp) * (kHD * 2) + lane * 8);
         const float k4[4] = {bf16_lo(kr.x), bf16_hi(kr.x), bf16_lo(kr.y), bf16_hi(kr.y)};
 #pragma unroll
         for (int g = 0; g < G; ++g) {
@@ -693,12 +875,12 @@ k_battn(BatchDims bd, BatchBuffers bb, const __grid_constant__ CUtensorMap map_k
           sc[g * ms + pos] = float_to_bf16_bits(round_bf16(__fmul_rn(round_bf16(val[k]), kAttnScale)));
       }
     }
-    consumer_sync();
+    attn_sync();
     // ---- per head: max, sum of exp, then probabilities in place
     float m[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) m[g] = -INFINITY;
-    for (uint32_t pos = t; pos < n; pos += kConsumerThreads)
+    for (uint32_t pos = t; pos < n; pos += 32 * kAttnWarps)
 #pragma unroll
       for (int g = 0; g < G; ++g) m[g] = fmaxf(m[g], bf16_bits_to_float(sc[g * ms + pos]));
 #pragma unroll
@@ -706,17 +888,17 @@ k_battn(BatchDims bd, BatchBuffers bb, const __grid_constant__ CUtensorMap map_k
       const float wm = warp_max(m[g]);
       if (lane == 0) red_m[cw][g] = wm;
     }
-    consumer_sync();
+    attn_sync();
     if (t < static_cast<uint32_t>(G)) {
       float mm = red_m[0][t];
-      for (int w = 1; w < kConsumerWarps; ++w) mm = fmaxf(mm, red_m[w][t]);
+      for (uint32_t w = 1; w < kAttnWarps; ++w) mm = fmaxf(mm, red_m[w][t]);
       sM[t] = mm;
     }
-    consumer_sync();
+    attn_sync();
     float l[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) l[g] = 0.f;
-    for (uint32_t pos = t; pos < n; pos += kConsumerThreads)
+    for (uint32_t pos = t; pos < n; pos += 32 * kAttnWarps)
 #pragma unroll
       for (int g = 0; g < G; ++g) l[g] += expf(bf16_bits_to_float(sc[g * ms + pos]) - sM[g]);
 #pragma unroll
@@ -724,20 +906,20 @@ k_battn(BatchDims bd, BatchBuffers bb, const __grid_constant__ CUtensorMap map_k
       const float ws = warp_sum(l[g]);
       if (lane == 0) red_s[cw][g] = ws;
     }
-    consumer_sync();
+    attn_sync();
     if (t < static_cast<uint32_t>(G)) {
       float ss = 0.f;
-      for (int w = 0; w < kConsumerWarps; ++w) ss += red_s[w][t];
+      for (uint32_t w = 0; w < kAttnWarps; ++w) ss += red_s[w][t];
       sInv[t] = 1.0f / ss;
     }
-    consumer_sync();
-    for (uint32_t pos = t; pos < n; pos += kConsumerThreads)
+    attn_sync();
+    for (uint32_t pos = t; pos < n; pos += 32 * kAttnWarps)
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         const float sv = bf16_bits_to_float(sc[g * ms + pos]);
         sc[g * ms + pos] = float_to_bf16_bits(__fmul_rn(expf(sv - sM[g]), sInv[g]));
       }
-    consumer_sync();
+    attn_sync();
     // ---- pass 2: p . v
     float acc[G][4];
 #pragma unroll
@@ -752,7 +934,8 @@ k_battn(BatchDims bd, BatchBuffers bb, const __grid_constant__ CUtensorMap map_k
       for (uint32_t pp = 0; pp < kAttnPosPerWarp; ++pp) {
         const uint32_t pos = i * kAttnPos + cw * kAttnPosPerWarp + pp;
         if (pos >= n || dead) continue;
-        const uint2 vr = *reinterpret_cast<const uint2 *>(st + (cw * kAttnPosPerWarp + pp) * (kHD * 2) + lane * 8);
+        const uint2 vr = pos == pos_new ? *reinterpret_cast<const uint2 *>(vnew + lane * 4)
+                                        : *reinterpret_cast<const uint2 *>(st + (cw * kAttnPosPerWarp + pp) * (kHD * 2) + lane * 8);
         const float v4[4] = {bf16_lo(vr.x), bf16_hi(vr.x), bf16_lo(vr.y), bf16_hi(vr.y)};
 #pragma unroll
         for (int g = 0; g < G; ++g) {
@@ -765,17 +948,17 @@ k_battn(BatchDims bd, BatchBuffers bb, const __grid_constant__ CUtensorMap map_k
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
     if (dead) failed = 1;
-    consumer_sync();  // every stage consumed: the ring is free for the warp partials
-    float *part = reinterpret_cast<float *>(ring);  // [8 warps][G][128]
+    attn_sync();  // every stage consumed: the ring is free for the warp partials
+    float *part = reinterpret_cast<float *>(ring);  // [16 warps][G][128]
 #pragma unroll
     for (int g = 0; g < G; ++g)
       *reinterpret_cast<float4 *>(part + (cw * G + g) * kHD + lane * 4) =
           make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
-    consumer_sync();
-    for (uint32_t e = t; e < G * kHD; e += kConsumerThreads) {
+    attn_sync();
+    for (uint32_t e = t; e < G * kHD; e += 32 * kAttnWarps) {
       float o = 0.f;
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) o += part[w * G * kHD + e];
+      for (uint32_t w = 0; w < kAttnWarps; ++w) o += part[w * G * kHD + e];
       const uint32_t g = e / kHD, dd = e % kHD;
       putv(bb.attn, (static_cast<size_t>(s) * bd.QH + h * G + g) * kHD + dd, o);
     }
@@ -789,6 +972,7 @@ k_battn(BatchDims bd, BatchBuffers bb, const __grid_constant__ CUtensorMap map_k
       if (!mbar_wait(&full[i % kAttnStages], (i / kAttnStages) & 1)) break;
     atomicOr(bb.error, kErrPipelineTimeout);
   }
+  if (threadIdx.x == 0) trace_mark(bd, bb, 2);
 }
 
 // --------------------------------------------------------------- argmax ----
@@ -799,7 +983,9 @@ __global__ void __launch_bounds__(256) k_bargmax(BatchDims d, BatchBuffers b, ui
   __shared__ ArgBest wb[8];
   __shared__ uint32_t wbad[8];
   grid_dep_launch();
+  if (threadIdx.x == 0) trace_mark(d, b, 0);
   grid_dep_wait();
+  if (threadIdx.x == 0) trace_mark(d, b, 1);
   const uint32_t s = blockIdx.x, t = threadIdx.x;
   ArgBest best{-INFINITY, 0xffffffffu};
   uint32_t bad = 0;
@@ -823,6 +1009,7 @@ __global__ void __launch_bounds__(256) k_bargmax(BatchDims d, BatchBuffers b, ui
     st.token = next;
     if (pos < d.max_seq) b.log[static_cast<size_t>(s) * d.max_seq + pos] = next;
     st.position = pos + 1;
+    trace_mark(d, b, 2);
   }
 }
 
@@ -863,7 +1050,8 @@ constexpr size_t kGemmSmem = static_cast<size_t>(kRing) * kStageBytes + 1024;
 
 // Y = X . W^T for W [rows][K] and X [16][K] (K a multiple of 64, both 16-byte
 // aligned with 16-byte row pitches), with epilogue EPI.
-template <int EPI>
+// NORM: X is the raw residual, RMS-normalised with p.norm_w inside the GEMM.
+template <int EPI, bool NORM = false>
 cudaError_t launch_bgemm(const bf16 *W, uint32_t rows, uint32_t K, const bf16 *X, BGemm p, cudaStream_t s) {
   if (K % kKb) return cudaErrorInvalidValue;
   CUtensorMap mw, mx;
@@ -876,7 +1064,7 @@ cudaError_t launch_bgemm(const bf16 *W, uint32_t rows, uint32_t K, const bf16 *X
   p.tiles = (rows + kTileM - 1) / kTileM;
   p.total = p.tiles * p.nk;
   const uint32_t grid = std::min(sm_count(), p.total);
-  return launch_pdl(k_bgemm<EPI>, dim3(grid), dim3(kGemmThreads), kGemmSmem, s, mw, mx, p);
+  return launch_pdl(k_bgemm<EPI, NORM>, dim3(grid), dim3(kGemmThreads), kGemmSmem, s, mw, mx, p);
 }
 
 int smem_optin() {
@@ -906,10 +1094,12 @@ cudaError_t launch_battention(const BatchDims &d, const BatchBuffers &b, const L
     e = make_tmap_2d_u16(&mv, w.vcache, static_cast<uint64_t>(d.KVH) * kHD, rows, static_cast<uint64_t>(d.KVH) * kHD,
                          kHD, kAttnPos);
     if (e != cudaSuccess) return e;
-    return launch_pdl(k_battn<G>, dim3(d.KVH, d.batch), dim3(kStreamThreads), smem, s, d, b, mk, mv);
+    return launch_pdl(k_battn<G>, dim3(d.KVH, d.batch), dim3(kAttnThreads), smem, s, d, b, w, mk, mv);
   }
+  cudaError_t e = launch_pdl(k_bheads, dim3(d.KVH, d.batch), dim3(256), 0, s, d, b, w);
+  if (e != cudaSuccess) return e;
   const dim3 grid(d.nchunks, d.KVH, d.batch), block(kStreamThreads);
-  const cudaError_t e = launch_pdl(k_bscores<G>, grid, block, 0, s, d, b, w);
+  e = launch_pdl(k_bscores<G>, grid, block, 0, s, d, b, w);
   return e != cudaSuccess ? e : launch_pdl(k_bpv<G>, grid, block, 0, s, d, b, w);
 }
 
@@ -922,49 +1112,61 @@ uint32_t batch_max_tiles(const BatchDims &d) {
   return std::max({qkv, o, gu, batch_lm_tiles(d.vocab)});
 }
 
-cudaError_t record_batch_step(const BatchDims &d, const BatchBuffers &b, const LayerWeights *layers,
+cudaError_t record_batch_step(const BatchDims &d0, const BatchBuffers &b, const LayerWeights *layers,
                               uint32_t n_layers, cudaStream_t s) {
-  if (d.batch < 1 || d.batch > kMaxBatch) return cudaErrorInvalidValue;
+  if (d0.batch < 1 || d0.batch > kMaxBatch) return cudaErrorInvalidValue;
+  BatchDims d = d0;
+  uint32_t slot = 0;
+  // Each launch gets the next trace slot.
+  auto at = [&](BGemm g) {
+    d.trace_slot = slot++;
+    g.d = d;
+    g.b = b;
+    return g;
+  };
+  auto next = [&]() {
+    d.trace_slot = slot++;
+    return d;
+  };
   const uint32_t G = d.QH / d.KVH;
-  BGemm base{};
-  base.d = d;
-  base.b = b;
 #define XPU_TRY(expr)                        \
   do {                                       \
     const cudaError_t e_ = (expr);           \
     if (e_ != cudaSuccess) return e_;        \
   } while (0)
-  XPU_TRY(launch_pdl(k_bnorm, dim3(d.batch), dim3(256), 0, s, d, b, layers[0].in_norm, 1));
+  XPU_TRY(launch_pdl(k_bnorm, dim3(d.batch), dim3(256), 0, s, next(), b, layers[0].in_norm, 1));
   for (uint32_t l = 0; l < n_layers; ++l) {
     const LayerWeights &w = layers[l];
-    if (l > 0) XPU_TRY(launch_pdl(k_bnorm, dim3(d.batch), dim3(256), 0, s, d, b, w.in_norm, 0));
-    BGemm pq = base;
-    pq.q_norm = w.q_norm;
-    pq.k_norm = w.k_norm;
-    pq.kcache = w.kcache;
-    pq.vcache = w.vcache;
-    XPU_TRY(launch_bgemm<kEpiQkv>(w.wqkv, (d.QH + 2 * d.KVH) * kHD, d.H, b.xn, pq, s));
+    BGemm pq{};
+    pq.out = b.qkv;
+    pq.norm_w = w.in_norm;
+    if (l == 0)  // the embedding kernel normalised layer 0's input
+      XPU_TRY(launch_bgemm<kEpiQkv>(w.wqkv, (d.QH + 2 * d.KVH) * kHD, d.H, b.xn, at(pq), s));
+    else
+      XPU_TRY((launch_bgemm<kEpiQkv, true>(w.wqkv, (d.QH + 2 * d.KVH) * kHD, d.H, b.x, at(pq), s)));
+    const BatchDims da = next();
     switch (G) {
-      case 1: XPU_TRY(launch_battention<1>(d, b, w, s)); break;
-      case 2: XPU_TRY(launch_battention<2>(d, b, w, s)); break;
-      case 4: XPU_TRY(launch_battention<4>(d, b, w, s)); break;
-      case 8: XPU_TRY(launch_battention<8>(d, b, w, s)); break;
+      case 1: XPU_TRY(launch_battention<1>(da, b, w, s)); break;
+      case 2: XPU_TRY(launch_battention<2>(da, b, w, s)); break;
+      case 4: XPU_TRY(launch_battention<4>(da, b, w, s)); break;
+      case 8: XPU_TRY(launch_battention<8>(da, b, w, s)); break;
       default: return cudaErrorInvalidValue;
     }
-    BGemm po = base;
+    BGemm po{};
     po.out = b.x;
-    XPU_TRY(launch_bgemm<kEpiResid>(w.wo, d.H, d.QH * kHD, b.attn, po, s));
-    XPU_TRY(launch_pdl(k_bnorm, dim3(d.batch), dim3(256), 0, s, d, b, w.post_norm, 0));
-    BGemm pg = base;
+    XPU_TRY(launch_bgemm<kEpiResid>(w.wo, d.H, d.QH * kHD, b.attn, at(po), s));
+    BGemm pg{};
     pg.out = b.h;
-    XPU_TRY(launch_bgemm<kEpiGateUp>(w.wgu, 2 * d.I, d.H, b.xn, pg, s));
-    BGemm pd = base;
+    pg.norm_w = w.post_norm;
+    XPU_TRY((launch_bgemm<kEpiGateUp, true>(w.wgu, 2 * d.I, d.H, b.x, at(pg), s)));
+    BGemm pd{};
     pd.out = b.x;
-    XPU_TRY(launch_bgemm<kEpiResid>(w.wd, d.H, d.I, b.h, pd, s));
+    XPU_TRY(launch_bgemm<kEpiResid>(w.wd, d.H, d.I, b.h, at(pd), s));
   }
-  XPU_TRY(launch_pdl(k_bnorm, dim3(d.batch), dim3(256), 0, s, d, b, b.final_norm, 0));
-  XPU_TRY(launch_bgemm<kEpiLm>(b.lm_head, d.vocab, d.H, b.xn, base, s));
-  XPU_TRY(launch_pdl(k_bargmax, dim3(d.batch), dim3(256), 0, s, d, b, batch_lm_tiles(d.vocab)));
+  BGemm pl{};
+  pl.norm_w = b.final_norm;
+  XPU_TRY((launch_bgemm<kEpiLm, true>(b.lm_head, d.vocab, d.H, b.x, at(pl), s)));
+  XPU_TRY(launch_pdl(k_bargmax, dim3(d.batch), dim3(256), 0, s, next(), b, batch_lm_tiles(d.vocab)));
 #undef XPU_TRY
   return cudaSuccess;
 }

@@ -22,6 +22,7 @@
 #include <cmath>
 #include <stdexcept>
 #include <cstddef>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -547,6 +548,21 @@ class Qwen3Engine {
     for (uint32_t i = 0; i < steps; ++i) CK(cudaGraphLaunch(batch_exec_, s));
   }
 
+  // Per-kernel timeline of the batched steps since the last call
+  // (XPU_BATCH_TRACE=1): [slot][8] globaltimer ns, see BatchBuffers::trace;
+  // returns the number of values written (0 when tracing is off). Resets it.
+  uint32_t batch_trace(uint64_t *host, uint32_t capacity) {
+    if (!btrace_) return 0;
+    const uint32_t total = kBatchTraceSlots * kBatchTraceValues;
+    const uint32_t n = std::min<uint32_t>(capacity, total);
+    CK(cudaStreamSynchronize(stream_));
+    if (host && n) CK(cudaMemcpy(host, btrace_, n * sizeof(uint64_t), cudaMemcpyDeviceToHost));
+    std::vector<unsigned long long> init(total, 0);
+    for (uint32_t i = 0; i < kBatchTraceSlots; ++i) init[kBatchTraceValues * i] = init[kBatchTraceValues * i + 3] = ~0ull;
+    CK(cudaMemcpy(btrace_, init.data(), init.size() * sizeof(unsigned long long), cudaMemcpyHostToDevice));
+    return host ? n : 0;
+  }
+
   void batch_logits(uint32_t seq, uint16_t *host, uint32_t count) {
     if (seq >= batch_cap_) throw InvalidArg("sequence index outside the batch capacity");
     if (!bb_.logits) throw InvalidArg("no batched step has run");
@@ -556,8 +572,8 @@ class Qwen3Engine {
     CK(cudaStreamSynchronize(stream_));
   }
 
-  // embed + norm, 8 per layer (no input norm on layer 0), final norm, lm_head, argmax
-  uint32_t batch_kernels_per_step() const { return 8 * shape_.num_hidden_layers + 3; }
+  // embed + norm, 5 per layer (qkv, attention, o_proj, gate/up, down), lm_head, argmax
+  uint32_t batch_kernels_per_step() const { return 5 * shape_.num_hidden_layers + 3; }
 
   // Bytes one batched step of n sequences must move: the weights once, plus
   // every sequence's K and V over `context` positions.
@@ -623,6 +639,7 @@ class Qwen3Engine {
     BatchBuffers b{};
     b.x = dev_zeros<bf16>(B * H);
     b.xn = dev_zeros<bf16>(B * H);
+    b.qkv = dev_zeros<bf16>(B * (Q + 2ull * bd_.KVH * 128));
     b.q = dev_zeros<bf16>(B * Q);
     b.attn = dev_zeros<bf16>(B * Q);
     b.h = dev_zeros<bf16>(B * bd_.I);
@@ -631,6 +648,7 @@ class Qwen3Engine {
     b.stats = dev_zeros<float>(B * bd_.QH * bd_.nchunks * 2);
     b.attn_part = dev_zeros<float>(B * Q * bd_.nchunks);
     b.gemm_part = dev_zeros<float>(static_cast<uint64_t>(batch_gemm_grid()) * 2 * B * 128);
+    b.ssq = dev_zeros<float>((H / 128) * B);
     b.cnt_tile = dev_zeros<unsigned>(batch_max_tiles(bd_));
     b.cnt_attn = dev_zeros<unsigned>(B * bd_.KVH);
     b.cand = dev_zeros<ArgBest>(B * batch_lm_tiles(bd_.vocab));
@@ -647,6 +665,11 @@ class Qwen3Engine {
     b.final_norm = reinterpret_cast<const bf16 *>(final_norm_);
     b.lm_head = reinterpret_cast<const bf16 *>(lm_head_);
     b.kv_seq_stride = static_cast<uint64_t>(max_seq_) * bd_.KVH * 128;
+    const char *trace_env = std::getenv("XPU_BATCH_TRACE");
+    if (trace_env && trace_env[0] == '1') {
+      b.trace = dev_alloc<unsigned long long>(kBatchTraceSlots * kBatchTraceValues);
+      btrace_ = b.trace;
+    }
     bb_ = b;
     CK(cudaMallocHost(&host_seq_, kMaxBatch * sizeof(SeqState) + 16));
     host_berr_ = reinterpret_cast<uint32_t *>(host_seq_ + kMaxBatch);
@@ -986,6 +1009,7 @@ class Qwen3Engine {
   uint32_t *bprompt_ = nullptr, *blog_ = nullptr;
   SeqState *host_seq_ = nullptr;
   uint32_t *host_berr_ = nullptr;
+  unsigned long long *btrace_ = nullptr;  // batched step trace (XPU_BATCH_TRACE=1)
 };
 
 }  // namespace xpu
@@ -1223,6 +1247,13 @@ int xpu_qwen3_batch_logits(xpu_qwen3_engine *engine, uint32_t sequence, uint16_t
 uint64_t xpu_qwen3_batch_bytes_per_step(xpu_qwen3_engine *engine, uint32_t batch, uint32_t context) {
   if (!engine || !engine->impl) return 0;
   return engine->impl->batch_bytes_per_step(batch, context);
+}
+
+int xpu_qwen3_batch_trace(xpu_qwen3_engine *engine, uint64_t *host_ns, uint32_t capacity, uint32_t *count) {
+  return guarded([&] {
+    if (!count) throw xpu::InvalidArg("xpu_qwen3_batch_trace: null pointer");
+    *count = eng(engine).batch_trace(host_ns, capacity);
+  });
 }
 
 uint32_t xpu_qwen3_batch_kernels_per_step(xpu_qwen3_engine *engine) {

@@ -231,3 +231,12 @@ class Qwen3Engine:
 
     def batch_kernels_per_step(self) -> int:
         return int(self.lib.xpu_qwen3_batch_kernels_per_step(self._h))
+
+    def batch_trace(self) -> np.ndarray:
+        """[kernels, 8] globaltimer ns of the batched steps since the last
+        call (XPU_BATCH_TRACE=1; empty otherwise), see
+        xpu_qwen3_batch_trace. Resets the trace."""
+        buf = np.zeros(8 * 512, np.uint64)
+        n = ctypes.c_uint32()
+        _lib.check(self.lib.xpu_qwen3_batch_trace(self._h, buf.ctypes.data, buf.size, ctypes.byref(n)))
+        return buf[:n.value].reshape(-1, 8)
