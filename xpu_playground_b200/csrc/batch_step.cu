@@ -727,6 +727,10 @@ __global__ void __launch_bounds__(256) k_bheads(BatchDims bd, BatchBuffers bb, L
 // batch-1 path); pass 2 streams V and accumulates p * v, and the CTA writes
 // the bf16 output of its G heads. Nothing crosses CTAs, so there is no
 // score scratch, statistics exchange or chunk combine in global memory.
+// Attention leaves HBM bandwidth unused, so the producer warp's other lanes
+// also prefetch a slice of the next GEMM's weights (o_proj, 33.5 MB on the
+// 8B shape, a quarter of L2) into L2 with an evict-last hint, while the K/V
+// stream is marked evict-first: the o_proj GEMM then streams from L2.
 // Warp 0 is the TMA producer; the 16 consumer warps take 4 positions each
 // of every stage, lane l dimensions 4l .. 4l + 3 (16 warps rather than 8:
 // a stage's dot products and reductions are short dependent chains, and
@@ -752,7 +756,7 @@ __host__ __device__ inline size_t attn_smem_bytes(uint32_t G, uint32_t max_seq) 
 template <int G>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 k_battn(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant__ CUtensorMap map_k,
-        const __grid_constant__ CUtensorMap map_v) {
+        const __grid_constant__ CUtensorMap map_v, const uint8_t *prefetch, uint64_t prefetch_bytes) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ uint64_t full[kAttnStages], empty[kAttnStages];
   __shared__ float red_m[kAttnWarps][G], red_s[kAttnWarps][G];
@@ -784,15 +788,30 @@ k_battn(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant__ C
   const uint32_t nst = (n + kAttnPos - 1) / kAttnPos;  // stages per pass
   const int32_t y0 = static_cast<int32_t>(s * ms), xh = static_cast<int32_t>(h * kHD);
 
-  if (warp == 0) {
-    if (lane == 0) {
+  if (warp == 0 && lane != 0) {
+    if (prefetch) {
+      // This CTA's slice of the next GEMM's weights, 32 KB per request.
+      uint64_t pol;
+      asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+      const uint64_t ctas = static_cast<uint64_t>(gridDim.x) * gridDim.y, c = blockIdx.y * gridDim.x + blockIdx.x;
+      const uint64_t b0 = (prefetch_bytes * c / ctas) & ~uint64_t(15), b1 = (prefetch_bytes * (c + 1) / ctas) & ~uint64_t(15);
+      for (uint64_t off = b0 + (lane - 1) * 32768ull; off < b1; off += 31 * 32768ull) {
+        const uint32_t len = static_cast<uint32_t>(b1 - off < 32768ull ? b1 - off : 32768ull);
+        asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(prefetch + off), "r"(len),
+                     "l"(pol)
+                     : "memory");
+      }
+    }
+  } else if (warp == 0) {
+    {
+      const uint64_t kv_pol = evict_first_policy();
       // The cache rows below the newest were written by earlier steps, and
       // the newest row is taken from shared memory (this CTA computes it):
       // the first ring's worth of K stages is fetched before the wait.
       uint32_t early = nst < kAttnStages ? nst : kAttnStages;
       for (uint32_t i = 0; i < early; ++i) {
         mbar_expect_tx(&full[i], kAttnStageBytes);
-        tma_load_2d_plain(ring + i * kAttnStageBytes, &map_k, xh, y0 + static_cast<int32_t>(i * kAttnPos), &full[i]);
+        tma_load_2d(ring + i * kAttnStageBytes, &map_k, xh, y0 + static_cast<int32_t>(i * kAttnPos), &full[i], kv_pol);
       }
       grid_dep_wait();
       uint32_t i = early;
@@ -802,11 +821,10 @@ k_battn(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant__ C
         mbar_expect_tx(&full[slot], kAttnStageBytes);
         const bool is_v = i >= nst;
         const int32_t y = y0 + static_cast<int32_t>((is_v ? i - nst : i) * kAttnPos);
-        tma_load_2d_plain(ring + slot * kAttnStageBytes, is_v ? &map_v : &map_k, xh, y, &full[slot]);
+        tma_load_2d(ring + slot * kAttnStageBytes, is_v ? &map_v : &map_k, xh, y, &full[slot], kv_pol);
       }
       issued_n = i;
     }
-    __syncwarp();
   } else {
     grid_dep_wait();
     if (threadIdx.x == 32) trace_mark(bd, bb, 1);
@@ -975,6 +993,336 @@ k_battn(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant__ C
   if (threadIdx.x == 0) trace_mark(bd, bb, 2);
 }
 
+// ------------------------------------------- tensor-core attention (one CTA) ----
+// The same (kv head h, sequence s) attention as k_battn with both products
+// on tcgen05 (M = 128, N = 16 head slots, G of them used):
+//   pass 1  S = K . Q^T per 128-position stage: A = the K stage (positions x
+//           128 dims, two 64-dim TMA boxes, K-major, 128-byte swizzle),
+//           B = the group's finished q (16 rows x 128 dims, same layout),
+//           D = 128 positions x 16 slots in TMEM (double buffered); the
+//           compute warps read one position per thread and store
+//           s = bf16(bf16(S) * scale) into P (bf16, rows = head slots,
+//           K-major, 128-byte swizzle, 64 positions per 2 KB atom);
+//   softmax M = max s, S = sum exp(s - M) per head (fixed order), then P
+//           = bf16(exp(s - M) * (1 / S)) in place, 0 past the context;
+//   pass 2  O^T = V^T . P^T accumulated over the V stages: A = the V stage
+//           read MN-major (dims contiguous: the cache rows as TMA lands
+//           them), B = P; D = 128 dims x 16 slots in TMEM, read one dim per
+//           thread into the bf16 output.
+// The newest position's k and v are finished by this CTA and written to
+// the caches (with a proxy fence) before the producer fetches the stages
+// that hold them; V rows past the context in the last stage are zeroed in
+// shared memory (a stale row must not meet a zero probability as 0 * NaN).
+// Warp 0: TMA producer (lane 0) and the L2 prefetch of the next GEMM's
+// weights (lanes 1-31); warp 1: TMEM owner and MMA issuer; warps 2-5:
+// compute (head epilogues, score conversion, softmax, output).
+constexpr uint32_t kTcPos = 128;                   // positions per stage
+constexpr uint32_t kTcBox = 128 * 64 * 2;          // one 64-dim box of a stage: 16 KB
+constexpr uint32_t kTcStage = 2 * kTcBox;          // 32 KB
+constexpr uint32_t kTcStages = 3;
+constexpr uint32_t kTcThreads = 192;
+constexpr uint32_t kTcN = 16;                      // MMA N: head slots
+constexpr uint32_t kPAtom = 16 * 128;              // 16 rows x 64 bf16: 2 KB
+constexpr uint32_t kTcTmemCols = 64;               // S[2] (2 x 16) + O (16)
+constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((kTcN >> 3) << 17) | ((128u >> 4) << 24);
+constexpr uint32_t kIdescO = kIdescS | (1u << 15);  // A MN-major
+
+__host__ __device__ inline size_t tc_attn_smem_bytes(uint32_t max_seq) {
+  const size_t atoms = (static_cast<size_t>(max_seq) + kTcPos - 1) / kTcPos * 2;  // P atoms of whole stages
+  return 1024 + static_cast<size_t>(kTcStages) * kTcStage + 2 * kPAtom + atoms * kPAtom;
+}
+
+// Byte offset of element (row r, column c < 64) inside a 128-byte swizzled
+// atom block of 128-byte rows.
+__device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) {
+  return r * 128 + ((((c >> 3) ^ (r & 7)) << 4) | ((c & 7) << 1));
+}
+
+__device__ __forceinline__ void tc_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int G>
+__global__ void __launch_bounds__(kTcThreads, 1)
+k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant__ CUtensorMap map_k,
+           const __grid_constant__ CUtensorMap map_v, const uint8_t *prefetch, uint64_t prefetch_bytes) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ uint64_t full[kTcStages], empty[kTcStages], s_full[2], s_empty[2], hd_ready, p_ready, last_landed,
+      v_patched, o_full, mma_done;
+  __shared__ uint32_t tmem_base, issued_n, consumed_n;
+  __shared__ float red[4][G], sM[G], sInv[G];
+  __shared__ int failed;
+  const uint32_t a0 = smem_addr(smem_raw);
+  uint8_t *ring = smem_raw + ((a0 + 1023u) / 1024u * 1024u - a0);
+  uint8_t *qs = ring + kTcStages * kTcStage;  // 2 atoms: dims 0-63, 64-127
+  uint8_t *ps = qs + 2 * kPAtom;              // P atoms, 64 positions each
+  const uint32_t h = blockIdx.x, s = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t n = bb.seq[s].position + 1, pos_new = n - 1;
+  const uint32_t nst = (n + kTcPos - 1) / kTcPos;
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < kTcStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (uint32_t i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);
+    }
+    mbar_init(&hd_ready, 4);
+    mbar_init(&p_ready, 4);
+    mbar_init(&last_landed, 1);
+    mbar_init(&v_patched, 4);
+    mbar_init(&o_full, 1);
+    mbar_init(&mma_done, 1);
+    fence_mbar_init();
+    failed = 0;
+    issued_n = 0;
+    consumed_n = 0;
+  }
+  if (warp == 1) tmem_alloc1(&tmem_base, kTcTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  grid_dep_launch();
+  if (threadIdx.x == 0) trace_mark(bd, bb, 0);
+  const int32_t y0 = static_cast<int32_t>(s * bd.max_seq), xh = static_cast<int32_t>(h * kHD);
+
+  if (warp == 0 && lane != 0) {
+    if (prefetch) {
+      uint64_t pol;
+      asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+      const uint64_t ctas = static_cast<uint64_t>(gridDim.x) * gridDim.y, c = blockIdx.y * gridDim.x + blockIdx.x;
+      const uint64_t b0 = (prefetch_bytes * c / ctas) & ~uint64_t(15), b1 = (prefetch_bytes * (c + 1) / ctas) & ~uint64_t(15);
+      for (uint64_t off = b0 + (lane - 1) * 32768ull; off < b1; off += 31 * 32768ull) {
+        const uint32_t len = static_cast<uint32_t>(b1 - off < 32768ull ? b1 - off : 32768ull);
+        asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(prefetch + off), "r"(len),
+                     "l"(pol)
+                     : "memory");
+      }
+    }
+  } else if (warp == 0) {
+    // Producer: stages 0 .. nst-1 are K, nst .. 2 nst - 1 are V. Stages
+    // without the newest row may go before the wait; the two that hold it
+    // wait until this CTA has written that row (hd_ready).
+    const uint64_t kv_pol = evict_first_policy();
+    auto issue = [&](uint32_t i, uint32_t slot) {
+      const bool is_v = i >= nst;
+      const int32_t y = y0 + static_cast<int32_t>((is_v ? i - nst : i) * kTcPos);
+      const CUtensorMap *m = is_v ? &map_v : &map_k;
+      mbar_expect_tx(&full[slot], kTcStage);
+      tma_load_2d(ring + slot * kTcStage, m, xh, y, &full[slot], kv_pol);
+      tma_load_2d(ring + slot * kTcStage + kTcBox, m, xh + 64, y, &full[slot], kv_pol);
+    };
+    uint32_t i = 0;
+    for (; i < kTcStages && i + 1 < nst; ++i) issue(i, i);  // K stages below the last one
+    grid_dep_wait();
+    bool have_row = false;
+    for (; i < 2 * nst; ++i) {
+      const uint32_t slot = i % kTcStages, use = i / kTcStages;
+      if (use > 0 && (failed_now(&failed) || !mbar_wait(&empty[slot], (use - 1) & 1))) { failed = 1; break; }
+      if (!have_row && (i == nst - 1 || i == 2 * nst - 1)) {
+        if (!mbar_wait(&hd_ready, 0)) { failed = 1; break; }
+        have_row = true;
+      }
+      issue(i, slot);
+    }
+    issued_n = i;
+  } else if (warp == 1) {
+    if (lane == 0) {
+      uint32_t i = 0;
+      bool ok = mbar_wait(&hd_ready, 0);  // q in shared memory
+      tc_fence_after();
+      // pass 1: scores
+      for (; ok && i < nst; ++i) {
+        const uint32_t slot = i % kTcStages, b = i & 1;
+        if (i >= 2 && !mbar_wait(&s_empty[b], ((i >> 1) - 1) & 1)) { ok = false; break; }
+        if (!mbar_wait(&full[slot], (i / kTcStages) & 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sa = smem_addr(ring + slot * kTcStage), sq = smem_addr(qs);
+#pragma unroll
+        for (uint32_t kk = 0; kk < 8; ++kk)
+          mma1_f16(tmem + b * kTcN, smem_desc(sa + (kk / 4) * kTcBox + 32 * (kk % 4), 16, 1024),
+                   smem_desc(sq + (kk / 4) * kPAtom + 32 * (kk % 4), 16, 1024), kIdescS, kk ? 1u : 0u);
+        mma1_commit(&empty[slot]);
+        mma1_commit(&s_full[b]);
+      }
+      // pass 2: p . v
+      if (ok) ok = mbar_wait(&p_ready, 0);
+      tc_fence_after();
+      for (uint32_t j = 0; ok && j < nst; ++j, ++i) {
+        const uint32_t slot = i % kTcStages;
+        if (!mbar_wait(&full[slot], (i / kTcStages) & 1)) { ok = false; break; }
+        if (j + 1 == nst) {
+          // The last V stage has landed: the compute warps zero its rows
+          // past the context before it is read (they learn of the landing
+          // from this thread, which observes the ring's phases in order).
+          mbar_arrive(&last_landed);
+          if (!mbar_wait(&v_patched, 0)) { ok = false; break; }
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_addr(ring + slot * kTcStage), sp = smem_addr(ps) + j * 2 * kPAtom;
+#pragma unroll
+        for (uint32_t kk = 0; kk < 8; ++kk)
+          mma1_f16(tmem + 2 * kTcN, smem_desc(sa + kk * 2048, kTcBox, 1024),
+                   smem_desc(sp + (kk / 4) * kPAtom + 32 * (kk % 4), 16, 1024), kIdescO, (j | kk) ? 1u : 0u);
+        mma1_commit(&empty[slot]);
+      }
+      if (ok) mma1_commit(&o_full);
+      if (!ok) failed = 1;
+      consumed_n = i;
+      mma1_commit(&mma_done);
+      if (!mbar_wait(&mma_done, 0)) failed = 1;
+    }
+  } else {
+    // Compute warps 2-5: thread et; TMEM lane quarter (warp % 4).
+    grid_dep_wait();
+    if (threadIdx.x == 64) trace_mark(bd, bb, 1);
+    const uint32_t et = threadIdx.x - 64, quarter = warp & 3, cw = warp - 2;
+    bool dead = false;
+    // Padding rows G..15 of q and of every P atom are zero.
+    for (uint32_t k = et; k < 2 * (kTcN - G) * 8; k += 128) {
+      const uint32_t atom = k / ((kTcN - G) * 8), rem = k % ((kTcN - G) * 8);
+      *reinterpret_cast<uint4 *>(qs + atom * kPAtom + (G + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
+    }
+    for (uint32_t k = et; k < 2 * nst * (kTcN - G) * 8; k += 128) {
+      const uint32_t atom = k / ((kTcN - G) * 8), rem = k % ((kTcN - G) * 8);
+      *reinterpret_cast<uint4 *>(ps + atom * kPAtom + (G + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
+    }
+    // Head epilogues at the newest position: q into shared memory, k and v
+    // into the caches.
+    for (uint32_t k = cw; k < static_cast<uint32_t>(G) + 2; k += 4) {
+      const uint32_t col = k < G ? h * G + k : (k == G ? bd.QH + h : bd.QH + bd.KVH + h);
+      float out[4];
+      head_finish(bd, bb, w, s, col, pos_new, out);
+      if (k < G) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t d = lane + 32 * j;
+          *reinterpret_cast<uint16_t *>(qs + (d / 64) * kPAtom + swz(k, d % 64)) = float_to_bf16_bits(out[j]);
+        }
+      } else {
+        bf16 *cache = (k == G ? w.kcache : w.vcache) + s * bb.kv_seq_stride +
+                      (static_cast<size_t>(pos_new) * bd.KVH + h) * kHD;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) putv(cache, lane + 32 * j, out[j]);
+      }
+    }
+    // Shared writes -> tensor-core reads; global cache writes -> TMA reads.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&hd_ready);
+    // pass 1: scores of position p = 128 i + 32 quarter + lane
+    float m[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) m[g] = -INFINITY;
+    for (uint32_t i = 0; i < nst; ++i) {
+      const uint32_t b = i & 1;
+      if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&s_full[b], (i >> 1) & 1));
+      float acc[16];
+#pragma unroll
+      for (int g = 0; g < 16; ++g) acc[g] = 0.f;
+      if (!dead) {
+        tc_fence_after();
+        tmem_ld16(tmem + ((quarter * 32u) << 16) + b * kTcN, acc);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[b]);
+      const uint32_t p = i * kTcPos + quarter * 32 + lane;
+      if (p < n) {
+        uint8_t *atom = ps + (p / 64) * kPAtom;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float sv = round_bf16(__fmul_rn(round_bf16(acc[g]), kAttnScale));
+          *reinterpret_cast<uint16_t *>(atom + swz(g, p % 64)) = float_to_bf16_bits(sv);
+          m[g] = fmaxf(m[g], sv);
+        }
+      }
+    }
+    // softmax statistics per head (quarters in order)
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float wm = warp_max(m[g]);
+      if (lane == 0) red[quarter][g] = wm;
+    }
+    tc_sync();
+    if (et < static_cast<uint32_t>(G)) sM[et] = fmaxf(fmaxf(red[0][et], red[1][et]), fmaxf(red[2][et], red[3][et]));
+    tc_sync();
+    float l[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) l[g] = 0.f;
+    for (uint32_t p = et; p < n; p += 128) {
+      const uint8_t *atom = ps + (p / 64) * kPAtom;
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+        l[g] += expf(bf16_bits_to_float(*reinterpret_cast<const uint16_t *>(atom + swz(g, p % 64))) - sM[g]);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float ws = warp_sum(l[g]);
+      if (lane == 0) red[quarter][g] = ws;
+    }
+    tc_sync();
+    if (et < static_cast<uint32_t>(G)) sInv[et] = 1.0f / (((red[0][et] + red[1][et]) + red[2][et]) + red[3][et]);
+    tc_sync();
+    for (uint32_t p = et; p < nst * kTcPos; p += 128) {
+      uint8_t *atom = ps + (p / 64) * kPAtom;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        uint16_t *e = reinterpret_cast<uint16_t *>(atom + swz(g, p % 64));
+        *e = p < n ? float_to_bf16_bits(__fmul_rn(expf(bf16_bits_to_float(*e) - sM[g]), sInv[g])) : 0;
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&p_ready);
+    // Zero the last V stage's rows past the context once it has landed.
+    {
+      const uint32_t slot = (2 * nst - 1) % kTcStages;
+      if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&last_landed, 0));
+      const uint32_t valid = n - (nst - 1) * kTcPos;
+      if (!dead)
+        for (uint32_t k = valid * 8 + et; k < kTcPos * 8; k += 128) {  // 16-byte pieces of rows valid..127
+          const uint32_t row = k / 8, piece = k % 8;
+          uint8_t *st = ring + slot * kTcStage;
+          *reinterpret_cast<uint4 *>(st + row * 128 + piece * 16) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4 *>(st + kTcBox + row * 128 + piece * 16) = make_uint4(0, 0, 0, 0);
+        }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&v_patched);
+    }
+    // output: dim d = 32 quarter + lane of the group's heads
+    if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&o_full, 0));
+    float o[16];
+#pragma unroll
+    for (int g = 0; g < 16; ++g) o[g] = 0.f;
+    if (!dead) {
+      tc_fence_after();
+      tmem_ld16(tmem + ((quarter * 32u) << 16) + 2 * kTcN, o);
+    }
+    const uint32_t d = quarter * 32 + lane;
+#pragma unroll
+    for (int g = 0; g < G; ++g) putv(bb.attn, (static_cast<size_t>(s) * bd.QH + h * G + g) * kHD + d, o[g]);
+    if (dead) failed = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (failed) {
+      const uint32_t from = consumed_n > issued_n ? issued_n : consumed_n;
+      for (uint32_t i = from; i < issued_n; ++i)
+        if (!mbar_wait(&full[i % kTcStages], (i / kTcStages) & 1)) break;
+      atomicOr(bb.error, kErrPipelineTimeout);
+    }
+    trace_mark(bd, bb, 2);
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc1(tmem, kTcTmemCols);
+  }
+}
+
 // --------------------------------------------------------------- argmax ----
 // Per sequence: the lm tiles' candidates in tile order -> greedy token
 // (lowest index on ties; 0xffffffff when any logit was NaN/Inf), then the
@@ -1084,8 +1432,21 @@ int smem_optin() {
 // (scores, then p.v with a last-CTA combine) per (chunk, head, sequence).
 template <int G>
 cudaError_t launch_battention(const BatchDims &d, const BatchBuffers &b, const LayerWeights &w, cudaStream_t s) {
-  const size_t smem = attn_smem_bytes(G, d.max_seq);
   const uint64_t rows = static_cast<uint64_t>(d.batch) * d.max_seq;
+  const uint64_t o_bytes = static_cast<uint64_t>(d.H) * d.QH * kHD * 2;
+  const size_t tc_smem = tc_attn_smem_bytes(d.max_seq);
+  if (tc_smem + 4096 <= static_cast<size_t>(smem_optin()) && rows >= kTcPos) {
+    CUtensorMap mk, mv;
+    cudaError_t e = make_tmap_2d_u16_swizzled(&mk, w.kcache, static_cast<uint64_t>(d.KVH) * kHD, rows,
+                                              static_cast<uint64_t>(d.KVH) * kHD, 64, kTcPos);
+    if (e != cudaSuccess) return e;
+    e = make_tmap_2d_u16_swizzled(&mv, w.vcache, static_cast<uint64_t>(d.KVH) * kHD, rows,
+                                  static_cast<uint64_t>(d.KVH) * kHD, 64, kTcPos);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(k_battn_tc<G>, dim3(d.KVH, d.batch), dim3(kTcThreads), tc_smem, s, d, b, w, mk, mv,
+                      reinterpret_cast<const uint8_t *>(w.wo), o_bytes);
+  }
+  const size_t smem = attn_smem_bytes(G, d.max_seq);
   if (smem + 4096 <= static_cast<size_t>(smem_optin()) && rows >= kAttnPos) {
     CUtensorMap mk, mv;
     cudaError_t e = make_tmap_2d_u16(&mk, w.kcache, static_cast<uint64_t>(d.KVH) * kHD, rows,
@@ -1094,7 +1455,9 @@ cudaError_t launch_battention(const BatchDims &d, const BatchBuffers &b, const L
     e = make_tmap_2d_u16(&mv, w.vcache, static_cast<uint64_t>(d.KVH) * kHD, rows, static_cast<uint64_t>(d.KVH) * kHD,
                          kHD, kAttnPos);
     if (e != cudaSuccess) return e;
-    return launch_pdl(k_battn<G>, dim3(d.KVH, d.batch), dim3(kAttnThreads), smem, s, d, b, w, mk, mv);
+    return launch_pdl(k_battn<G>, dim3(d.KVH, d.batch), dim3(kAttnThreads), smem, s, d, b, w, mk, mv,
+                      reinterpret_cast<const uint8_t *>(w.wo),
+                      static_cast<uint64_t>(d.H) * d.QH * kHD * 2);
   }
   cudaError_t e = launch_pdl(k_bheads, dim3(d.KVH, d.batch), dim3(256), 0, s, d, b, w);
   if (e != cudaSuccess) return e;
