@@ -308,7 +308,10 @@ def run_ours(args) -> None:
     if world > 1:
         eng.connect_tensor_parallel(dist.new_group(backend="gloo"))
     prompt = seeded_prompt(args.context, shape.vocab)
-    eng.generate(prompt, 1)  # device-resident prefill, token by token
+    if world == 1:
+        eng.prefill(prompt)  # chunked prefill: 16 positions per batched tcgen05 step
+    else:
+        eng.generate(prompt, 1)  # tensor parallel: device-resident prefill, token by token
     stream = torch.cuda.ExternalStream(eng.info().stream, device=device)
     eng.enqueue_steps(W)
     eng.synchronize()

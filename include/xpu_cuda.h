@@ -303,8 +303,18 @@ uint64_t xpu_qwen3_bytes_per_token(xpu_qwen3_engine *engine, uint32_t context);
  *   xpu_qwen3_generate; all sequences advance together, one host sync.
  * xpu_qwen3_batch_set_state / _enqueue_steps / _get_state: device-resident
  *   stepping of the batch set up by the last batched call.
- * xpu_qwen3_batch_logits: bf16 logits of sequence `sequence` of the last step. */
+ * xpu_qwen3_batch_logits: bf16 logits of row `sequence` (< 16) of the last
+ *   batched step: sequence s of a batch, or after xpu_qwen3_prefill the last
+ *   chunk's positions, the last prompt position in row (prompt_len - 1) % 16. */
 #define XPU_MAX_BATCH 16
+/* Chunked prefill of the batch-1 sequence (replaces the token-by-token prompt
+ * loop of qwen3/main.cpp:343-344): prompt[0..prompt_len) runs 16 positions
+ * per step through the batched GEMMs, with causal attention inside each
+ * chunk, writing the batch-1 KV cache; then the engine's state continues at
+ * position prompt_len with *next_token (the greedy token after the prompt),
+ * so xpu_qwen3_enqueue_steps / xpu_qwen3_decode carry on from there. One
+ * GPU only. */
+int xpu_qwen3_prefill(xpu_qwen3_engine *engine, const uint32_t *prompt, uint32_t prompt_len, uint32_t *next_token);
 int xpu_qwen3_create_batched(const xpu_qwen3_shape *shape, uint32_t maximum_sequence, int device,
                              uint32_t max_batch, xpu_qwen3_engine **out);
 int xpu_qwen3_batch_decode(xpu_qwen3_engine *engine, uint32_t batch, const uint32_t *tokens,

@@ -59,6 +59,8 @@ struct BatchDims {
   uint32_t batch;          // active sequences (1..16)
   float eps;
   uint32_t trace_slot;     // this launch's slot in BatchBuffers::trace
+  uint32_t seq_rows;       // cache rows between two sequences: max_seq, or 0 when
+                           // every sequence is a position of one prompt (prefill)
 };
 
 struct BatchBuffers {
@@ -103,7 +105,10 @@ uint32_t batch_max_tiles(const BatchDims &d);
 uint32_t batch_gemm_grid();
 
 // Records one batched step (d.batch sequences) on `s` (graph capture).
+// prefill: the d.batch "sequences" are consecutive positions of one prompt
+// sharing one cache (d.seq_rows = 0, b.kv_seq_stride = 0); every position's
+// k and v are finished and cached before attention reads them.
 cudaError_t record_batch_step(const BatchDims &d, const BatchBuffers &b, const LayerWeights *layers,
-                              uint32_t n_layers, cudaStream_t s);
+                              uint32_t n_layers, cudaStream_t s, bool prefill = false);
 
 }  // namespace xpu

@@ -1040,7 +1040,9 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) {
 
 __device__ __forceinline__ void tc_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-template <int G>
+// HEADS: the CTA finishes its group's heads (decode); otherwise q, k and v
+// are finished and cached by k_bheads first (prefill).
+template <int G, bool HEADS>
 __global__ void __launch_bounds__(kTcThreads, 1)
 k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant__ CUtensorMap map_k,
            const __grid_constant__ CUtensorMap map_v, const uint8_t *prefetch, uint64_t prefetch_bytes) {
@@ -1084,7 +1086,7 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
   const uint32_t tmem = tmem_base;
   grid_dep_launch();
   if (threadIdx.x == 0) trace_mark(bd, bb, 0);
-  const int32_t y0 = static_cast<int32_t>(s * bd.max_seq), xh = static_cast<int32_t>(h * kHD);
+  const int32_t y0 = static_cast<int32_t>(s * bd.seq_rows), xh = static_cast<int32_t>(h * kHD);
 
   if (warp == 0 && lane != 0) {
     if (prefetch) {
@@ -1099,6 +1101,22 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
                      : "memory");
       }
     }
+  } else if (warp == 0 && !HEADS) {
+    // Prefill: every row this CTA reads was cached by earlier kernels.
+    const uint64_t kv_pol = evict_first_policy();
+    grid_dep_wait();
+    uint32_t i = 0;
+    for (; i < 2 * nst; ++i) {
+      const uint32_t slot = i % kTcStages, use = i / kTcStages;
+      if (use > 0 && (failed_now(&failed) || !mbar_wait(&empty[slot], (use - 1) & 1))) { failed = 1; break; }
+      const bool is_v = i >= nst;
+      const int32_t y = y0 + static_cast<int32_t>((is_v ? i - nst : i) * kTcPos);
+      const CUtensorMap *m = is_v ? &map_v : &map_k;
+      mbar_expect_tx(&full[slot], kTcStage);
+      tma_load_2d(ring + slot * kTcStage, m, xh, y, &full[slot], kv_pol);
+      tma_load_2d(ring + slot * kTcStage + kTcBox, m, xh + 64, y, &full[slot], kv_pol);
+    }
+    issued_n = i;
   } else if (warp == 0) {
     // Producer: stages 0 .. nst-1 are K, nst .. 2 nst - 1 are V. Stages
     // without the newest row may go before the wait; the two that hold it
@@ -1188,8 +1206,14 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
       *reinterpret_cast<uint4 *>(ps + atom * kPAtom + (G + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
     }
     // Head epilogues at the newest position: q into shared memory, k and v
-    // into the caches.
-    for (uint32_t k = cw; k < static_cast<uint32_t>(G) + 2; k += 4) {
+    // into the caches (prefill: q from k_bheads).
+    if (!HEADS)
+      for (uint32_t k = et; k < G * kHD; k += 128) {
+        const uint32_t g = k / kHD, d = k % kHD;
+        *reinterpret_cast<uint16_t *>(qs + (d / 64) * kPAtom + swz(g, d % 64)) =
+            reinterpret_cast<const uint16_t *>(bb.q)[(static_cast<size_t>(s) * bd.QH + h * G + g) * kHD + d];
+      }
+    for (uint32_t k = cw; HEADS && k < static_cast<uint32_t>(G) + 2; k += 4) {
       const uint32_t col = k < G ? h * G + k : (k == G ? bd.QH + h : bd.QH + bd.KVH + h);
       float out[4];
       head_finish(bd, bb, w, s, col, pos_new, out);
@@ -1431,8 +1455,9 @@ int smem_optin() {
 // spans at least one stage; otherwise the batch-1 chunked kernels
 // (scores, then p.v with a last-CTA combine) per (chunk, head, sequence).
 template <int G>
-cudaError_t launch_battention(const BatchDims &d, const BatchBuffers &b, const LayerWeights &w, cudaStream_t s) {
-  const uint64_t rows = static_cast<uint64_t>(d.batch) * d.max_seq;
+cudaError_t launch_battention(const BatchDims &d, const BatchBuffers &b, const LayerWeights &w, cudaStream_t s,
+                              bool prefill) {
+  const uint64_t rows = prefill ? d.max_seq : static_cast<uint64_t>(d.batch) * d.max_seq;
   const uint64_t o_bytes = static_cast<uint64_t>(d.H) * d.QH * kHD * 2;
   const size_t tc_smem = tc_attn_smem_bytes(d.max_seq);
   if (tc_smem + 4096 <= static_cast<size_t>(smem_optin()) && rows >= kTcPos) {
@@ -1443,11 +1468,17 @@ cudaError_t launch_battention(const BatchDims &d, const BatchBuffers &b, const L
     e = make_tmap_2d_u16_swizzled(&mv, w.vcache, static_cast<uint64_t>(d.KVH) * kHD, rows,
                                   static_cast<uint64_t>(d.KVH) * kHD, 64, kTcPos);
     if (e != cudaSuccess) return e;
-    return launch_pdl(k_battn_tc<G>, dim3(d.KVH, d.batch), dim3(kTcThreads), tc_smem, s, d, b, w, mk, mv,
+    if (prefill) {
+      e = launch_pdl(k_bheads, dim3(d.KVH, d.batch), dim3(256), 0, s, d, b, w);
+      if (e != cudaSuccess) return e;
+      return launch_pdl(k_battn_tc<G, false>, dim3(d.KVH, d.batch), dim3(kTcThreads), tc_smem, s, d, b, w, mk, mv,
+                        reinterpret_cast<const uint8_t *>(w.wo), o_bytes);
+    }
+    return launch_pdl(k_battn_tc<G, true>, dim3(d.KVH, d.batch), dim3(kTcThreads), tc_smem, s, d, b, w, mk, mv,
                       reinterpret_cast<const uint8_t *>(w.wo), o_bytes);
   }
   const size_t smem = attn_smem_bytes(G, d.max_seq);
-  if (smem + 4096 <= static_cast<size_t>(smem_optin()) && rows >= kAttnPos) {
+  if (!prefill && smem + 4096 <= static_cast<size_t>(smem_optin()) && rows >= kAttnPos) {
     CUtensorMap mk, mv;
     cudaError_t e = make_tmap_2d_u16(&mk, w.kcache, static_cast<uint64_t>(d.KVH) * kHD, rows,
                                      static_cast<uint64_t>(d.KVH) * kHD, kHD, kAttnPos);
@@ -1476,7 +1507,7 @@ uint32_t batch_max_tiles(const BatchDims &d) {
 }
 
 cudaError_t record_batch_step(const BatchDims &d0, const BatchBuffers &b, const LayerWeights *layers,
-                              uint32_t n_layers, cudaStream_t s) {
+                              uint32_t n_layers, cudaStream_t s, bool prefill) {
   if (d0.batch < 1 || d0.batch > kMaxBatch) return cudaErrorInvalidValue;
   BatchDims d = d0;
   uint32_t slot = 0;
@@ -1509,10 +1540,10 @@ cudaError_t record_batch_step(const BatchDims &d0, const BatchBuffers &b, const 
       XPU_TRY((launch_bgemm<kEpiQkv, true>(w.wqkv, (d.QH + 2 * d.KVH) * kHD, d.H, b.x, at(pq), s)));
     const BatchDims da = next();
     switch (G) {
-      case 1: XPU_TRY(launch_battention<1>(da, b, w, s)); break;
-      case 2: XPU_TRY(launch_battention<2>(da, b, w, s)); break;
-      case 4: XPU_TRY(launch_battention<4>(da, b, w, s)); break;
-      case 8: XPU_TRY(launch_battention<8>(da, b, w, s)); break;
+      case 1: XPU_TRY(launch_battention<1>(da, b, w, s, prefill)); break;
+      case 2: XPU_TRY(launch_battention<2>(da, b, w, s, prefill)); break;
+      case 4: XPU_TRY(launch_battention<4>(da, b, w, s, prefill)); break;
+      case 8: XPU_TRY(launch_battention<8>(da, b, w, s, prefill)); break;
       default: return cudaErrorInvalidValue;
     }
     BGemm po{};

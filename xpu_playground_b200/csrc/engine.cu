@@ -24,6 +24,7 @@
 #include <cstddef>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <memory>
 #include <string>
 #include <vector>
@@ -103,6 +104,8 @@ class Qwen3Engine {
     cudaSetDevice(device_);
     if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
     if (batch_exec_) cudaGraphExecDestroy(batch_exec_);
+    for (auto &kv : prefill_exec_) cudaGraphExecDestroy(kv.second);
+    if (host_prefill_) cudaFreeHost(host_prefill_);
     if (plan_) step_plan_destroy(plan_);
     if (stream_) cudaStreamSynchronize(stream_);
     for (void *p : peer_regions_) cudaIpcCloseMemHandle(p);
@@ -519,6 +522,57 @@ class Qwen3Engine {
     }
   }
 
+  // Chunked prefill of the batch-1 sequence: prompt[0..n) goes through the
+  // batched step 16 positions at a time (each position one "sequence" of a
+  // batch sharing the batch-1 KV cache, so the projections are tcgen05
+  // GEMMs over 16 tokens instead of 16 GEMV passes). The batch-1 state is
+  // then set to continue at position n with the greedy token after the
+  // prompt, which is returned (qwen3/main.cpp:343-344 feeds the prompt
+  // token by token instead). Single GPU only.
+  uint32_t prefill(const uint32_t *prompt, uint32_t n) {
+    if (tp_ > 1) throw InvalidArg("chunked prefill runs on one GPU (tp_size 1)");
+    if (n == 0) throw InvalidArg("at least one prompt token is required");
+    if (n > max_seq_) throw InvalidArg("prompt exceeds the maximum sequence");
+    for (uint32_t i = 0; i < n; ++i)
+      if (prompt[i] >= shape_.vocab_size) throw InvalidArg("prompt token id outside the vocabulary");
+    if (!loaded_) throw InvalidArg("no weights: call init_synthetic, load a checkpoint or set every tensor");
+    if (!bb_.x) allocate_batch();
+    CK(cudaSetDevice(device_));
+    const uint32_t chunks = (n + kMaxBatch - 1) / kMaxBatch;
+    if (prefill_cap_ < chunks) {
+      if (host_prefill_) CK(cudaFreeHost(host_prefill_));
+      host_prefill_ = nullptr;
+      CK(cudaMallocHost(&host_prefill_, static_cast<size_t>(chunks) * kMaxBatch * sizeof(SeqState)));
+      prefill_cap_ = chunks;
+    }
+    CK(cudaStreamSynchronize(stream_));  // the staging area may still feed an earlier call
+    *host_berr_ = 0;
+    CK(cudaMemcpyAsync(bb_.error, host_berr_, sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
+    uint32_t last = 0;
+    for (uint32_t k = 0; k < chunks; ++k) {
+      const uint32_t c = std::min<uint32_t>(kMaxBatch, n - k * kMaxBatch);
+      SeqState *st = host_prefill_ + static_cast<size_t>(k) * kMaxBatch;
+      for (uint32_t s = 0; s < c; ++s) st[s] = SeqState{prompt[k * kMaxBatch + s], k * kMaxBatch + s, 0, 0};
+      CK(cudaMemcpyAsync(bb_.seq, st, c * sizeof(SeqState), cudaMemcpyHostToDevice, stream_));
+      CK(cudaGraphLaunch(prefill_graph(c), stream_));
+      last = c - 1;
+    }
+    SeqState tail{};
+    CK(cudaMemcpyAsync(&tail, bb_.seq + last, sizeof(SeqState), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaMemcpyAsync(host_berr_, bb_.error, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    after_batch_check();
+    if (*host_berr_ & 1u) throw InvalidArg("prefill met a NaN/Inf logit or an invalid token");
+    *host_state_ = DecodeState{};
+    host_state_->token = tail.next;
+    host_state_->next = tail.next;
+    host_state_->position = n;
+    write_state();
+    CK(cudaMemcpyAsync(log_ + (n - 1), &tail.next, sizeof(uint32_t), cudaMemcpyHostToDevice, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    return tail.next;
+  }
+
   // Set sequences 0..n-1 (token, position) without running; enqueue_steps
   // then advances them device-resident.
   void batch_set_state(uint32_t n, const uint32_t *tokens, const uint32_t *positions) {
@@ -564,7 +618,7 @@ class Qwen3Engine {
   }
 
   void batch_logits(uint32_t seq, uint16_t *host, uint32_t count) {
-    if (seq >= batch_cap_) throw InvalidArg("sequence index outside the batch capacity");
+    if (seq >= kMaxBatch) throw InvalidArg("sequence index outside the batch (16 rows)");
     if (!bb_.logits) throw InvalidArg("no batched step has run");
     if (count > shape_.vocab_size) throw InvalidArg("logit count exceeds the vocabulary");
     CK(cudaMemcpyAsync(host, bb_.logits + static_cast<size_t>(seq) * shape_.vocab_size, count * 2ull,
@@ -635,6 +689,7 @@ class Qwen3Engine {
     bd_.nchunks = pos_chunks(max_seq_);
     bd_.batch = 1;
     bd_.eps = s.rms_norm_eps;
+    bd_.seq_rows = max_seq_;
     const uint64_t B = kMaxBatch, H = bd_.H, Q = bd_.QH * 128ull;
     BatchBuffers b{};
     b.x = dev_zeros<bf16>(B * H);
@@ -673,6 +728,33 @@ class Qwen3Engine {
     bb_ = b;
     CK(cudaMallocHost(&host_seq_, kMaxBatch * sizeof(SeqState) + 16));
     host_berr_ = reinterpret_cast<uint32_t *>(host_seq_ + kMaxBatch);
+  }
+
+  // The prefill graph for chunks of c positions (built once per c).
+  cudaGraphExec_t prefill_graph(uint32_t c) {
+    auto it = prefill_exec_.find(c);
+    if (it != prefill_exec_.end()) return it->second;
+    BatchDims d = bd_;
+    d.batch = c;
+    d.seq_rows = 0;
+    BatchBuffers b = bb_;
+    b.kv_seq_stride = 0;
+    std::vector<LayerWeights> lw(shape_.num_hidden_layers);
+    for (uint32_t l = 0; l < shape_.num_hidden_layers; ++l) lw[l] = layer_weights(l);
+    cudaGraph_t graph = nullptr;
+    CK(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+    const cudaError_t rec = record_batch_step(d, b, lw.data(), shape_.num_hidden_layers, stream_, true);
+    const cudaError_t end = cudaStreamEndCapture(stream_, &graph);
+    if (rec != cudaSuccess || end != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      CK(rec != cudaSuccess ? rec : end);
+    }
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    CK(e);
+    prefill_exec_[c] = exec;
+    return exec;
   }
 
   // Builds (once per batch size) the batched step graph for n sequences.
@@ -1010,6 +1092,9 @@ class Qwen3Engine {
   SeqState *host_seq_ = nullptr;
   uint32_t *host_berr_ = nullptr;
   unsigned long long *btrace_ = nullptr;  // batched step trace (XPU_BATCH_TRACE=1)
+  std::map<uint32_t, cudaGraphExec_t> prefill_exec_;  // chunked-prefill graphs by chunk size
+  SeqState *host_prefill_ = nullptr;                 // pinned per-chunk step states
+  uint32_t prefill_cap_ = 0;
 };
 
 }  // namespace xpu
@@ -1186,6 +1271,16 @@ int xpu_qwen3_set_mode(xpu_qwen3_engine *engine, int mode) {
 
 int xpu_qwen3_synchronize(xpu_qwen3_engine *engine) {
   return guarded([&] { eng(engine).sync(); });
+}
+
+int xpu_qwen3_prefill(xpu_qwen3_engine *engine, const uint32_t *prompt, uint32_t prompt_len, uint32_t *next_token) {
+  int status = guarded([&] {
+    if (!prompt || !next_token) throw xpu::InvalidArg("xpu_qwen3_prefill: null pointer");
+    *next_token = eng(engine).prefill(prompt, prompt_len);
+  });
+  if (status == XPU_OK && *next_token == 0xffffffffu)
+    return xpu::fail(XPU_ERR_NONFINITE, "model produced a NaN or infinity in vocabulary logits");
+  return status;
 }
 
 int xpu_qwen3_batch_decode(xpu_qwen3_engine *engine, uint32_t batch, const uint32_t *tokens,

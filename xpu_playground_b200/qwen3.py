@@ -178,6 +178,15 @@ class Qwen3Engine:
     def bytes_per_token(self, context: int) -> int:
         return int(self.lib.xpu_qwen3_bytes_per_token(self._h, context))
 
+    def prefill(self, prompt: list[int]) -> int:
+        """Chunked prefill (16 positions per batched step) of the batch-1
+        sequence; returns the greedy token after the prompt and leaves the
+        state at position len(prompt) (xpu_qwen3_prefill)."""
+        p = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = ctypes.c_uint32()
+        _lib.check(self.lib.xpu_qwen3_prefill(self._h, p.ctypes.data, p.size, ctypes.byref(out)))
+        return out.value
+
     # ----------------------------------------------------- batched decode ----
     def batch_decode(self, tokens: list[int], positions: list[int]) -> list[int]:
         """One step of len(tokens) sequences (xpu_qwen3_batch_decode)."""
