@@ -308,8 +308,15 @@ def run_ours(args) -> None:
     if world > 1:
         eng.connect_tensor_parallel(dist.new_group(backend="gloo"))
     prompt = seeded_prompt(args.context, shape.vocab)
+    prefill_info = None
     if world == 1:
-        eng.prefill(prompt)  # chunked prefill: 16 positions per batched tcgen05 step
+        eng.synchronize()
+        t_pre = time.perf_counter()
+        eng.prefill(prompt)  # chunked prefill: 16 positions per batched tcgen05 step (synchronous)
+        t_pre = time.perf_counter() - t_pre
+        prefill_info = {"tokens": args.context, "seconds": round(t_pre, 4),
+                        "tok_s": round(args.context / t_pre, 1), "positions_per_step": 16,
+                        "timing": "host wall clock around xpu_qwen3_prefill (synchronous)"}
     else:
         eng.generate(prompt, 1)  # tensor parallel: device-resident prefill, token by token
     stream = torch.cuda.ExternalStream(eng.info().stream, device=device)
@@ -360,6 +367,8 @@ def run_ours(args) -> None:
     peak, peak_kind = measured_peaks()
 
     extra = {}
+    if prefill_info:
+        extra["prefill"] = prefill_info
     if args.batch and world == 1:
         eng.synchronize()
         extra["batch_decode"] = batch_extra(torch, device, shape, args.context, args.batch,

@@ -1019,17 +1019,18 @@ k_battn(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant__ C
 constexpr uint32_t kTcPos = 128;                   // positions per stage
 constexpr uint32_t kTcBox = 128 * 64 * 2;          // one 64-dim box of a stage: 16 KB
 constexpr uint32_t kTcStage = 2 * kTcBox;          // 32 KB
-constexpr uint32_t kTcStages = 3;
+constexpr uint32_t kTcMaxStages = 6;             // ring slots: as many as fit next to P (>= 2)
 constexpr uint32_t kTcThreads = 192;
 constexpr uint32_t kTcN = 16;                      // MMA N: head slots
 constexpr uint32_t kPAtom = 16 * 128;              // 16 rows x 64 bf16: 2 KB
-constexpr uint32_t kTcTmemCols = 64;               // S[2] (2 x 16) + O (16)
+constexpr uint32_t kTcSBufs = 4;                   // TMEM score buffers (MMA runs up to 4 stages ahead)
+constexpr uint32_t kTcTmemCols = 128;              // S[4] (4 x 16) + O (16)
 constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((kTcN >> 3) << 17) | ((128u >> 4) << 24);
 constexpr uint32_t kIdescO = kIdescS | (1u << 15);  // A MN-major
 
-__host__ __device__ inline size_t tc_attn_smem_bytes(uint32_t max_seq) {
+__host__ __device__ inline size_t tc_attn_smem_bytes(uint32_t max_seq, uint32_t stages) {
   const size_t atoms = (static_cast<size_t>(max_seq) + kTcPos - 1) / kTcPos * 2;  // P atoms of whole stages
-  return 1024 + static_cast<size_t>(kTcStages) * kTcStage + 2 * kPAtom + atoms * kPAtom;
+  return 1024 + static_cast<size_t>(stages) * kTcStage + 2 * kPAtom + atoms * kPAtom;
 }
 
 // Byte offset of element (row r, column c < 64) inside a 128-byte swizzled
@@ -1045,26 +1046,28 @@ __device__ __forceinline__ void tc_sync() { asm volatile("bar.sync 1, 128;" ::: 
 template <int G, bool HEADS>
 __global__ void __launch_bounds__(kTcThreads, 1)
 k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant__ CUtensorMap map_k,
-           const __grid_constant__ CUtensorMap map_v, const uint8_t *prefetch, uint64_t prefetch_bytes) {
+           const __grid_constant__ CUtensorMap map_v, const uint8_t *prefetch, uint64_t prefetch_bytes,
+           uint32_t stages) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  __shared__ uint64_t full[kTcStages], empty[kTcStages], s_full[2], s_empty[2], hd_ready, p_ready, last_landed,
+  __shared__ uint64_t full[kTcMaxStages], empty[kTcMaxStages], s_full[kTcSBufs], s_empty[kTcSBufs], hd_ready, p_ready,
+      last_landed,
       v_patched, o_full, mma_done;
   __shared__ uint32_t tmem_base, issued_n, consumed_n;
   __shared__ float red[4][G], sM[G], sInv[G];
   __shared__ int failed;
   const uint32_t a0 = smem_addr(smem_raw);
   uint8_t *ring = smem_raw + ((a0 + 1023u) / 1024u * 1024u - a0);
-  uint8_t *qs = ring + kTcStages * kTcStage;  // 2 atoms: dims 0-63, 64-127
+  uint8_t *qs = ring + stages * kTcStage;  // 2 atoms: dims 0-63, 64-127
   uint8_t *ps = qs + 2 * kPAtom;              // P atoms, 64 positions each
   const uint32_t h = blockIdx.x, s = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t n = bb.seq[s].position + 1, pos_new = n - 1;
   const uint32_t nst = (n + kTcPos - 1) / kTcPos;
   if (threadIdx.x == 0) {
-    for (uint32_t i = 0; i < kTcStages; ++i) {
+    for (uint32_t i = 0; i < stages; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
-    for (uint32_t i = 0; i < 2; ++i) {
+    for (uint32_t i = 0; i < kTcSBufs; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 4);
     }
@@ -1107,7 +1110,7 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
     grid_dep_wait();
     uint32_t i = 0;
     for (; i < 2 * nst; ++i) {
-      const uint32_t slot = i % kTcStages, use = i / kTcStages;
+      const uint32_t slot = i % stages, use = i / stages;
       if (use > 0 && (failed_now(&failed) || !mbar_wait(&empty[slot], (use - 1) & 1))) { failed = 1; break; }
       const bool is_v = i >= nst;
       const int32_t y = y0 + static_cast<int32_t>((is_v ? i - nst : i) * kTcPos);
@@ -1131,11 +1134,11 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
       tma_load_2d(ring + slot * kTcStage + kTcBox, m, xh + 64, y, &full[slot], kv_pol);
     };
     uint32_t i = 0;
-    for (; i < kTcStages && i + 1 < nst; ++i) issue(i, i);  // K stages below the last one
+    for (; i < stages && i + 1 < nst; ++i) issue(i, i);  // K stages below the last one
     grid_dep_wait();
     bool have_row = false;
     for (; i < 2 * nst; ++i) {
-      const uint32_t slot = i % kTcStages, use = i / kTcStages;
+      const uint32_t slot = i % stages, use = i / stages;
       if (use > 0 && (failed_now(&failed) || !mbar_wait(&empty[slot], (use - 1) & 1))) { failed = 1; break; }
       if (!have_row && (i == nst - 1 || i == 2 * nst - 1)) {
         if (!mbar_wait(&hd_ready, 0)) { failed = 1; break; }
@@ -1151,9 +1154,9 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
       tc_fence_after();
       // pass 1: scores
       for (; ok && i < nst; ++i) {
-        const uint32_t slot = i % kTcStages, b = i & 1;
-        if (i >= 2 && !mbar_wait(&s_empty[b], ((i >> 1) - 1) & 1)) { ok = false; break; }
-        if (!mbar_wait(&full[slot], (i / kTcStages) & 1)) { ok = false; break; }
+        const uint32_t slot = i % stages, b = i % kTcSBufs;
+        if (i >= kTcSBufs && !mbar_wait(&s_empty[b], ((i / kTcSBufs) - 1) & 1)) { ok = false; break; }
+        if (!mbar_wait(&full[slot], (i / stages) & 1)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sa = smem_addr(ring + slot * kTcStage), sq = smem_addr(qs);
 #pragma unroll
@@ -1167,8 +1170,8 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
       if (ok) ok = mbar_wait(&p_ready, 0);
       tc_fence_after();
       for (uint32_t j = 0; ok && j < nst; ++j, ++i) {
-        const uint32_t slot = i % kTcStages;
-        if (!mbar_wait(&full[slot], (i / kTcStages) & 1)) { ok = false; break; }
+        const uint32_t slot = i % stages;
+        if (!mbar_wait(&full[slot], (i / stages) & 1)) { ok = false; break; }
         if (j + 1 == nst) {
           // The last V stage has landed: the compute warps zero its rows
           // past the context before it is read (they learn of the landing
@@ -1180,7 +1183,7 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
         const uint32_t sa = smem_addr(ring + slot * kTcStage), sp = smem_addr(ps) + j * 2 * kPAtom;
 #pragma unroll
         for (uint32_t kk = 0; kk < 8; ++kk)
-          mma1_f16(tmem + 2 * kTcN, smem_desc(sa + kk * 2048, kTcBox, 1024),
+          mma1_f16(tmem + kTcSBufs * kTcN, smem_desc(sa + kk * 2048, kTcBox, 1024),
                    smem_desc(sp + (kk / 4) * kPAtom + 32 * (kk % 4), 16, 1024), kIdescO, (j | kk) ? 1u : 0u);
         mma1_commit(&empty[slot]);
       }
@@ -1196,14 +1199,10 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
     if (threadIdx.x == 64) trace_mark(bd, bb, 1);
     const uint32_t et = threadIdx.x - 64, quarter = warp & 3, cw = warp - 2;
     bool dead = false;
-    // Padding rows G..15 of q and of every P atom are zero.
+    // Padding rows G..15 of q are zero (those of P after the heads).
     for (uint32_t k = et; k < 2 * (kTcN - G) * 8; k += 128) {
       const uint32_t atom = k / ((kTcN - G) * 8), rem = k % ((kTcN - G) * 8);
       *reinterpret_cast<uint4 *>(qs + atom * kPAtom + (G + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
-    }
-    for (uint32_t k = et; k < 2 * nst * (kTcN - G) * 8; k += 128) {
-      const uint32_t atom = k / ((kTcN - G) * 8), rem = k % ((kTcN - G) * 8);
-      *reinterpret_cast<uint4 *>(ps + atom * kPAtom + (G + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
     }
     // Head epilogues at the newest position: q into shared memory, k and v
     // into the caches (prefill: q from k_bheads).
@@ -1235,13 +1234,18 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
     asm volatile("fence.proxy.async.global;" ::: "memory");
     __syncwarp();
     if (lane == 0) mbar_arrive(&hd_ready);
+    if (et == 0) trace_mark(bd, bb, 5);  // heads finished
+    for (uint32_t k = et; k < 2 * nst * (kTcN - G) * 8; k += 128) {
+      const uint32_t atom = k / ((kTcN - G) * 8), rem = k % ((kTcN - G) * 8);
+      *reinterpret_cast<uint4 *>(ps + atom * kPAtom + (G + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
+    }
     // pass 1: scores of position p = 128 i + 32 quarter + lane
     float m[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) m[g] = -INFINITY;
     for (uint32_t i = 0; i < nst; ++i) {
-      const uint32_t b = i & 1;
-      if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&s_full[b], (i >> 1) & 1));
+      const uint32_t b = i % kTcSBufs;
+      if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&s_full[b], (i / kTcSBufs) & 1));
       float acc[16];
 #pragma unroll
       for (int g = 0; g < 16; ++g) acc[g] = 0.f;
@@ -1263,7 +1267,9 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
         }
       }
     }
-    // softmax statistics per head (quarters in order)
+    // softmax statistics per head (quarters in order); a running sum during
+    // pass 1 (online rescaling) measured slower: its exp sits on the
+    // per-stage path, this one after it.
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const float wm = warp_max(m[g]);
@@ -1300,9 +1306,10 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
     if (lane == 0) mbar_arrive(&p_ready);
+    if (et == 0) trace_mark(bd, bb, 6);  // probabilities ready
     // Zero the last V stage's rows past the context once it has landed.
     {
-      const uint32_t slot = (2 * nst - 1) % kTcStages;
+      const uint32_t slot = (2 * nst - 1) % stages;
       if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&last_landed, 0));
       const uint32_t valid = n - (nst - 1) * kTcPos;
       if (!dead)
@@ -1318,12 +1325,13 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
     }
     // output: dim d = 32 quarter + lane of the group's heads
     if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&o_full, 0));
+    if (et == 0) trace_mark(bd, bb, 7);  // output accumulated
     float o[16];
 #pragma unroll
     for (int g = 0; g < 16; ++g) o[g] = 0.f;
     if (!dead) {
       tc_fence_after();
-      tmem_ld16(tmem + ((quarter * 32u) << 16) + 2 * kTcN, o);
+      tmem_ld16(tmem + ((quarter * 32u) << 16) + kTcSBufs * kTcN, o);
     }
     const uint32_t d = quarter * 32 + lane;
 #pragma unroll
@@ -1336,7 +1344,7 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
     if (failed) {
       const uint32_t from = consumed_n > issued_n ? issued_n : consumed_n;
       for (uint32_t i = from; i < issued_n; ++i)
-        if (!mbar_wait(&full[i % kTcStages], (i / kTcStages) & 1)) break;
+        if (!mbar_wait(&full[i % stages], (i / stages) & 1)) break;
       atomicOr(bb.error, kErrPipelineTimeout);
     }
     trace_mark(bd, bb, 2);
@@ -1459,7 +1467,9 @@ cudaError_t launch_battention(const BatchDims &d, const BatchBuffers &b, const L
                               bool prefill) {
   const uint64_t rows = prefill ? d.max_seq : static_cast<uint64_t>(d.batch) * d.max_seq;
   const uint64_t o_bytes = static_cast<uint64_t>(d.H) * d.QH * kHD * 2;
-  const size_t tc_smem = tc_attn_smem_bytes(d.max_seq);
+  uint32_t stages = kTcMaxStages;
+  while (stages > 2 && tc_attn_smem_bytes(d.max_seq, stages) + 4096 > static_cast<size_t>(smem_optin())) --stages;
+  const size_t tc_smem = tc_attn_smem_bytes(d.max_seq, stages);
   if (tc_smem + 4096 <= static_cast<size_t>(smem_optin()) && rows >= kTcPos) {
     CUtensorMap mk, mv;
     cudaError_t e = make_tmap_2d_u16_swizzled(&mk, w.kcache, static_cast<uint64_t>(d.KVH) * kHD, rows,
@@ -1472,10 +1482,10 @@ cudaError_t launch_battention(const BatchDims &d, const BatchBuffers &b, const L
       e = launch_pdl(k_bheads, dim3(d.KVH, d.batch), dim3(256), 0, s, d, b, w);
       if (e != cudaSuccess) return e;
       return launch_pdl(k_battn_tc<G, false>, dim3(d.KVH, d.batch), dim3(kTcThreads), tc_smem, s, d, b, w, mk, mv,
-                        reinterpret_cast<const uint8_t *>(w.wo), o_bytes);
+                        reinterpret_cast<const uint8_t *>(w.wo), o_bytes, stages);
     }
     return launch_pdl(k_battn_tc<G, true>, dim3(d.KVH, d.batch), dim3(kTcThreads), tc_smem, s, d, b, w, mk, mv,
-                      reinterpret_cast<const uint8_t *>(w.wo), o_bytes);
+                      reinterpret_cast<const uint8_t *>(w.wo), o_bytes, stages);
   }
   const size_t smem = attn_smem_bytes(G, d.max_seq);
   if (!prefill && smem + 4096 <= static_cast<size_t>(smem_optin()) && rows >= kAttnPos) {

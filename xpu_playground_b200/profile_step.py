@@ -18,6 +18,20 @@ Under torchrun the ranks run one tensor-parallel engine and rank 0 reports:
 step, the mean/max over CTAs of the time spent staging the activation,
 streaming its items, finishing (arrivals and epilogues) and in the grid
 barrier, averaged over layers.
+
+--batch B profiles the batched step (B sequences, one CUDA graph of tcgen05
+GEMMs and attention kernels per step) instead: every sequence is prefilled
+through the batched step to `--context` positions, `--warm` steps follow, and
+one last step runs between cudaProfilerStart/Stop, so the launch list of one
+step is
+
+    ncu --metrics gpu__time_duration.sum --clock-control none --profile-from-start off \
+        --csv python -m xpu_playground_b200.profile_step --batch 16 --context 512
+
+With --trace it prints that step's per-kernel timeline (XPU_BATCH_TRACE=1):
+per kernel kind the critical-path time (end minus the previous kernel's end),
+when its wait on the previous kernel returned, when its last CTA saw its first
+stage and its final accumulator, and the epilogue tail.
 """
 
 from __future__ import annotations
@@ -39,7 +53,11 @@ def main() -> None:
     ap.add_argument("--warm", type=int, default=2)
     ap.add_argument("--mode", choices=["persistent", "graph"], default="persistent")
     ap.add_argument("--trace", action="store_true")
+    ap.add_argument("--batch", type=int, default=0, help="profile the batched step of this many sequences")
     args = ap.parse_args()
+    if args.batch:
+        batch_profile(args)
+        return
     if args.trace:
         os.environ["XPU_STEP_TRACE"] = "1"
 
@@ -103,6 +121,67 @@ def main() -> None:
         dist.barrier()
         eng.close()
         dist.destroy_process_group()
+
+
+def batch_profile(args) -> None:
+    if args.trace:
+        os.environ["XPU_BATCH_TRACE"] = "1"
+    import torch
+
+    from .qwen3 import Qwen3Engine
+    from .qwen3_config import PRESETS
+
+    shape, B = PRESETS[args.preset], args.batch
+    eng = Qwen3Engine(shape, args.context + args.warm + 8, max_batch=B)
+    eng.init_synthetic(2026)
+    rng = np.random.default_rng(7)
+    prompts = [[int(t) for t in rng.integers(0, shape.vocab, size=args.context)] for _ in range(B)]
+    eng.batch_generate(prompts, 1)  # prefill: every sequence at `context` positions
+    eng.batch_enqueue_steps(args.warm)
+    eng.synchronize()
+    if args.trace:
+        eng.batch_trace()  # reset
+    torch.cuda.cudart().cudaProfilerStart()
+    eng.batch_enqueue_steps(1)
+    eng.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    _, pos, err = eng.batch_state(B)
+    print(f"{args.preset}: batch {B}, positions {pos[0]}, error {err}, kernels/step {eng.batch_kernels_per_step()}")
+    if args.trace:
+        tr = eng.batch_trace().astype(np.int64)[:eng.batch_kernels_per_step()]
+        names = ["embed"] + ["qkv", "attention", "o_proj", "gate_up", "down"] * shape.layers + ["lm_head", "argmax"]
+        t0, prev = tr[0, 0], tr[0, 0]
+        print(f"step span {(tr[:, 2].max() - t0) / 1e3:.1f} us")
+        acc: dict[str, np.ndarray] = {}
+        for name, row in zip(names, tr):
+            start, wmax, end, wmin, smax, first, last, epi = row
+            a = acc.setdefault(name, np.zeros(6))
+            a[0] += 1
+            a[1] += (end - prev) / 1e3
+            a[2] += (wmin - prev) / 1e3
+            if first:
+                a[3] += (first - wmin) / 1e3
+                a[4] += (last - wmin) / 1e3
+                a[5] += (epi - last) / 1e3
+            if name == "attention" and first:
+                # attention marks: heads finished, probabilities ready, output accumulated
+                att = acc.setdefault("attention phases", np.zeros(6))
+                att[0] += 1
+                att[1] += (first - wmin) / 1e3
+                att[2] += (last - first) / 1e3
+                att[3] += (epi - last) / 1e3
+                att[4] += (end - epi) / 1e3
+            prev = end
+        for name, a in acc.items():
+            c = a[0]
+            if name == "attention phases":
+                print(f"attention phases (last CTA, after the wait): heads {a[1] / c:6.2f} us, scores + softmax "
+                      f"{a[2] / c:6.2f}, p.v {a[3] / c:6.2f}, output {a[4] / c:6.2f}")
+                continue
+            print(f"{name:9s} x{int(c):3d} critical {a[1] / c:7.2f} us | wait returns {a[2] / c:5.2f} after the "
+                  f"previous end | first stage {a[3] / c:6.2f}, final accumulator {a[4] / c:6.2f} after the wait | "
+                  f"epilogue tail {a[5] / c:5.2f}")
+    eng.close()
 
 
 if __name__ == "__main__":
