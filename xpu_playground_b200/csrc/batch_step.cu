@@ -245,10 +245,13 @@ __device__ __forceinline__ void run_epilogue(const BGemm &p, uint32_t t, uint32_
 __device__ __forceinline__ bool failed_now(const int *f) { return *reinterpret_cast<const volatile int *>(f) != 0; }
 
 // End of the stage that starts at K block kb: up to kBoxes blocks, not past
-// the tile or the CTA's range.
-__device__ __forceinline__ uint32_t stage_end(uint32_t kb, uint32_t kb1, uint32_t nk) {
+// the tile or the CTA's range. A CTA's first stage (kb == kb0) is one block:
+// it is the one the pipeline waits for after the previous kernel, and a
+// 16 KB weight box lands well before a 64 KB stage would when every SM
+// starts at once.
+__device__ __forceinline__ uint32_t stage_end(uint32_t kb, uint32_t kb0, uint32_t kb1, uint32_t nk) {
   const uint32_t tile_end = (kb / nk + 1) * nk;
-  return min(min(kb + kBoxes, kb1), tile_end);
+  return min(min(kb + (kb == kb0 ? 1u : kBoxes), kb1), tile_end);
 }
 
 // Round two floats to bf16 (RNE) and pack them: lo in the low half.
@@ -340,7 +343,7 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
       // has finished, the activations of those stages and the rest.
       uint32_t pre_end[kRing];
       for (; issued < kRing && kb < kb1; ++issued) {
-        const uint32_t e = stage_end(kb, kb1, nk);
+        const uint32_t e = stage_end(kb, kb0, kb1, nk);
         uint8_t *st = ring + issued * kStageBytes;
         mbar_expect_tx(&full[issued], (e - kb) * (kWBytes + kXBytes));
         for (uint32_t j = 0; j < e - kb; ++j)
@@ -357,7 +360,7 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
       for (uint32_t i = issued; kb < kb1; ++i) {
         const uint32_t s = i % kRing, use = i / kRing;
         if (failed_now(&failed) || !mbar_wait(&empty[s], (use - 1) & 1)) { failed = 1; break; }
-        const uint32_t e = stage_end(kb, kb1, nk);
+        const uint32_t e = stage_end(kb, kb0, kb1, nk);
         uint8_t *st = ring + s * kStageBytes;
         mbar_expect_tx(&full[s], (e - kb) * (kWBytes + kXBytes));
         for (uint32_t j = 0; j < e - kb; ++j)
@@ -375,7 +378,7 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
     if (lane == 0) {
       uint32_t seg = 0, i = 0;
       for (uint32_t kb = kb0; kb < kb1; ++i) {
-        const uint32_t e = stage_end(kb, kb1, nk);
+        const uint32_t e = stage_end(kb, kb0, kb1, nk);
         const bool first = kb == kb0 || kb % nk == 0, last = e == kb1 || e % nk == 0;
         const uint32_t buf = seg & 1;
         if (first && seg >= 2) {
@@ -433,7 +436,7 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
       bool dead = false;
       uint32_t i = 0;
       for (uint32_t kb = kb0; kb < kb1; ++i) {
-        const uint32_t e = stage_end(kb, kb1, nk), s = i % kRing;
+        const uint32_t e = stage_end(kb, kb0, kb1, nk), s = i % kRing;
         if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&full[s], (i / kRing) & 1));
         if (dead) { failed = 1; break; }
         norm_stage(ring + s * kStageBytes + kStageW, kb, e, nk, p.norm_w, s_rs, u);
