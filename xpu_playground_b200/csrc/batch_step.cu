@@ -996,33 +996,40 @@ k_battn(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant__ C
   if (threadIdx.x == 0) trace_mark(bd, bb, 2);
 }
 
-// ------------------------------------------- tensor-core attention (one CTA) ----
-// The same (kv head h, sequence s) attention as k_battn with both products
-// on tcgen05 (M = 128, N = 16 head slots, G of them used):
-//   pass 1  S = K . Q^T per 128-position stage: A = the K stage (positions x
-//           128 dims, two 64-dim TMA boxes, K-major, 128-byte swizzle),
-//           B = the group's finished q (16 rows x 128 dims, same layout),
-//           D = 128 positions x 16 slots in TMEM (double buffered); the
-//           compute warps read one position per thread and store
-//           s = bf16(bf16(S) * scale) into P (bf16, rows = head slots,
-//           K-major, 128-byte swizzle, 64 positions per 2 KB atom);
-//   softmax M = max s, S = sum exp(s - M) per head (fixed order), then P
-//           = bf16(exp(s - M) * (1 / S)) in place, 0 past the context;
-//   pass 2  O^T = V^T . P^T accumulated over the V stages: A = the V stage
-//           read MN-major (dims contiguous: the cache rows as TMA lands
-//           them), B = P; D = 128 dims x 16 slots in TMEM, read one dim per
-//           thread into the bf16 output.
-// The newest position's k and v are finished by this CTA and written to
-// the caches (with a proxy fence) before the producer fetches the stages
-// that hold them; V rows past the context in the last stage are zeroed in
-// shared memory (a stale row must not meet a zero probability as 0 * NaN).
+// ------------------------------------ tensor-core attention (2-CTA cluster) ----
+// The (kv head h, sequence s) attention of k_battn with both products on
+// tcgen05 (M = 128, N = 16 head slots, G of them used), split over a
+// cluster of two CTAs that take the first and second half of the
+// context's 128-position stages:
+//   pass 1  S = K . Q^T per stage: A = the K stage (positions x 128 dims, two
+//           64-dim TMA boxes, K-major, 128-byte swizzle), B = the group's
+//           finished q (16 rows x 128 dims, same layout), D = 128 positions
+//           x 16 slots in TMEM (4 buffers); the compute warps read one
+//           position per thread and store s = bf16(bf16(S) * scale) into P
+//           (bf16, rows = head slots, K-major, 128-byte swizzle, 64
+//           positions per 2 KB atom);
+//   softmax the two CTAs exchange their maxima and then their sums of
+//           exp(s - M) through distributed shared memory (stores into the
+//           peer plus a remote mbarrier arrival): M = max, S = sum in CTA
+//           order, identical in both; then P = bf16(exp(s - M) * (1 / S)) in
+//           place, 0 past the context;
+//   pass 2  O^T = V^T . P^T over the CTA's V stages: A = the V stage read
+//           MN-major (dims contiguous: cache rows as TMA lands them), B = P;
+//           D = 128 dims x 16 slots in TMEM; the second CTA stores its O^T
+//           into the first's shared memory, which adds the halves in order
+//           and writes the bf16 output.
+// The CTA holding the newest position finishes that position's k and v and
+// writes them to the caches (with a proxy fence) before its producer
+// fetches the stages that hold them; its last V stage's rows past the
+// context are zeroed in shared memory (a stale row must not meet a zero
+// probability as 0 * NaN). Both CTAs finish the group's q.
 // Warp 0: TMA producer (lane 0) and the L2 prefetch of the next GEMM's
 // weights (lanes 1-31); warp 1: TMEM owner and MMA issuer; warps 2-5:
-// compute (head epilogues, score conversion, softmax, output).
+// compute. Two clusters share an SM (their rings are sized for that).
 constexpr uint32_t kTcPos = 128;                   // positions per stage
 constexpr uint32_t kTcBox = 128 * 64 * 2;          // one 64-dim box of a stage: 16 KB
 constexpr uint32_t kTcStage = 2 * kTcBox;          // 32 KB
-constexpr uint32_t kTcMaxStages = 6;             // ring slots: as many as fit next to P (>= 2)
+constexpr uint32_t kTcMaxStages = 6;               // ring slots: as many as fit (>= 2)
 constexpr uint32_t kTcThreads = 192;
 constexpr uint32_t kTcN = 16;                      // MMA N: head slots
 constexpr uint32_t kPAtom = 16 * 128;              // 16 rows x 64 bf16: 2 KB
@@ -1031,9 +1038,10 @@ constexpr uint32_t kTcTmemCols = 128;              // S[4] (4 x 16) + O (16)
 constexpr uint32_t kIdescS = (1u << 4) | (1u << 7) | (1u << 10) | ((kTcN >> 3) << 17) | ((128u >> 4) << 24);
 constexpr uint32_t kIdescO = kIdescS | (1u << 15);  // A MN-major
 
+// Dynamic shared memory of one CTA: ring + q + P for half the stages of max_seq.
 __host__ __device__ inline size_t tc_attn_smem_bytes(uint32_t max_seq, uint32_t stages) {
-  const size_t atoms = (static_cast<size_t>(max_seq) + kTcPos - 1) / kTcPos * 2;  // P atoms of whole stages
-  return 1024 + static_cast<size_t>(stages) * kTcStage + 2 * kPAtom + atoms * kPAtom;
+  const size_t half = ((static_cast<size_t>(max_seq) + kTcPos - 1) / kTcPos + 1) / 2;
+  return 1024 + static_cast<size_t>(stages) * kTcStage + 2 * kPAtom + half * 2 * kPAtom;
 }
 
 // Byte offset of element (row r, column c < 64) inside a 128-byte swizzled
@@ -1044,27 +1052,31 @@ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) {
 
 __device__ __forceinline__ void tc_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-// HEADS: the CTA finishes its group's heads (decode); otherwise q, k and v
-// are finished and cached by k_bheads first (prefill).
+// HEADS: the cluster finishes its group's heads (decode); otherwise q, k and
+// v are finished and cached by k_bheads first (prefill).
 template <int G, bool HEADS>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, 2)
 k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant__ CUtensorMap map_k,
            const __grid_constant__ CUtensorMap map_v, const uint8_t *prefetch, uint64_t prefetch_bytes,
            uint32_t stages) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ uint64_t full[kTcMaxStages], empty[kTcMaxStages], s_full[kTcSBufs], s_empty[kTcSBufs], hd_ready, p_ready,
-      last_landed,
-      v_patched, o_full, mma_done;
+      last_landed, v_patched, o_full, mma_done, x_max, x_sum, x_out;
   __shared__ uint32_t tmem_base, issued_n, consumed_n;
   __shared__ float red[4][G], sM[G], sInv[G];
+  __shared__ float xm[2][G], xl[2][G];  // the two CTAs' maxima / sums (written by both)
+  __shared__ float xo[G][kHD];           // second CTA's O^T (in the first CTA)
   __shared__ int failed;
   const uint32_t a0 = smem_addr(smem_raw);
   uint8_t *ring = smem_raw + ((a0 + 1023u) / 1024u * 1024u - a0);
   uint8_t *qs = ring + stages * kTcStage;  // 2 atoms: dims 0-63, 64-127
-  uint8_t *ps = qs + 2 * kPAtom;              // P atoms, 64 positions each
-  const uint32_t h = blockIdx.x, s = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t *ps = qs + 2 * kPAtom;           // P atoms, 64 positions each
+  const uint32_t rank = cluster_rank(), peer = rank ^ 1u;
+  const uint32_t h = blockIdx.x >> 1, s = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t n = bb.seq[s].position + 1, pos_new = n - 1;
-  const uint32_t nst = (n + kTcPos - 1) / kTcPos;
+  const uint32_t nst = (n + kTcPos - 1) / kTcPos, nh = (nst + 1) / 2;
+  const uint32_t st0 = rank ? nh : 0, my = (rank ? nst : nh) - st0;  // this CTA's stages [st0, st0 + my)
+  const bool owner = my > 0 && st0 + my == nst;                      // holds the newest position
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < stages; ++i) {
       mbar_init(&full[i], 1);
@@ -1080,6 +1092,9 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
     mbar_init(&v_patched, 4);
     mbar_init(&o_full, 1);
     mbar_init(&mma_done, 1);
+    mbar_init(&x_max, G);    // the peer's G maximum writers
+    mbar_init(&x_sum, G);    // the peer's G sum writers
+    mbar_init(&x_out, 128);  // the second CTA's 128 output threads
     fence_mbar_init();
     failed = 0;
     issued_n = 0;
@@ -1087,7 +1102,7 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
   }
   if (warp == 1) tmem_alloc1(&tmem_base, kTcTmemCols);
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before either signals the other
   tc_fence_after();
   const uint32_t tmem = tmem_base;
   grid_dep_launch();
@@ -1107,43 +1122,29 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
                      : "memory");
       }
     }
-  } else if (warp == 0 && !HEADS) {
-    // Prefill: every row this CTA reads was cached by earlier kernels.
-    const uint64_t kv_pol = evict_first_policy();
-    grid_dep_wait();
-    uint32_t i = 0;
-    for (; i < 2 * nst; ++i) {
-      const uint32_t slot = i % stages, use = i / stages;
-      if (use > 0 && (failed_now(&failed) || !mbar_wait(&empty[slot], (use - 1) & 1))) { failed = 1; break; }
-      const bool is_v = i >= nst;
-      const int32_t y = y0 + static_cast<int32_t>((is_v ? i - nst : i) * kTcPos);
-      const CUtensorMap *m = is_v ? &map_v : &map_k;
-      mbar_expect_tx(&full[slot], kTcStage);
-      tma_load_2d(ring + slot * kTcStage, m, xh, y, &full[slot], kv_pol);
-      tma_load_2d(ring + slot * kTcStage + kTcBox, m, xh + 64, y, &full[slot], kv_pol);
-    }
-    issued_n = i;
   } else if (warp == 0) {
-    // Producer: stages 0 .. nst-1 are K, nst .. 2 nst - 1 are V. Stages
-    // without the newest row may go before the wait; the two that hold it
-    // wait until this CTA has written that row (hd_ready).
+    // Producer: local stages 0 .. my-1 are K, my .. 2 my - 1 are V (global
+    // stage st0 + local). Stages without the newest row may go before the
+    // wait (decode); the owner's last K and V stages wait until the newest
+    // row is cached (hd_ready). Prefill: every row was cached before.
     const uint64_t kv_pol = evict_first_policy();
     auto issue = [&](uint32_t i, uint32_t slot) {
-      const bool is_v = i >= nst;
-      const int32_t y = y0 + static_cast<int32_t>((is_v ? i - nst : i) * kTcPos);
+      const bool is_v = i >= my;
+      const int32_t y = y0 + static_cast<int32_t>((st0 + (is_v ? i - my : i)) * kTcPos);
       const CUtensorMap *m = is_v ? &map_v : &map_k;
       mbar_expect_tx(&full[slot], kTcStage);
       tma_load_2d(ring + slot * kTcStage, m, xh, y, &full[slot], kv_pol);
       tma_load_2d(ring + slot * kTcStage + kTcBox, m, xh + 64, y, &full[slot], kv_pol);
     };
     uint32_t i = 0;
-    for (; i < stages && i + 1 < nst; ++i) issue(i, i);  // K stages below the last one
+    if (HEADS)
+      for (; i < stages && i < my && st0 + i + 1 < nst; ++i) issue(i, i);  // K stages below the newest row
     grid_dep_wait();
-    bool have_row = false;
-    for (; i < 2 * nst; ++i) {
+    bool have_row = !HEADS || !owner;
+    for (; i < 2 * my; ++i) {
       const uint32_t slot = i % stages, use = i / stages;
       if (use > 0 && (failed_now(&failed) || !mbar_wait(&empty[slot], (use - 1) & 1))) { failed = 1; break; }
-      if (!have_row && (i == nst - 1 || i == 2 * nst - 1)) {
+      if (!have_row && (i == my - 1 || i == 2 * my - 1)) {
         if (!mbar_wait(&hd_ready, 0)) { failed = 1; break; }
         have_row = true;
       }
@@ -1153,10 +1154,10 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
   } else if (warp == 1) {
     if (lane == 0) {
       uint32_t i = 0;
-      bool ok = mbar_wait(&hd_ready, 0);  // q in shared memory
+      bool ok = my == 0 || mbar_wait(&hd_ready, 0);  // q in shared memory
       tc_fence_after();
       // pass 1: scores
-      for (; ok && i < nst; ++i) {
+      for (; ok && i < my; ++i) {
         const uint32_t slot = i % stages, b = i % kTcSBufs;
         if (i >= kTcSBufs && !mbar_wait(&s_empty[b], ((i / kTcSBufs) - 1) & 1)) { ok = false; break; }
         if (!mbar_wait(&full[slot], (i / stages) & 1)) { ok = false; break; }
@@ -1170,12 +1171,12 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
         mma1_commit(&s_full[b]);
       }
       // pass 2: p . v
-      if (ok) ok = mbar_wait(&p_ready, 0);
+      if (ok && my) ok = mbar_wait(&p_ready, 0);
       tc_fence_after();
-      for (uint32_t j = 0; ok && j < nst; ++j, ++i) {
+      for (uint32_t j = 0; ok && j < my; ++j, ++i) {
         const uint32_t slot = i % stages;
         if (!mbar_wait(&full[slot], (i / stages) & 1)) { ok = false; break; }
-        if (j + 1 == nst) {
+        if (owner && j + 1 == my) {
           // The last V stage has landed: the compute warps zero its rows
           // past the context before it is read (they learn of the landing
           // from this thread, which observes the ring's phases in order).
@@ -1190,7 +1191,7 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
                    smem_desc(sp + (kk / 4) * kPAtom + 32 * (kk % 4), 16, 1024), kIdescO, (j | kk) ? 1u : 0u);
         mma1_commit(&empty[slot]);
       }
-      if (ok) mma1_commit(&o_full);
+      if (ok && my) mma1_commit(&o_full);
       if (!ok) failed = 1;
       consumed_n = i;
       mma1_commit(&mma_done);
@@ -1207,15 +1208,16 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
       const uint32_t atom = k / ((kTcN - G) * 8), rem = k % ((kTcN - G) * 8);
       *reinterpret_cast<uint4 *>(qs + atom * kPAtom + (G + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
     }
-    // Head epilogues at the newest position: q into shared memory, k and v
-    // into the caches (prefill: q from k_bheads).
+    // Head epilogues at the newest position: q into shared memory (both
+    // CTAs), k and v into the caches (the owner; prefill: all from k_bheads).
     if (!HEADS)
       for (uint32_t k = et; k < G * kHD; k += 128) {
         const uint32_t g = k / kHD, d = k % kHD;
         *reinterpret_cast<uint16_t *>(qs + (d / 64) * kPAtom + swz(g, d % 64)) =
             reinterpret_cast<const uint16_t *>(bb.q)[(static_cast<size_t>(s) * bd.QH + h * G + g) * kHD + d];
       }
-    for (uint32_t k = cw; HEADS && k < static_cast<uint32_t>(G) + 2; k += 4) {
+    const uint32_t nheads = owner ? G + 2 : G;
+    for (uint32_t k = cw; HEADS && k < nheads; k += 4) {
       const uint32_t col = k < G ? h * G + k : (k == G ? bd.QH + h : bd.QH + bd.KVH + h);
       float out[4];
       head_finish(bd, bb, w, s, col, pos_new, out);
@@ -1238,15 +1240,15 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
     __syncwarp();
     if (lane == 0) mbar_arrive(&hd_ready);
     if (et == 0) trace_mark(bd, bb, 5);  // heads finished
-    for (uint32_t k = et; k < 2 * nst * (kTcN - G) * 8; k += 128) {
+    for (uint32_t k = et; k < 2 * my * (kTcN - G) * 8; k += 128) {
       const uint32_t atom = k / ((kTcN - G) * 8), rem = k % ((kTcN - G) * 8);
       *reinterpret_cast<uint4 *>(ps + atom * kPAtom + (G + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
     }
-    // pass 1: scores of position p = 128 i + 32 quarter + lane
+    // pass 1: scores of position p = 128 (st0 + i) + 32 quarter + lane
     float m[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) m[g] = -INFINITY;
-    for (uint32_t i = 0; i < nst; ++i) {
+    for (uint32_t i = 0; i < my; ++i) {
       const uint32_t b = i % kTcSBufs;
       if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&s_full[b], (i / kTcSBufs) & 1));
       float acc[16];
@@ -1259,36 +1261,42 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[b]);
-      const uint32_t p = i * kTcPos + quarter * 32 + lane;
+      const uint32_t pl = i * kTcPos + quarter * 32 + lane, p = st0 * kTcPos + pl;
       if (p < n) {
-        uint8_t *atom = ps + (p / 64) * kPAtom;
+        uint8_t *atom = ps + (pl / 64) * kPAtom;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
           const float sv = round_bf16(__fmul_rn(round_bf16(acc[g]), kAttnScale));
-          *reinterpret_cast<uint16_t *>(atom + swz(g, p % 64)) = float_to_bf16_bits(sv);
+          *reinterpret_cast<uint16_t *>(atom + swz(g, pl % 64)) = float_to_bf16_bits(sv);
           m[g] = fmaxf(m[g], sv);
         }
       }
     }
-    // softmax statistics per head (quarters in order); a running sum during
-    // pass 1 (online rescaling) measured slower: its exp sits on the
-    // per-stage path, this one after it.
+    // softmax statistics: this CTA's per head (quarters in order), then both
+    // CTAs' through distributed shared memory (same values in both CTAs).
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const float wm = warp_max(m[g]);
       if (lane == 0) red[quarter][g] = wm;
     }
     tc_sync();
-    if (et < static_cast<uint32_t>(G)) sM[et] = fmaxf(fmaxf(red[0][et], red[1][et]), fmaxf(red[2][et], red[3][et]));
+    if (et < static_cast<uint32_t>(G)) {
+      const float cm = fmaxf(fmaxf(red[0][et], red[1][et]), fmaxf(red[2][et], red[3][et]));
+      xm[rank][et] = cm;
+      st_cluster_f32(cluster_addr(&xm[rank][et], peer), cm);
+      remote_arrive(cluster_addr(&x_max, peer));
+    }
+    if (!dead) dead = !__all_sync(kFullMask, mbar_wait_cluster(&x_max, 0));
+    if (et < static_cast<uint32_t>(G)) sM[et] = fmaxf(xm[0][et], xm[1][et]);
     tc_sync();
     float l[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) l[g] = 0.f;
-    for (uint32_t p = et; p < n; p += 128) {
-      const uint8_t *atom = ps + (p / 64) * kPAtom;
+    for (uint32_t pl = et; pl < my * kTcPos && st0 * kTcPos + pl < n; pl += 128) {
+      const uint8_t *atom = ps + (pl / 64) * kPAtom;
 #pragma unroll
       for (int g = 0; g < G; ++g)
-        l[g] += expf(bf16_bits_to_float(*reinterpret_cast<const uint16_t *>(atom + swz(g, p % 64))) - sM[g]);
+        l[g] += expf(bf16_bits_to_float(*reinterpret_cast<const uint16_t *>(atom + swz(g, pl % 64))) - sM[g]);
     }
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -1296,23 +1304,31 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
       if (lane == 0) red[quarter][g] = ws;
     }
     tc_sync();
-    if (et < static_cast<uint32_t>(G)) sInv[et] = 1.0f / (((red[0][et] + red[1][et]) + red[2][et]) + red[3][et]);
+    if (et < static_cast<uint32_t>(G)) {
+      const float cl = ((red[0][et] + red[1][et]) + red[2][et]) + red[3][et];
+      xl[rank][et] = cl;
+      st_cluster_f32(cluster_addr(&xl[rank][et], peer), cl);
+      remote_arrive(cluster_addr(&x_sum, peer));
+    }
+    if (!dead) dead = !__all_sync(kFullMask, mbar_wait_cluster(&x_sum, 0));
+    if (et < static_cast<uint32_t>(G)) sInv[et] = 1.0f / (xl[0][et] + xl[1][et]);
     tc_sync();
-    for (uint32_t p = et; p < nst * kTcPos; p += 128) {
-      uint8_t *atom = ps + (p / 64) * kPAtom;
+    for (uint32_t pl = et; pl < my * kTcPos; pl += 128) {
+      uint8_t *atom = ps + (pl / 64) * kPAtom;
+      const bool valid = st0 * kTcPos + pl < n;
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        uint16_t *e = reinterpret_cast<uint16_t *>(atom + swz(g, p % 64));
-        *e = p < n ? float_to_bf16_bits(__fmul_rn(expf(bf16_bits_to_float(*e) - sM[g]), sInv[g])) : 0;
+        uint16_t *e = reinterpret_cast<uint16_t *>(atom + swz(g, pl % 64));
+        *e = valid ? float_to_bf16_bits(__fmul_rn(expf(bf16_bits_to_float(*e) - sM[g]), sInv[g])) : 0;
       }
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
     if (lane == 0) mbar_arrive(&p_ready);
     if (et == 0) trace_mark(bd, bb, 6);  // probabilities ready
-    // Zero the last V stage's rows past the context once it has landed.
-    {
-      const uint32_t slot = (2 * nst - 1) % stages;
+    // The owner zeroes its last V stage's rows past the context once landed.
+    if (owner) {
+      const uint32_t slot = (2 * my - 1) % stages;
       if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&last_landed, 0));
       const uint32_t valid = n - (nst - 1) * kTcPos;
       if (!dead)
@@ -1327,18 +1343,26 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
       if (lane == 0) mbar_arrive(&v_patched);
     }
     // output: dim d = 32 quarter + lane of the group's heads
-    if (!dead) dead = !__all_sync(kFullMask, mbar_wait(&o_full, 0));
+    if (!dead && my) dead = !__all_sync(kFullMask, mbar_wait(&o_full, 0));
     if (et == 0) trace_mark(bd, bb, 7);  // output accumulated
     float o[16];
 #pragma unroll
     for (int g = 0; g < 16; ++g) o[g] = 0.f;
-    if (!dead) {
+    if (!dead && my) {
       tc_fence_after();
       tmem_ld16(tmem + ((quarter * 32u) << 16) + kTcSBufs * kTcN, o);
     }
     const uint32_t d = quarter * 32 + lane;
+    if (rank == 1) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) putv(bb.attn, (static_cast<size_t>(s) * bd.QH + h * G + g) * kHD + d, o[g]);
+      for (int g = 0; g < G; ++g) st_cluster_f32(cluster_addr(&xo[g][d], 0), o[g]);
+      remote_arrive(cluster_addr(&x_out, 0));
+    } else {
+      if (!dead) dead = !__all_sync(kFullMask, mbar_wait_cluster(&x_out, 0));
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+        putv(bb.attn, (static_cast<size_t>(s) * bd.QH + h * G + g) * kHD + d, o[g] + xo[g][d]);
+    }
     if (dead) failed = 1;
   }
   tc_fence_before();
@@ -1352,6 +1376,7 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
     }
     trace_mark(bd, bb, 2);
   }
+  cluster_sync();  // neither CTA leaves while the other may still address its shared memory
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc1(tmem, kTcTmemCols);
@@ -1465,15 +1490,44 @@ int smem_optin() {
 // max_seq positions fit in shared memory next to the K/V ring and the cache
 // spans at least one stage; otherwise the batch-1 chunked kernels
 // (scores, then p.v with a last-CTA combine) per (chunk, head, sequence).
+// Launch with a 2-CTA cluster and programmatic dependent launch.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_pair(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                            Args... args) {
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// Attention path: the tensor-core cluster kernel when half the stages' P
+// and a ring of >= 2 stages fit in half an SM's shared memory (two clusters
+// per SM) and the cache spans a stage; else the CUDA-core fused kernel
+// (decode) or the batch-1 chunked kernels (scores, then p.v with a last-CTA
+// combine) per (chunk, head, sequence).
 template <int G>
 cudaError_t launch_battention(const BatchDims &d, const BatchBuffers &b, const LayerWeights &w, cudaStream_t s,
                               bool prefill) {
   const uint64_t rows = prefill ? d.max_seq : static_cast<uint64_t>(d.batch) * d.max_seq;
   const uint64_t o_bytes = static_cast<uint64_t>(d.H) * d.QH * kHD * 2;
+  const size_t half_sm = static_cast<size_t>(smem_optin()) / 2;
   uint32_t stages = kTcMaxStages;
-  while (stages > 2 && tc_attn_smem_bytes(d.max_seq, stages) + 4096 > static_cast<size_t>(smem_optin())) --stages;
+  while (stages > 2 && tc_attn_smem_bytes(d.max_seq, stages) + 2048 > half_sm) --stages;
   const size_t tc_smem = tc_attn_smem_bytes(d.max_seq, stages);
-  if (tc_smem + 4096 <= static_cast<size_t>(smem_optin()) && rows >= kTcPos) {
+  if (tc_smem + 2048 <= half_sm && rows >= kTcPos) {
     CUtensorMap mk, mv;
     cudaError_t e = make_tmap_2d_u16_swizzled(&mk, w.kcache, static_cast<uint64_t>(d.KVH) * kHD, rows,
                                               static_cast<uint64_t>(d.KVH) * kHD, 64, kTcPos);
@@ -1484,11 +1538,11 @@ cudaError_t launch_battention(const BatchDims &d, const BatchBuffers &b, const L
     if (prefill) {
       e = launch_pdl(k_bheads, dim3(d.KVH, d.batch), dim3(256), 0, s, d, b, w);
       if (e != cudaSuccess) return e;
-      return launch_pdl(k_battn_tc<G, false>, dim3(d.KVH, d.batch), dim3(kTcThreads), tc_smem, s, d, b, w, mk, mv,
-                        reinterpret_cast<const uint8_t *>(w.wo), o_bytes, stages);
+      return launch_pdl_pair(k_battn_tc<G, false>, dim3(2 * d.KVH, d.batch), dim3(kTcThreads), tc_smem, s, d, b, w,
+                             mk, mv, reinterpret_cast<const uint8_t *>(w.wo), o_bytes, stages);
     }
-    return launch_pdl(k_battn_tc<G, true>, dim3(d.KVH, d.batch), dim3(kTcThreads), tc_smem, s, d, b, w, mk, mv,
-                      reinterpret_cast<const uint8_t *>(w.wo), o_bytes, stages);
+    return launch_pdl_pair(k_battn_tc<G, true>, dim3(2 * d.KVH, d.batch), dim3(kTcThreads), tc_smem, s, d, b, w, mk,
+                           mv, reinterpret_cast<const uint8_t *>(w.wo), o_bytes, stages);
   }
   const size_t smem = attn_smem_bytes(G, d.max_seq);
   if (!prefill && smem + 4096 <= static_cast<size_t>(smem_optin()) && rows >= kAttnPos) {

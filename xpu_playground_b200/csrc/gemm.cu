@@ -65,27 +65,6 @@ constexpr int kEpilogueWarps = 8;
 constexpr int kGemmThreads = 64 + 32 * kEpilogueWarps;
 constexpr unsigned kErrGemmTimeout = 1u;
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// Address of the same shared-memory object in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t cluster_addr(const void *p, uint32_t rank) {
-  uint32_t out;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr(p)), "r"(rank));
-  return out;
-}
-
-__device__ __forceinline__ void remote_arrive(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
-}
-
 // Instruction descriptor, kind::f16: FP32 accumulator, A K-major, B MN-major.
 __host__ __device__ constexpr uint32_t instr_desc(bool fp16, uint32_t m, uint32_t n) {
   return (1u << 4) |                          // D format F32
