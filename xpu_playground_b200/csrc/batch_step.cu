@@ -668,19 +668,40 @@ __global__ void __launch_bounds__(kStreamThreads) k_bpv(BatchDims bd, BatchBuffe
 // owns dimensions l + 32 j, so both rotate-half partners sit in one lane):
 // q/k: RMSNorm with the head norm weight, then RoPE; v: unchanged. Returns
 // the lane's four finished values (dims l, l + 32, l + 64, l + 96).
-__device__ inline void head_finish(const BatchDims &bd, const BatchBuffers &bb, const LayerWeights &w, uint32_t s,
-                                   uint32_t col, uint32_t pos, float (&out)[4]) {
-  const uint32_t lane = threadIdx.x & 31, rows = (bd.QH + 2 * bd.KVH) * kHD;
-  const bf16 *raw = bb.qkv + static_cast<size_t>(s) * rows + static_cast<size_t>(col) * kHD;
+// The step-invariant inputs of one head epilogue (norm weight, RoPE row):
+// they can be loaded before waiting for the QKV GEMM.
+struct HeadConst {
+  float nw[4], c[4], s[4];
+};
+
+__device__ inline HeadConst head_const(const BatchDims &bd, const BatchBuffers &bb, const LayerWeights &w, uint32_t col,
+                                       uint32_t pos) {
+  const uint32_t lane = threadIdx.x & 31;
   const bool is_v = col >= bd.QH + bd.KVH, is_q = col < bd.QH;
-  float v[4], nwv[4], cv[4], sv[4];
+  HeadConst k;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    v[j] = bfv(raw, lane + 32 * j);
-    nwv[j] = is_v ? 0.f : bfv(is_q ? w.q_norm : w.k_norm, lane + 32 * j);
-    cv[j] = is_v ? 0.f : bfv(bb.cos_t, static_cast<size_t>(pos) * kHD + lane + 32 * j);
-    sv[j] = is_v ? 0.f : bfv(bb.sin_t, static_cast<size_t>(pos) * kHD + lane + 32 * j);
+    k.nw[j] = is_v ? 0.f : bfv(is_q ? w.q_norm : w.k_norm, lane + 32 * j);
+    k.c[j] = is_v ? 0.f : bfv(bb.cos_t, static_cast<size_t>(pos) * kHD + lane + 32 * j);
+    k.s[j] = is_v ? 0.f : bfv(bb.sin_t, static_cast<size_t>(pos) * kHD + lane + 32 * j);
   }
+  return k;
+}
+
+// The lane's four raw values of head `col` of sequence s (QKV GEMM output).
+__device__ inline void head_raw(const BatchDims &bd, const BatchBuffers &bb, uint32_t s, uint32_t col, float (&v)[4]) {
+  const uint32_t lane = threadIdx.x & 31, rows = (bd.QH + 2 * bd.KVH) * kHD;
+  const bf16 *raw = bb.qkv + static_cast<size_t>(s) * rows + static_cast<size_t>(col) * kHD;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] = bfv(raw, lane + 32 * j);
+}
+
+__device__ inline void head_math(const BatchDims &bd, uint32_t col, const float (&v)[4], const HeadConst &k,
+                                 float (&out)[4]) {
+  const bool is_v = col >= bd.QH + bd.KVH;
+  const float(&nwv)[4] = k.nw;
+  const float(&cv)[4] = k.c;
+  const float(&sv)[4] = k.s;
   if (is_v) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) out[j] = v[j];
@@ -700,6 +721,14 @@ __device__ inline void head_finish(const BatchDims &bd, const BatchBuffers &bb, 
     out[j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(a, cv[j])), round_bf16(__fmul_rn(-c, sv[j]))));
     out[j + 2] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(c, cv[j + 2])), round_bf16(__fmul_rn(a, sv[j + 2]))));
   }
+}
+
+__device__ inline void head_finish(const BatchDims &bd, const BatchBuffers &bb, const LayerWeights &w, uint32_t s,
+                                   uint32_t col, uint32_t pos, float (&out)[4]) {
+  const HeadConst k = head_const(bd, bb, w, col, pos);
+  float v[4];
+  head_raw(bd, bb, s, col, v);
+  head_math(bd, col, v, k, out);
 }
 
 // Chunked-attention path: the head epilogues of (kv head blockIdx.x,
@@ -1199,8 +1228,6 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
     }
   } else {
     // Compute warps 2-5: thread et; TMEM lane quarter (warp % 4).
-    grid_dep_wait();
-    if (threadIdx.x == 64) trace_mark(bd, bb, 1);
     const uint32_t et = threadIdx.x - 64, quarter = warp & 3, cw = warp - 2;
     bool dead = false;
     // Padding rows G..15 of q are zero (those of P after the heads).
@@ -1208,6 +1235,21 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
       const uint32_t atom = k / ((kTcN - G) * 8), rem = k % ((kTcN - G) * 8);
       *reinterpret_cast<uint4 *>(qs + atom * kPAtom + (G + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
     }
+    // This warp's heads (cw and cw + 4 of q 0..G-1, then k, v for the owner):
+    // their norm weights and RoPE rows do not depend on the previous kernel.
+    const uint32_t nheads = owner ? G + 2 : G;
+    uint32_t hcol[2] = {0, 0};
+    HeadConst hk[2];
+#pragma unroll
+    for (uint32_t t2 = 0; t2 < 2; ++t2) {
+      const uint32_t k = cw + 4 * t2;
+      if (HEADS && k < nheads) {
+        hcol[t2] = k < G ? h * G + k : (k == G ? bd.QH + h : bd.QH + bd.KVH + h);
+        hk[t2] = head_const(bd, bb, w, hcol[t2], pos_new);
+      }
+    }
+    grid_dep_wait();
+    if (threadIdx.x == 64) trace_mark(bd, bb, 1);
     // Head epilogues at the newest position: q into shared memory (both
     // CTAs), k and v into the caches (the owner; prefill: all from k_bheads).
     if (!HEADS)
@@ -1216,11 +1258,16 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
         *reinterpret_cast<uint16_t *>(qs + (d / 64) * kPAtom + swz(g, d % 64)) =
             reinterpret_cast<const uint16_t *>(bb.q)[(static_cast<size_t>(s) * bd.QH + h * G + g) * kHD + d];
       }
-    const uint32_t nheads = owner ? G + 2 : G;
-    for (uint32_t k = cw; HEADS && k < nheads; k += 4) {
-      const uint32_t col = k < G ? h * G + k : (k == G ? bd.QH + h : bd.QH + bd.KVH + h);
+    float hraw[2][4];
+#pragma unroll
+    for (uint32_t t2 = 0; t2 < 2; ++t2)
+      if (HEADS && cw + 4 * t2 < nheads) head_raw(bd, bb, s, hcol[t2], hraw[t2]);  // both heads' loads in flight
+#pragma unroll
+    for (uint32_t t2 = 0; t2 < 2; ++t2) {
+      const uint32_t k = cw + 4 * t2;
+      if (!HEADS || k >= nheads) continue;
       float out[4];
-      head_finish(bd, bb, w, s, col, pos_new, out);
+      head_math(bd, hcol[t2], hraw[t2], hk[t2], out);
       if (k < G) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
