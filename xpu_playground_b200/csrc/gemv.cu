@@ -24,21 +24,24 @@ gemv_vec_kernel(const T *__restrict__ A, const T *__restrict__ x, T *__restrict_
                 uint32_t m, uint32_t k) {
   extern __shared__ uint4 xs[];  // k / 8 chunks of x
   const uint32_t chunks = k >> 3;
-  const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
-  for (uint32_t i = threadIdx.x; i < chunks; i += kGemvThreads) xs[i] = ld_ro16(x4 + i);
-  __syncthreads();
-
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t row0 = (blockIdx.x * kGemvWarps + warp) * ROWS;
-  if (row0 >= m) return;
+  // The rows' first batch is requested before x is staged, so the two
+  // round trips overlap (a 4096 x 4096 launch is only a few microseconds).
   const uint4 *rows[ROWS];
 #pragma unroll
   for (int r = 0; r < ROWS; ++r) {
     const uint32_t row = min(row0 + r, m - 1);  // clamp: duplicate rows are dropped below
     rows[r] = reinterpret_cast<const uint4 *>(A + static_cast<size_t>(row) * k);
   }
+  uint4 first[ROWS][UNROLL];
+  warp_rows_load<ROWS, UNROLL>(rows, 0, row0 < m ? chunks : 0, lane, first);
+  const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
+  for (uint32_t i = threadIdx.x; i < chunks; i += kGemvThreads) xs[i] = ld_ro16(x4 + i);
+  __syncthreads();
+  if (row0 >= m) return;
   float acc[ROWS];
-  warp_dot_rows<T, ROWS, UNROLL>(rows, xs, chunks, lane, acc);
+  warp_dot_rows<T, ROWS, UNROLL>(rows, xs, chunks, lane, first, acc);
   if (lane == 0) {
 #pragma unroll
     for (int r = 0; r < ROWS; ++r)
