@@ -9,6 +9,11 @@
 //     chunk, then a butterfly shuffle sum folds the 32 lanes (fixed order).
 // Rows whose K is not a multiple of 8, or whose base is not 16-byte aligned,
 // take the scalar kernel below (same FP32 math, one element per lane step).
+// The vector kernel is launched with programmatic dependent launch: it lets
+// the next launch start right away and waits for the previous one before
+// its first global access, so back-to-back GEMVs overlap the next launch's
+// CTA start-up with this one's tail (a 4096 x 4096 launch streams for only
+// ~5 us) while every read still sees the previous kernel's writes.
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "xpu_internal.h"
@@ -23,6 +28,8 @@ __global__ void __launch_bounds__(kGemvThreads)
 gemv_vec_kernel(const T *__restrict__ A, const T *__restrict__ x, T *__restrict__ y,
                 uint32_t m, uint32_t k) {
   extern __shared__ uint4 xs[];  // k / 8 chunks of x
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint32_t chunks = k >> 3;
   const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t row0 = (blockIdx.x * kGemvWarps + warp) * ROWS;
@@ -75,9 +82,18 @@ static cudaError_t launch_vec(const T *A, const T *x, T *y, uint32_t m, uint32_t
     if (e != cudaSuccess) return e;
   }
   const uint32_t rows_per_cta = kGemvWarps * ROWS;
-  const uint32_t grid = (m + rows_per_cta - 1) / rows_per_cta;
-  kernel<<<grid, kGemvThreads, smem, stream>>>(A, x, y, m, k);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((m + rows_per_cta - 1) / rows_per_cta);
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, A, x, y, m, k);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <typename T>
