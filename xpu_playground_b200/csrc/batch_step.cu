@@ -98,10 +98,8 @@ struct BGemm {
 };
 
 struct EpiShared {
-  uint16_t vals[kSeqN][kTileM];  // bf16 bits
-  float red[4][kSeqN];
-  float ssq[2][4][kSeqN];        // residual epilogue, alternating per tile
-  ArgBest best[4][kSeqN];
+  float ssq[2][4][kSeqN];  // residual epilogue, alternating per tile
+  ArgBest best[4][kSeqN];  // lm_head epilogue
   uint32_t bad[4][kSeqN];
 };
 
