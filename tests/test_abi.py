@@ -49,6 +49,38 @@ def test_invalid_arguments_fail_on_host(call):
     assert _lib.last_error()
 
 
+@pytest.mark.parametrize("call", [
+    lambda L: L.xpu_qwen3_create_batched(None, 16, 0, 4, None),
+    lambda L: L.xpu_qwen3_batch_decode(None, 1, 1, 1, 1),
+    lambda L: L.xpu_qwen3_batch_generate(None, 1, 1, 1, 4, 0, 1, 1),
+    lambda L: L.xpu_qwen3_batch_set_state(None, 1, 1, 1),
+    lambda L: L.xpu_qwen3_batch_get_state(None, 1, None, None, None),
+    lambda L: L.xpu_qwen3_batch_enqueue_steps(None, 1, None),
+    lambda L: L.xpu_qwen3_batch_logits(None, 0, 1, 4),
+    lambda L: L.xpu_qwen3_batch_trace(None, None, 0, None),
+    lambda L: L.xpu_qwen3_prefill(None, 1, 4, 1),
+])
+def test_batched_entries_reject_null_engine(call):
+    """The batched-decode and prefill entries check their handle and
+    pointers on the host (no device is touched)."""
+    L = _lib.load()
+    assert call(L) == _lib.XPU_ERR_INVALID
+    assert _lib.last_error()
+
+
+def test_batched_byte_model_without_engine():
+    L = _lib.load()
+    assert L.xpu_qwen3_batch_bytes_per_step(None, 16, 2048) == 0
+    assert L.xpu_qwen3_batch_kernels_per_step(None) == 0
+
+
+def test_python_engine_refuses_batched_tensor_parallel():
+    from xpu_playground_b200.qwen3 import Qwen3Engine
+    from xpu_playground_b200.qwen3_config import PRESETS
+    with pytest.raises(ValueError, match="one GPU"):
+        Qwen3Engine(PRESETS["tiny"], 16, tp_rank=0, tp_size=2, max_batch=4)
+
+
 def test_attention_group_sizes():
     L = _lib.load()
     # 12 query heads over 8 kv heads is not a whole group -> invalid
