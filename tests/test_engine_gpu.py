@@ -223,3 +223,21 @@ def test_persistent_step_equals_graph_step(preset):
     assert a.decode(7, 140) == b.decode(7, 140)
     assert np.array_equal(a.logits(), b.logits())
     a.close(); b.close()
+
+
+@pytest.mark.parametrize("prompt_len", [18930, 37880])
+def test_persistent_step_equals_graph_step_at_long_contexts(prompt_len):
+    """Contexts whose 128-position chunks outnumber the SMs: the persistent
+    step gives each CTA runs of 2 (above 148 chunks) or 3 (above 296 chunks)
+    chunks of a kv head per attention item, the graph step one chunk per CTA.
+    Generation crosses those boundaries (148 -> 149 and 296 -> 297 chunks)
+    with identical tokens and identical final logits."""
+    shape = PRESETS["tiny"]
+    prompt = prompt_ids(prompt_len, shape.vocab, 11)
+    out = []
+    for mode in ("persistent", "graph"):
+        with Qwen3Engine(shape, 40960, mode=mode) as e:
+            e.init_synthetic(13)
+            out.append((e.generate(prompt, 24), e.logits()))
+    assert out[0][0] == out[1][0]
+    assert np.array_equal(out[0][1], out[1][1])

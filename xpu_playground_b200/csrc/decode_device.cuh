@@ -171,7 +171,7 @@ __device__ inline bool qkv_items(const DecodeDims &d, const DecodeBuffers &b, co
 constexpr uint32_t kMaxQkvSplits = 4;  // split partials held in registers by the head epilogue
 
 __device__ inline void qkv_head_warp(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w,
-                                     uint32_t head, uint32_t pos) {
+                                     uint32_t head, uint32_t pos, bf16 *q_dst = nullptr) {
   const uint32_t lane = lane_id();
   const uint32_t rows_total = (d.QH_l + 2 * d.KVH_l) * kHD;
   const bool is_v = head >= d.QH_l + d.KVH_l, is_q = head < d.QH_l;
@@ -229,7 +229,7 @@ __device__ inline void qkv_head_warp(const DecodeDims &d, const DecodeBuffers &b
     out[j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(a, cv[j])), round_bf16(__fmul_rn(-c, sv[j]))));
     out[j + 2] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(c, cv[j + 2])), round_bf16(__fmul_rn(a, sv[j + 2]))));
   }
-  bf16 *dst = is_q ? b.q + static_cast<size_t>(head) * kHD
+  bf16 *dst = is_q ? (q_dst ? q_dst : b.q + static_cast<size_t>(head) * kHD)
                    : w.kcache + (static_cast<size_t>(pos) * d.KVH_l + (head - d.QH_l)) * kHD;
 #pragma unroll
   for (int j = 0; j < 4; ++j) put(dst, lane + 32 * j, out[j]);
@@ -240,13 +240,14 @@ __device__ inline void qkv_head_warp(const DecodeDims &d, const DecodeBuffers &b
 // by the item's CTA itself (so no separate finishing phase): the group's q
 // heads, and for the item holding the newest position also its k and v
 // heads (into the cache at pos). Every CTA of the group computes the same q
-// bits, so their duplicate stores to b.q are harmless.
+// bits, so their duplicate stores to b.q are harmless. With q_shared the q
+// heads go to shared memory ([G][128]) instead, for this CTA alone.
 __device__ inline void attn_group_heads(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w,
-                                        uint32_t kvh, bool newest, uint32_t pos) {
+                                        uint32_t kvh, bool newest, uint32_t pos, bf16 *q_shared = nullptr) {
   const uint32_t G = d.QH_l / d.KVH_l, n = G + (newest ? 2 : 0);
   for (uint32_t h = cwarp(); h < n; h += kConsumerWarps) {
     const uint32_t head = h < G ? kvh * G + h : (h == G ? d.QH_l + kvh : d.QH_l + d.KVH_l + kvh);
-    qkv_head_warp(d, b, w, head, pos);
+    qkv_head_warp(d, b, w, head, pos, q_shared && h < G ? q_shared + h * kHD : nullptr);
   }
   consumer_sync();
 }
@@ -519,64 +520,109 @@ struct AttnShared {
   int flag;
 };
 
-// s = bf16(bf16(q.k) * scale) for the chunk's positions; chunk max and sum of
-// exp(s - max) into stats.
-template <int G>
-// finish_heads (persistent step): the item also runs its group's head
-// epilogues (attn_group_heads) - after issuing the loads of every cached K
-// row except the newest, whose row the epilogue writes, so the two memory
-// round trips overlap.
-__device__ inline void scores_item(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w, uint32_t kvh,
-                                   uint32_t chunk, uint32_t nchunks, uint32_t n, AttnShared<G> &as,
-                                   bool finish_heads = false) {
-  const uint32_t lane = lane_id(), cw = cwarp();
-  const uint32_t p0 = chunk * kPosChunk, p1 = min(p0 + kPosChunk, n);
-  const uint32_t pw = p0 + cw * kPosPerWarp;
-  const uint32_t newest = n - 1;
-  uint2 kr[kPosPerWarp];
+// This warp's 16 cache rows of the chunk (one 8-byte slice per lane), zero
+// past the context; the row at position `skip` is left out (its head
+// epilogue has not written it yet) and loaded by reload_row afterwards.
+__device__ __forceinline__ void load_rows(const bf16 *cache, const DecodeDims &d, uint32_t kvh, uint32_t pw,
+                                          uint32_t p1, uint32_t skip, uint2 (&r)[kPosPerWarp]) {
+  const uint32_t lane = lane_id();
 #pragma unroll
   for (uint32_t i = 0; i < kPosPerWarp; ++i) {
     const uint32_t p = pw + i;
-    kr[i] = p < p1 && !(finish_heads && p == newest)
-                ? ldcg8(w.kcache + (static_cast<size_t>(p) * d.KVH_l + kvh) * kHD + lane * 4)
-                : make_uint2(0, 0);
+    r[i] = p < p1 && p != skip ? ldcg8(cache + (static_cast<size_t>(p) * d.KVH_l + kvh) * kHD + lane * 4)
+                               : make_uint2(0, 0);
   }
-  if (finish_heads) {
-    attn_group_heads(d, b, w, kvh, chunk == newest / kPosChunk, newest);
-    if (newest >= pw && newest < pw + kPosPerWarp)
+}
+
+__device__ __forceinline__ void reload_row(const bf16 *cache, const DecodeDims &d, uint32_t kvh, uint32_t pw,
+                                           uint32_t p, uint2 (&r)[kPosPerWarp]) {
+  if (p >= pw && p < pw + kPosPerWarp)
 #pragma unroll
-      for (uint32_t i = 0; i < kPosPerWarp; ++i)
-        if (pw + i == newest) kr[i] = ldcg8(w.kcache + (static_cast<size_t>(newest) * d.KVH_l + kvh) * kHD + lane * 4);
+    for (uint32_t i = 0; i < kPosPerWarp; ++i)
+      if (pw + i == p) r[i] = ldcg8(cache + (static_cast<size_t>(p) * d.KVH_l + kvh) * kHD + lane_id() * 4);
+}
+
+// Warp sums of N (16 or 32) per-lane values at once, by recursive halving:
+// at offset o (16, 8, 4, 2, 1) each lane keeps half of its values, adds the
+// partner lane's (lane ^ o) copies of them, and hands over the other half;
+// once one value is left the remaining offsets add like warp_sum. Every total
+// is thus warp_sum's addition tree over the same lane pairs (bit-identical)
+// at N - 1 shuffles instead of 5 N. Returns the total of value `lane` (N =
+// 32) or `lane >> 1` (N = 16).
+template <int N>
+__device__ __forceinline__ float warp_sum_transposed(float (&v)[N]) {
+  static_assert(N == 16 || N == 32, "16 or 32 values per lane");
+  const uint32_t lane = lane_id();
+#pragma unroll
+  for (int step = 0; step < 5; ++step) {
+    const int o = 16 >> step, n = N >> step;
+    if (n >= 2) {
+      const bool up = (lane & o) != 0;
+#pragma unroll
+      for (int k = 0; k < n / 2; ++k) {
+        const float send = up ? v[k] : v[k + n / 2];
+        const float keep = up ? v[k + n / 2] : v[k];
+        v[k] = keep + __shfl_xor_sync(kFullMask, send, o);
+      }
+    } else {
+      v[0] += __shfl_xor_sync(kFullMask, v[0], o);
+    }
   }
+  return v[0];
+}
+
+// s = bf16(bf16(q.k) * scale) for the chunk's positions into sc (and
+// b.scores when store_scores); chunk max and sum of exp(s - max) into stats.
+// q comes from q_shared ([G][128], this CTA's head epilogue) or b.q.
+template <int G>
+__device__ inline void chunk_scores(const DecodeDims &d, const DecodeBuffers &b, uint32_t kvh, uint32_t chunk,
+                                    uint32_t nchunks, uint32_t p0, uint32_t p1, const uint2 (&kr)[kPosPerWarp],
+                                    float (&sc)[G][kPosChunk], bool store_scores,
+                                    const bf16 *q_shared = nullptr) {
+  const uint32_t lane = lane_id(), cw = cwarp();
   float q[G][4];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    const uint2 raw = ldcg8(b.q + (static_cast<size_t>(kvh) * G + g) * kHD + lane * 4);
+    const uint2 raw = q_shared ? *reinterpret_cast<const uint2 *>(q_shared + g * kHD + lane * 4)
+                               : ldcg8(b.q + (static_cast<size_t>(kvh) * G + g) * kHD + lane * 4);
     q[g][0] = bf16_lo(raw.x); q[g][1] = bf16_hi(raw.x);
     q[g][2] = bf16_lo(raw.y); q[g][3] = bf16_hi(raw.y);
   }
+  // Positions in batches whose G x batch per-lane dot-product partials (16
+  // or 32 values) are summed over the warp together.
+  constexpr int kBatch = G >= 2 ? 32 / G : 16;
+  constexpr int kVals = kBatch * G;
 #pragma unroll
-  for (uint32_t i = 0; i < kPosPerWarp; ++i) {
-    const float k4[4] = {bf16_lo(kr[i].x), bf16_hi(kr[i].x), bf16_lo(kr[i].y), bf16_hi(kr[i].y)};
+  for (int bt = 0; bt < static_cast<int>(kPosPerWarp) / kBatch; ++bt) {
+    float v[kVals];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float s = 0.f;
+    for (int ii = 0; ii < kBatch; ++ii) {
+      const uint2 k = kr[bt * kBatch + ii];
+      const float k4[4] = {bf16_lo(k.x), bf16_hi(k.x), bf16_lo(k.y), bf16_hi(k.y)};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) s = fmaf(q[g][j], k4[j], s);
-      s = warp_sum(s);
-      if (lane == 0) as.sc[g][cw * kPosPerWarp + i] = round_bf16(__fmul_rn(round_bf16(s), kAttnScale));
+      for (int g = 0; g < G; ++g) {
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s = fmaf(q[g][j], k4[j], s);
+        v[ii * G + g] = s;
+      }
     }
+    const float tot = warp_sum_transposed<kVals>(v);
+    const uint32_t idx = kVals == 32 ? lane : lane >> 1;
+    if (kVals == 32 || (lane & 1) == 0)
+      sc[idx % G][cw * kPosPerWarp + bt * kBatch + idx / G] = round_bf16(__fmul_rn(round_bf16(tot), kAttnScale));
   }
   consumer_sync();
   for (uint32_t g = cw; g < static_cast<uint32_t>(G); g += kConsumerWarps) {
     float m = -INFINITY;
-    for (uint32_t i = lane; i < p1 - p0; i += 32) m = fmaxf(m, as.sc[g][i]);
+    for (uint32_t i = lane; i < p1 - p0; i += 32) m = fmaxf(m, sc[g][i]);
     m = warp_max(m);
     float l = 0.f;
-    for (uint32_t i = lane; i < p1 - p0; i += 32) l += expf(as.sc[g][i] - m);
+    for (uint32_t i = lane; i < p1 - p0; i += 32) l += expf(sc[g][i] - m);
     l = warp_sum(l);
     const uint32_t h = kvh * G + g;
-    for (uint32_t i = lane; i < p1 - p0; i += 32) b.scores[static_cast<size_t>(h) * d.max_seq + p0 + i] = as.sc[g][i];
+    if (store_scores)
+      for (uint32_t i = lane; i < p1 - p0; i += 32) b.scores[static_cast<size_t>(h) * d.max_seq + p0 + i] = sc[g][i];
     if (lane == 0) {
       b.stats[(static_cast<size_t>(h) * nchunks + chunk) * 2] = m;
       b.stats[(static_cast<size_t>(h) * nchunks + chunk) * 2 + 1] = l;
@@ -585,32 +631,13 @@ __device__ inline void scores_item(const DecodeDims &d, const DecodeBuffers &b, 
   consumer_sync();
 }
 
-// Probabilities bf16(exp(s - M) * (1 / S)) over all chunks' statistics, the
-// chunk's partial sum of p * v, and (last CTA of the kv head) the sum over
-// chunks into the attention output.
+// Softmax statistics over all `nch` chunks of every head of the group:
+// sM = global max M, sInv = 1 / S with S = sum of l_c exp(m_c - M) (each
+// lane its chunks lane, lane + 32, ..., then a warp sum).
 template <int G>
-__device__ inline void pv_item(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w, uint32_t kvh,
-                               uint32_t chunk, uint32_t nchunks, uint32_t n, AttnShared<G> &as,
-                               bool defer_combine = false) {
-  const uint32_t lane = lane_id(), cw = cwarp(), t = ctid();
-  const uint32_t nch = (n + kPosChunk - 1) / kPosChunk;
-  const uint32_t p0 = chunk * kPosChunk, p1 = min(p0 + kPosChunk, n);
-  const uint32_t pw = p0 + cw * kPosPerWarp;
-  uint2 vr[kPosPerWarp];
-#pragma unroll
-  for (uint32_t i = 0; i < kPosPerWarp; ++i) {
-    const uint32_t p = pw + i;
-    vr[i] = p < p1 ? ldcg8(w.vcache + (static_cast<size_t>(p) * d.KVH_l + kvh) * kHD + lane * 4) : make_uint2(0, 0);
-  }
-  // This thread's scores of the chunk, loaded now with the V rows (they do
-  // not depend on the softmax statistics).
-  constexpr uint32_t kScPerThread = (G * kPosChunk + kConsumerThreads - 1) / kConsumerThreads;
-  float sreg[kScPerThread];
-#pragma unroll
-  for (uint32_t k = 0; k < kScPerThread; ++k) {
-    const uint32_t i = t + k * kConsumerThreads, g = i / kPosChunk, p = p0 + i % kPosChunk;
-    sreg[k] = (i < G * kPosChunk && p < p1) ? __ldcg(b.scores + static_cast<size_t>(kvh * G + g) * d.max_seq + p) : 0.f;
-  }
+__device__ inline void group_stats(const DecodeBuffers &b, uint32_t kvh, uint32_t nchunks, uint32_t nch,
+                                   float (&sM)[G], float (&sInv)[G]) {
+  const uint32_t lane = lane_id(), cw = cwarp();
   for (uint32_t g = cw; g < static_cast<uint32_t>(G); g += kConsumerWarps) {
     const float *st = b.stats + static_cast<size_t>(kvh * G + g) * nchunks * 2;
     // this lane's first chunk statistics, read once (up to 32 chunks, 4096
@@ -623,18 +650,18 @@ __device__ inline void pv_item(const DecodeDims &d, const DecodeBuffers &b, cons
     float sum = lane < nch ? cl * expf(cm - m) : 0.f;
     for (uint32_t c = lane + 32; c < nch; c += 32) sum += __ldcg(st + 2 * c + 1) * expf(__ldcg(st + 2 * c) - m);
     sum = warp_sum(sum);
-    if (lane == 0) { as.sM[g] = m; as.sInv[g] = 1.0f / sum; }
+    if (lane == 0) { sM[g] = m; sInv[g] = 1.0f / sum; }
   }
   consumer_sync();
-#pragma unroll
-  for (uint32_t k = 0; k < kScPerThread; ++k) {
-    const uint32_t i = t + k * kConsumerThreads;
-    if (i < G * kPosChunk) {
-      const uint32_t g = i / kPosChunk, j = i % kPosChunk;
-      as.sc[g][j] = p0 + j < p1 ? round_bf16(__fmul_rn(expf(sreg[k] - as.sM[g]), as.sInv[g])) : 0.f;
-    }
-  }
-  consumer_sync();
+}
+
+// The chunk's partial sum of p * v (probabilities in sc) into
+// attn_part[head][chunk] (warps' partials added in warp order).
+template <int G>
+__device__ inline void chunk_pv(const DecodeBuffers &b, uint32_t kvh, uint32_t chunk, uint32_t nchunks,
+                                const uint2 (&vr)[kPosPerWarp], const float (&sc)[G][kPosChunk],
+                                float (&sacc)[kConsumerWarps][G][kHD]) {
+  const uint32_t lane = lane_id(), cw = cwarp(), t = ctid();
   float acc[G][4];
 #pragma unroll
   for (int g = 0; g < G; ++g)
@@ -645,7 +672,7 @@ __device__ inline void pv_item(const DecodeDims &d, const DecodeBuffers &b, cons
     const float v4[4] = {bf16_lo(vr[i].x), bf16_hi(vr[i].x), bf16_lo(vr[i].y), bf16_hi(vr[i].y)};
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const float prob = as.sc[g][cw * kPosPerWarp + i];
+      const float prob = sc[g][cw * kPosPerWarp + i];
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc[g][j] = fmaf(prob, v4[j], acc[g][j]);
     }
@@ -653,15 +680,71 @@ __device__ inline void pv_item(const DecodeDims &d, const DecodeBuffers &b, cons
 #pragma unroll
   for (int g = 0; g < G; ++g)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) as.sacc[cw][g][lane * 4 + j] = acc[g][j];
+    for (int j = 0; j < 4; ++j) sacc[cw][g][lane * 4 + j] = acc[g][j];
   consumer_sync();
   for (uint32_t e = t; e < G * kHD; e += kConsumerThreads) {
     const uint32_t g = e / kHD, dd = e % kHD;
     float tot = 0.f;
 #pragma unroll
-    for (uint32_t ww = 0; ww < static_cast<uint32_t>(kConsumerWarps); ++ww) tot += as.sacc[ww][g][dd];
+    for (uint32_t ww = 0; ww < static_cast<uint32_t>(kConsumerWarps); ++ww) tot += sacc[ww][g][dd];
     b.attn_part[(static_cast<size_t>(kvh * G + g) * nchunks + chunk) * kHD + dd] = tot;
   }
+}
+
+// Scores of one item (kv head, chunk).
+// finish_heads (persistent step): the item also runs its group's head
+// epilogues (attn_group_heads) - after issuing the loads of every cached K
+// row except the newest, whose row the epilogue writes, so the two memory
+// round trips overlap.
+template <int G>
+__device__ inline void scores_item(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w, uint32_t kvh,
+                                   uint32_t chunk, uint32_t nchunks, uint32_t n, AttnShared<G> &as,
+                                   bool finish_heads = false) {
+  const uint32_t p0 = chunk * kPosChunk, p1 = min(p0 + kPosChunk, n);
+  const uint32_t pw = p0 + cwarp() * kPosPerWarp;
+  const uint32_t newest = n - 1;
+  uint2 kr[kPosPerWarp];
+  load_rows(w.kcache, d, kvh, pw, p1, finish_heads ? newest : 0xffffffffu, kr);
+  if (finish_heads) {
+    attn_group_heads(d, b, w, kvh, chunk == newest / kPosChunk, newest);
+    reload_row(w.kcache, d, kvh, pw, newest, kr);
+  }
+  chunk_scores<G>(d, b, kvh, chunk, nchunks, p0, p1, kr, as.sc, true);
+}
+
+// Probabilities bf16(exp(s - M) * (1 / S)) over all chunks' statistics, the
+// chunk's partial sum of p * v, and (last CTA of the kv head) the sum over
+// chunks into the attention output.
+template <int G>
+__device__ inline void pv_item(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w, uint32_t kvh,
+                               uint32_t chunk, uint32_t nchunks, uint32_t n, AttnShared<G> &as,
+                               bool defer_combine = false) {
+  const uint32_t t = ctid();
+  const uint32_t nch = (n + kPosChunk - 1) / kPosChunk;
+  const uint32_t p0 = chunk * kPosChunk, p1 = min(p0 + kPosChunk, n);
+  const uint32_t pw = p0 + cwarp() * kPosPerWarp;
+  uint2 vr[kPosPerWarp];
+  load_rows(w.vcache, d, kvh, pw, p1, 0xffffffffu, vr);
+  // This thread's scores of the chunk, loaded now with the V rows (they do
+  // not depend on the softmax statistics).
+  constexpr uint32_t kScPerThread = (G * kPosChunk + kConsumerThreads - 1) / kConsumerThreads;
+  float sreg[kScPerThread];
+#pragma unroll
+  for (uint32_t k = 0; k < kScPerThread; ++k) {
+    const uint32_t i = t + k * kConsumerThreads, g = i / kPosChunk, p = p0 + i % kPosChunk;
+    sreg[k] = (i < G * kPosChunk && p < p1) ? __ldcg(b.scores + static_cast<size_t>(kvh * G + g) * d.max_seq + p) : 0.f;
+  }
+  group_stats<G>(b, kvh, nchunks, nch, as.sM, as.sInv);
+#pragma unroll
+  for (uint32_t k = 0; k < kScPerThread; ++k) {
+    const uint32_t i = t + k * kConsumerThreads;
+    if (i < G * kPosChunk) {
+      const uint32_t g = i / kPosChunk, j = i % kPosChunk;
+      as.sc[g][j] = p0 + j < p1 ? round_bf16(__fmul_rn(expf(sreg[k] - as.sM[g]), as.sInv[g])) : 0.f;
+    }
+  }
+  consumer_sync();
+  chunk_pv<G>(b, kvh, chunk, nchunks, vr, as.sc, as.sacc);
   if (defer_combine) {  // persistent step: the o_proj staging combines the chunks (stage_attn_parts)
     consumer_sync();
     return;
@@ -677,6 +760,72 @@ __device__ inline void pv_item(const DecodeDims &d, const DecodeBuffers &b, cons
     if (t == 0) b.cnt_attn[kvh] = 0;
   }
   consumer_sync();
+}
+
+// Attention staging of the persistent step: the scores of up to
+// kMaxItemChunks chunks of one item, the group's softmax statistics and the
+// warps' p.v partials.
+constexpr uint32_t kMaxItemChunks = 3;  // 40960 positions over >= 107 CTAs
+
+template <int G>
+struct StepAttnShared {
+  float sc[kMaxItemChunks][G][kPosChunk];
+  alignas(16) bf16 q[G][kHD];  // the group's q heads (head epilogue -> scores)
+  float sM[G], sInv[G];
+  float sacc[kConsumerWarps][G][kHD];
+};
+
+// Persistent step, one pass per item: chunks [c0, c1) of kv head kvh. The
+// head epilogues (q heads into shared memory) and scores of scores_item for
+// each chunk, then - once every
+// item of the kv head has published its chunk statistics - the probabilities
+// and partial p.v of pv_item (combine deferred to the o_proj staging). The
+// first chunk's V rows are in flight during the wait.
+// `wait()` arrives on the kv head's counter and waits (bounded) for the
+// layer's full count: false on a timeout or another waiter's failure. The
+// arithmetic per chunk is that of scores_item + pv_item, so the bits are the
+// same. No CTA may hold two items of one kv head (it would wait for itself).
+template <int G, typename Wait>
+__device__ inline bool attn_item(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w, uint32_t kvh,
+                                 uint32_t c0, uint32_t c1, uint32_t nchunks, uint32_t n, StepAttnShared<G> &as,
+                                 Wait wait) {
+  const uint32_t t = ctid(), cw = cwarp();
+  const uint32_t nch = (n + kPosChunk - 1) / kPosChunk;
+  const uint32_t newest = n - 1, newest_chunk = newest / kPosChunk;
+  uint2 vr[kPosPerWarp];
+  for (uint32_t c = c0; c < c1; ++c) {
+    const uint32_t p0 = c * kPosChunk, p1 = min(p0 + kPosChunk, n);
+    const uint32_t pw = p0 + cw * kPosPerWarp;
+    uint2 kr[kPosPerWarp];
+    load_rows(w.kcache, d, kvh, pw, p1, c == c0 ? newest : 0xffffffffu, kr);
+    if (c == c0) {
+      attn_group_heads(d, b, w, kvh, newest_chunk >= c0 && newest_chunk < c1, newest, &as.q[0][0]);
+      reload_row(w.kcache, d, kvh, pw, newest, kr);
+    }
+    chunk_scores<G>(d, b, kvh, c, nchunks, p0, p1, kr, as.sc[c - c0], false, &as.q[0][0]);
+  }
+  // the first chunk's V rows, in flight during the wait
+  load_rows(w.vcache, d, kvh, c0 * kPosChunk + cw * kPosPerWarp, min(c0 * kPosChunk + kPosChunk, n), 0xffffffffu, vr);
+  if (!wait()) return false;
+  group_stats<G>(b, kvh, nchunks, nch, as.sM, as.sInv);
+  constexpr uint32_t kScPerThread = (G * kPosChunk + kConsumerThreads - 1) / kConsumerThreads;
+  for (uint32_t c = c0; c < c1; ++c) {
+    const uint32_t p0 = c * kPosChunk, p1 = min(p0 + kPosChunk, n);
+    if (c != c0) load_rows(w.vcache, d, kvh, p0 + cw * kPosPerWarp, p1, 0xffffffffu, vr);
+    float (&sc)[G][kPosChunk] = as.sc[c - c0];
+#pragma unroll
+    for (uint32_t k = 0; k < kScPerThread; ++k) {
+      const uint32_t i = t + k * kConsumerThreads;
+      if (i < G * kPosChunk) {
+        const uint32_t g = i / kPosChunk, j = i % kPosChunk;
+        sc[g][j] = p0 + j < p1 ? round_bf16(__fmul_rn(expf(sc[g][j] - as.sM[g]), as.sInv[g])) : 0.f;
+      }
+    }
+    consumer_sync();
+    chunk_pv<G>(b, kvh, c, nchunks, vr, sc, as.sacc);
+    consumer_sync();
+  }
+  return true;
 }
 
 // Persistent step, o_proj input: for each K part that this CTA's o_proj

@@ -10,10 +10,13 @@
 // filling with the next matrix, so HBM never idles between phases and no
 // kernel launch, prologue or tail separates them.
 //
-// Phases per layer (grid barrier after each): qkv (+ per-head q/k norm,
-// RoPE, cache write by the last CTA of the head), attention scores,
-// attention p.v (+ chunk combine by the last CTA of the kv head), o_proj
-// (+ residual by the last CTA of each row tile), gate/up + SwiGLU, down
+// Phases per layer (grid barrier after each): qkv (split-K partials),
+// attention (per item = kv head x a run of 128-position chunks, one run per
+// CTA and kv head at most: the group's q/k norm + RoPE and the cache write,
+// scores, then - once every item of the kv head has published its softmax
+// statistics, counted on a per-kv-head arrival counter instead of a grid
+// barrier - probabilities and partial p.v), o_proj (+ chunk combine in its
+// staging, residual by the last CTA of each row tile), gate/up + SwiGLU, down
 // (+ residual); then lm_head + argmax. The per-item math is the same code as
 // the multi-kernel path (decode_device.cuh), so both give identical bits.
 //
@@ -52,6 +55,7 @@ struct StepParams {
   const CUtensorMap *maps;     // [4 * n_layers + 1] (device): qkv, o, gate/up, down per layer; lm_head
   StepGeoms g;
   unsigned long long *bar;     // grid-barrier arrival counter (device)
+  unsigned long long *acnt;    // [KVH_l] attention arrival counters (device, monotonic)
   uint32_t n_layers;
   uint32_t x_elems;            // capacity (bf16 elements) of the staging/attention region
   uint64_t *trace;             // optional: [gridDim.x][trace_events] globaltimer stamps
@@ -63,6 +67,7 @@ struct StepPlan {
   LayerWeights *d_layers = nullptr;
   CUtensorMap *d_maps = nullptr;
   unsigned long long *d_bar = nullptr;
+  unsigned long long *d_acnt = nullptr;
   uint32_t grid = 0;
   size_t smem = 0;
   int group = 0;
@@ -71,6 +76,8 @@ struct StepPlan {
 namespace {
 
 using namespace dec;
+
+constexpr uint32_t kMaxStepKvHeads = 16;  // kv heads per rank (attention arrival counters)
 
 // XPU_STEP_TRACE=1 records per-CTA phase timestamps (read with xpu_qwen3_trace).
 bool trace_enabled() {
@@ -164,7 +171,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constan
   if (blockIdx.x == 0)  // the residual stream starts as the embedding row
     for (uint32_t c = ctid(); c < d.H / 8; c += kConsumerThreads)
       reinterpret_cast<uint4 *>(b.x)[c] = reinterpret_cast<const uint4 *>(x_embed)[c];
-  AttnShared<G> &as = *reinterpret_cast<AttnShared<G> *>(sm.xs);
+  StepAttnShared<G> &as = *reinterpret_cast<StepAttnShared<G> *>(sm.xs);
   uint32_t ev = 0;
   auto stamp = [&]() {
     if (p.trace && ctid() == 0 && ev < p.trace_events) p.trace[static_cast<size_t>(blockIdx.x) * p.trace_events + ev] = global_ns();
@@ -172,7 +179,14 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constan
   };
   stamp();
   const uint32_t npc = pos_chunks_dev(d.max_seq), nch = (n + kPosChunk - 1) / kPosChunk;
-  const uint32_t attn_items = d.KVH_l * nch;
+  // Attention items: (kv head, run of cpi chunks), at most one item of a kv
+  // head per CTA (ipk <= gridDim.x).
+  const uint32_t cpi = (nch + gridDim.x - 1) / gridDim.x, ipk = (nch + cpi - 1) / cpi;
+  const uint32_t attn_items = d.KVH_l * ipk;
+  if (cpi > kMaxItemChunks || d.KVH_l > kMaxStepKvHeads) {  // the plan rules both out
+    if (blockIdx.x == 0 && ctid() == 0) flag_error(st, kErrPipelineTimeout);
+    return;
+  }
   const bool tp = d.tp_size > 1;
   const unsigned long long x_base = st->x_base;
   uint32_t it = 0, nbar = 0, nx = 0;
@@ -185,6 +199,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constan
     ++nx;
     return tp_barrier(p, bar_base + static_cast<unsigned long long>(nbar) * gridDim.x, x_base + nx, &bflag);
   };
+  // Attention arrival counters only grow: every item of kv head h arrives
+  // once per layer, so layer l of this step completes at base[h] + (l + 1) *
+  // ipk. The bases are read before this CTA's first grid barrier; no CTA
+  // arrives before passing it, so every CTA reads the same bases.
+  __shared__ unsigned long long s_abase[kMaxStepKvHeads];
+  if (ctid() < d.KVH_l) s_abase[ctid()] = *reinterpret_cast<volatile unsigned long long *>(p.acnt + ctid());
+  consumer_sync();
   for (uint32_t l = 0; l < p.n_layers; ++l) {
     const LayerWeights w = p.layers[l];
     // trace events per layer: [staged, items, finished, barrier] x 6 phases
@@ -198,15 +219,20 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constan
     if (!barrier()) return;
     stamp();
     stamp();
-    for (uint32_t item = blockIdx.x; item < attn_items; item += gridDim.x)
-      scores_item<G>(d, b, w, item / nch, item % nch, npc, n, as, true);
+    {
+      const unsigned long long full = static_cast<unsigned long long>(l + 1) * ipk;
+      for (uint32_t item = blockIdx.x; item < attn_items; item += gridDim.x) {
+        const uint32_t kvh = item / ipk, c0 = (item % ipk) * cpi, c1 = min(c0 + cpi, nch);
+        if (!attn_item<G>(d, b, w, kvh, c0, c1, npc, n, as, [&]() {
+              return grid_barrier(p.acnt + kvh, s_abase[kvh] + full, st, &bflag);
+            }))
+          return;
+      }
+    }
     stamp();
     stamp();
-    if (!barrier()) return;
+    stamp();  // (one attention phase: the trace keeps the stamps of two)
     stamp();
-    stamp();
-    for (uint32_t item = blockIdx.x; item < attn_items; item += gridDim.x)
-      pv_item<G>(d, b, w, item / nch, item % nch, npc, n, as, true);
     stamp();
     stamp();
     if (!barrier()) return;
@@ -308,10 +334,10 @@ cudaError_t step_plan_create(const DecodeDims &d, const DecodeBuffers &b, const 
   plan->group = static_cast<int>(d.QH_l / d.KVH_l);
   size_t attn_bytes = 0;
   switch (plan->group) {
-    case 1: attn_bytes = sizeof(AttnShared<1>); break;
-    case 2: attn_bytes = sizeof(AttnShared<2>); break;
-    case 4: attn_bytes = sizeof(AttnShared<4>); break;
-    case 8: attn_bytes = sizeof(AttnShared<8>); break;
+    case 1: attn_bytes = sizeof(StepAttnShared<1>); break;
+    case 2: attn_bytes = sizeof(StepAttnShared<2>); break;
+    case 4: attn_bytes = sizeof(StepAttnShared<4>); break;
+    case 8: attn_bytes = sizeof(StepAttnShared<8>); break;
     default: delete plan; return cudaErrorInvalidValue;
   }
   const uint32_t stage_elems = std::max(std::max(d.H, K_o), d.I_l);
@@ -334,8 +360,13 @@ cudaError_t step_plan_create(const DecodeDims &d, const DecodeBuffers &b, const 
   for (StreamGeom *x : {&g.qkv, &g.o, &g.gu, &g.down, &g.lm}) { x->slot = slot; x->stages = nslots; }
   plan->smem = stream_smem_bytes(g.qkv, p.x_elems);
 
-  // Items a CTA owns in one phase must fit the deferred-arrival table.
+  // Items a CTA owns in one phase must fit the deferred-arrival table; an
+  // attention item holds at most kMaxItemChunks chunks of the context.
   plan->grid = static_cast<uint32_t>(sms);
+  if (d.KVH_l > kMaxStepKvHeads || (pos_chunks(d.max_seq) + plan->grid - 1) / plan->grid > kMaxItemChunks) {
+    delete plan;
+    return cudaErrorInvalidConfiguration;
+  }
   for (const StreamGeom *x : {&g.qkv, &g.o, &g.down})
     if ((x->items() + plan->grid - 1) / plan->grid > kMaxLocalItems) { delete plan; return cudaErrorInvalidConfiguration; }
 
@@ -372,10 +403,13 @@ cudaError_t step_plan_create(const DecodeDims &d, const DecodeBuffers &b, const 
   }
   if (e == cudaSuccess) e = cudaMalloc(&plan->d_bar, sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMemset(plan->d_bar, 0, sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMalloc(&plan->d_acnt, d.KVH_l * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMemset(plan->d_acnt, 0, d.KVH_l * sizeof(unsigned long long));
   if (e != cudaSuccess) { step_plan_destroy(plan); return e; }
   p.layers = plan->d_layers;
   p.maps = plan->d_maps;
   p.bar = plan->d_bar;
+  p.acnt = plan->d_acnt;
   *out = plan;
   return cudaSuccess;
 }
@@ -386,6 +420,7 @@ void step_plan_destroy(StepPlan *plan) {
   if (plan->d_maps) cudaFree(plan->d_maps);
   if (plan->d_layers) cudaFree(plan->d_layers);
   if (plan->d_bar) cudaFree(plan->d_bar);
+  if (plan->d_acnt) cudaFree(plan->d_acnt);
   delete plan;
 }
 
