@@ -69,6 +69,7 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemv", action="store_true")
+    ap.add_argument("--no-small", action="store_true", help="skip the Qwen3-0.6B decode measurement in extra")
     ap.add_argument("--batch", type=int, default=16,
                     help="sequences of the batched-decode measurement in extra (0: skip)")
     return ap.parse_args()
@@ -289,6 +290,44 @@ def batch_extra(torch, device, shape, context: int, batch: int, steps: int, warm
     return out
 
 
+def small_extra(torch, device, warmup: int) -> dict:
+    """the Qwen3-0.6B shape (28 layers, hidden 1024,
+    16/8 heads, tied), a 128-token seeded prompt (chunked prefill), then 128
+    device-resident greedy decode steps timed with CUDA events; roofline =
+    every weight once + the live K/V per step. At 1.2 GB per token the step is
+    bound by its per-layer phase latencies rather than by HBM."""
+    from xpu_playground_b200.qwen3 import Qwen3Engine
+    from xpu_playground_b200.qwen3_config import PRESETS
+
+    shape, prompt_len, steps = PRESETS["qwen3-0.6b"], 128, 128
+    eng = Qwen3Engine(shape, prompt_len + warmup + steps + 8, device=device.index or 0)
+    eng.init_synthetic(2026)
+    eng.prefill(seeded_prompt(prompt_len, shape.vocab))
+    stream = torch.cuda.ExternalStream(eng.info().stream, device=device)
+    eng.enqueue_steps(warmup)
+    eng.synchronize()
+    _, pos0, _ = eng.state()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    eng.enqueue_steps(steps)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    _, pos1, err = eng.state()
+    if err:
+        raise SystemExit(f"0.6B decode error word {err}")
+    nbytes = eng.bytes_per_token((pos0 + pos1) // 2)
+    peak, kind = measured_peaks()
+    eng.close()
+    return {"workload": "qwen3-0.6b-shaped greedy decode, batch 1, 128-token prompt then 128 decode steps",
+            "value": round(1000.0 / ms, 1), "unit": "tok/s", "ms_per_step": round(ms, 4),
+            "context_tokens": [pos0, pos1],
+            "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": nbytes,
+                         "achieved": round(nbytes / (ms * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4),
+                         "peak_source": f"{kind} HBM copy bandwidth"}}
+
+
 def measured_tflops() -> float:
     try:
         return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
@@ -379,6 +418,9 @@ def run_ours(args) -> None:
     extra = {}
     if prefill_info:
         extra["prefill"] = prefill_info
+    if not args.no_small and world == 1:
+        eng.synchronize()
+        extra["qwen3_0p6b_decode"] = small_extra(torch, device, warmup=max(W, 3))
     if args.batch and world == 1:
         eng.synchronize()
         extra["batch_decode"] = batch_extra(torch, device, shape, args.context, args.batch,

@@ -691,24 +691,15 @@ __device__ inline void chunk_pv(const DecodeBuffers &b, uint32_t kvh, uint32_t c
   }
 }
 
-// Scores of one item (kv head, chunk).
-// finish_heads (persistent step): the item also runs its group's head
-// epilogues (attn_group_heads) - after issuing the loads of every cached K
-// row except the newest, whose row the epilogue writes, so the two memory
-// round trips overlap.
+// Scores of one item (kv head, chunk) of the multi-kernel paths, whose head
+// epilogues ran before (the persistent step runs them inside attn_item).
 template <int G>
 __device__ inline void scores_item(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w, uint32_t kvh,
-                                   uint32_t chunk, uint32_t nchunks, uint32_t n, AttnShared<G> &as,
-                                   bool finish_heads = false) {
+                                   uint32_t chunk, uint32_t nchunks, uint32_t n, AttnShared<G> &as) {
   const uint32_t p0 = chunk * kPosChunk, p1 = min(p0 + kPosChunk, n);
   const uint32_t pw = p0 + cwarp() * kPosPerWarp;
-  const uint32_t newest = n - 1;
   uint2 kr[kPosPerWarp];
-  load_rows(w.kcache, d, kvh, pw, p1, finish_heads ? newest : 0xffffffffu, kr);
-  if (finish_heads) {
-    attn_group_heads(d, b, w, kvh, chunk == newest / kPosChunk, newest);
-    reload_row(w.kcache, d, kvh, pw, newest, kr);
-  }
+  load_rows(w.kcache, d, kvh, pw, p1, 0xffffffffu, kr);
   chunk_scores<G>(d, b, kvh, chunk, nchunks, p0, p1, kr, as.sc, true);
 }
 
@@ -717,8 +708,7 @@ __device__ inline void scores_item(const DecodeDims &d, const DecodeBuffers &b, 
 // chunks into the attention output.
 template <int G>
 __device__ inline void pv_item(const DecodeDims &d, const DecodeBuffers &b, const LayerWeights &w, uint32_t kvh,
-                               uint32_t chunk, uint32_t nchunks, uint32_t n, AttnShared<G> &as,
-                               bool defer_combine = false) {
+                               uint32_t chunk, uint32_t nchunks, uint32_t n, AttnShared<G> &as) {
   const uint32_t t = ctid();
   const uint32_t nch = (n + kPosChunk - 1) / kPosChunk;
   const uint32_t p0 = chunk * kPosChunk, p1 = min(p0 + kPosChunk, n);
@@ -745,10 +735,6 @@ __device__ inline void pv_item(const DecodeDims &d, const DecodeBuffers &b, cons
   }
   consumer_sync();
   chunk_pv<G>(b, kvh, chunk, nchunks, vr, as.sc, as.sacc);
-  if (defer_combine) {  // persistent step: the o_proj staging combines the chunks (stage_attn_parts)
-    consumer_sync();
-    return;
-  }
   if (arrive_one(b.cnt_attn + kvh, nch, &as.flag)) {
     for (uint32_t e = t; e < G * kHD; e += kConsumerThreads) {
       const uint32_t g = e / kHD, dd = e % kHD;
