@@ -51,7 +51,7 @@ METRIC = "Qwen3 decode tok/s @1/2/4/8 B200; GEMV GB/s & GEMM TFLOP/s vs roofline
 FALLBACK_HBM_GBS = 6650.0  # profiling recipe's fallback, used only without MEASURED_PEAKS.json
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of k_step divided by
 # its algorithmic bytes, from the ncu capture summarised in
-# profiles/k_step_qwen3-8b_decode.md (2.0334 GB read + 4.5 MB written for 2.0333 GB
+# profiles/k_step_qwen3-8b_decode.md (2.0334 GB read + 3.6 MB written for 2.0333 GB
 # of algorithmic bytes on the 8B-shaped 2-layer step; traffic grows with the
 # weights streamed, so the ratio carries over to 36 layers).
 TRAFFIC_RATIO = 1.002
