@@ -430,6 +430,14 @@ def run_ours(args) -> None:
         extra.update(gemv_extra(torch, device, rank, world))
         if rank == 0:
             extra.update(gemm_extra(torch, device, measured_tflops()))
+        if rank == 0 and not args.no_cpu_baseline:
+            # the reference's host loops on this box's cores, beside the GPU numbers
+            from oracle.cpu_baseline import gemm_cpu_baseline, gemv_cpu_baseline
+            for key, (m, k) in (("gemv_4096_bf16", (4096, 4096)), ("gemv_16384_bf16", (16384, 16384))):
+                if key in extra:
+                    extra[key]["cpu_baseline"] = gemv_cpu_baseline(m, k)
+            if "gemm_4096_bf16" in extra:
+                extra["gemm_4096_bf16"]["cpu_baseline"] = gemm_cpu_baseline(4096, 4096, 4096)
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         from oracle.cpu_baseline import hf_decode_baseline

@@ -100,3 +100,46 @@ def hf_decode_baseline(shape: Qwen3Shape, context: int, steps: int = 6,
                    f"at {shape.layers} layers; {time.perf_counter() - t_start:.0f} s of host time"),
         "per_token_s": per_token,
     }
+
+
+def _timed(fn, min_seconds: float) -> float:
+    """Seconds per call of fn after one warm-up call, averaged over repeats
+    that together take at least min_seconds."""
+    fn()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        reps += 1
+        if time.perf_counter() - t0 >= min_seconds:
+            return (time.perf_counter() - t0) / reps
+
+
+def gemv_cpu_baseline(m: int, k: int, fp16: bool = False, min_seconds: float = 1.0) -> dict:
+    """The reference's host GEMV check loop (gemv.cpp:126-130: FP32
+    accumulation over decoded 16-bit inputs, row by row), restated as
+    orc_gemv and run on every host thread, timed on the benchmark's own shape
+    with seeded uniform[-1, 1] inputs; matrix GB/s (2 m k bytes per call)."""
+    from oracle import oracle as orc
+    A = orc.uniform16(m * k, 5, 1, fp16).reshape(m, k)
+    x = orc.uniform16(k, 5, 2, fp16)
+    dt = _timed(lambda: orc.gemv(A, x, fp16), min_seconds)
+    return {"value": round(2.0 * m * k / dt / 1e9, 2), "unit": "GB/s", "cores": orc.num_threads(),
+            "kind": "port", "sample": f"{m}x{k} {'fp16' if fp16 else 'bf16'}, FP32 host loop, "
+                                      f"{dt * 1e3:.1f} ms per call"}
+
+
+def gemm_cpu_baseline(m: int, n: int, k: int, fp16: bool = False, sample_rows: int = 128,
+                      min_seconds: float = 1.0) -> dict:
+    """FP32 host GEMM (orc_gemm: rows of C across every host thread, each
+    accumulating over k in order) on a bounded sample of the benchmark shape:
+    `sample_rows` of the m rows of C against the full k x n operand; TFLOP/s
+    of the sample (2 rows n k FLOP per call), which a whole m x n x k product
+    would take m / sample_rows times as long to reach."""
+    from oracle import oracle as orc
+    rows = min(sample_rows, m)
+    A = orc.uniform16(rows * k, 6, 1, fp16).reshape(rows, k)
+    B = orc.uniform16(k * n, 6, 2, fp16).reshape(k, n)
+    dt = _timed(lambda: orc.gemm(A, B, fp16), min_seconds)
+    return {"value": round(2.0 * rows * n * k / dt / 1e12, 5), "unit": "TFLOP/s", "cores": orc.num_threads(),
+            "kind": "port", "sample": f"{rows} of {m} rows of C, n {n}, k {k}, {'fp16' if fp16 else 'bf16'} inputs, "
+                                      f"FP32 host loop, {dt:.2f} s per call"}
