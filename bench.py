@@ -335,6 +335,15 @@ def measured_tflops() -> float:
         return 1590.0  # profiling recipe's fallback burst figure
 
 
+def decode_config(args, shape) -> dict:
+    """The workload keys both arms report (the reference arm times the same
+    model shape, prompt length and decode steps on the host)."""
+    return {"workload": f"{args.preset}-shaped greedy decode, batch 1, {args.context}-token prompt then "
+                        f"{args.steps} timed decode steps",
+            "layers": shape.layers, "hidden": shape.hidden, "heads": f"{shape.q_heads}/{shape.kv_heads}",
+            "intermediate": shape.intermediate, "vocab": shape.vocab, "tied_lm_head": shape.tied}
+
+
 def run_ours(args) -> None:
     import torch
     import torch.distributed as dist
@@ -461,10 +470,7 @@ def run_ours(args) -> None:
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,0.02) bf16 weights, seeded uniform prompt ids)",
             "config": {
-                "workload": f"{args.preset}-shaped greedy decode, batch 1, {args.context}-token prompt then "
-                            f"{K} timed decode steps",
-                "layers": shape.layers, "hidden": shape.hidden, "heads": f"{shape.q_heads}/{shape.kv_heads}",
-                "intermediate": shape.intermediate, "vocab": shape.vocab, "tied_lm_head": shape.tied,
+                **decode_config(args, shape),
                 "context_tokens": [pos0, pos1],
                 "decode_mode": mode,
                 "parallelism": "single GPU" if world == 1 else f"tp{world} (tensor parallel, one sequence)",
@@ -513,12 +519,11 @@ def run_reference(args) -> None:
         "warmup": args.warmup,
         "ms_per_step": round(1000.0 / value, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (random N(0,0.02) bf16 weights, seeded prompt ids)",
-        "config": {"workload": f"{args.preset}-shaped greedy decode, batch 1, {args.context}-token prompt",
-                   "layers": shape.layers, "hidden": shape.hidden, "vocab": shape.vocab},
+        "config": {**decode_config(args, shape), "parallelism": "host CPU (rank 0 alone)"},
         "cpu_baseline": dict(cpu, value=round(value, 3)),
         "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": round(time.time() - t0, 1),
