@@ -53,7 +53,8 @@ BENCH_PROGRAMS: dict[str, str] = {
     "peak_mem_2d": "peak_mem_2d.cpp",
     "peak_compute_dpas": "peak_compute_dpas.cpp",
 }
-# Other C++ host programs: name -> sources under host/ (all link libxpu_cuda.so).
+# Other C++ host programs: name -> sources under host/ (all link libxpu_cuda.so;
+# peak_sycl also links libxpu_bench.so, whose run_* entries it calls).
 HOST_PROGRAMS: dict[str, list[str]] = {
     "peak_sycl": ["peak_sycl.cpp"],
     "qwen3": ["qwen3_cli.cpp"],
@@ -131,8 +132,10 @@ def build_programs() -> list[Path]:
         srcs = [HOST / f for f in files]
         out = BIN_DIR / name
         outputs.append(out)
-        if _stale(out, [*srcs, LIB, Path(__file__), *headers]):
-            _run([CXX, *CXX_FLAGS, f"-I{QWEN3_API}", *map(str, srcs), "-o", str(out), *link, rpath])
+        extra = ["-lxpu_bench"] if name == "peak_sycl" else []
+        if _stale(out, [*srcs, LIB, BENCH_LIB, Path(__file__), *headers]):
+            _run([CXX, *CXX_FLAGS, f"-I{QWEN3_API}", *map(str, srcs), "-o", str(out), f"-L{LIB_DIR}", *extra, *link,
+                  rpath])
     return outputs
 
 

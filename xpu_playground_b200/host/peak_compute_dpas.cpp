@@ -1,9 +1,9 @@
-// `peak_compute_dpas` (dense BF16 tensor-core calibrator) through
-// xpu_peak_compute, with the reference program's flags, timing loop,
-// closed-form checksum and output lines (peak_compute_dpas.cpp:24-222).
-// --work-items is the number of CTAs (default: one per SM); each issues
-// rounds x 8 tcgen05 MMAs of 128x256x16. The percentage is of the B200's
-// nominal dense BF16 peak (the reference prints its B70's).
+// `peak_compute_dpas` program: the dense BF16 tensor-core calibrator on
+// xpu_peak_compute. Flags, the timing loop's shape, the closed-form
+// checksum and the output lines are the reference program's interface
+// (peak_compute_dpas.cpp:24-222). --work-items counts CTAs (default: one
+// per SM), each issuing rounds x 8 tcgen05 MMAs of 128x256x16; the
+// percentage is of the B200's nominal dense BF16 peak.
 #include <cmath>
 #include <iomanip>
 #include <iostream>
@@ -15,90 +15,84 @@ namespace {
 
 using namespace xpu_cli;
 
-constexpr double kPeakTFlops = 2250.0;  // B200 dense BF16, nominal
-constexpr uint64_t kFlopsPerMma = 2ull * 128 * 256 * 16;
+constexpr double kNominalTFlops = 2250.0;  // B200 dense BF16
+constexpr uint64_t kMmaFlop = 2ull * 128 * 256 * 16;
 constexpr uint64_t kMmasPerRound = 8;
 
-struct Options {
+struct ComputeRun {
   size_t work_items = 0;  // 0: one CTA per SM
   unsigned rounds = 8192;
   unsigned iterations = 1000;
 };
 
-[[noreturn]] void usage(const char *program, int status) {
-  std::ostream &out = status == 0 ? std::cout : std::cerr;
-  out << "Usage: " << program << " [--work-items N] [--rounds N] [--iterations N]\n"
-      << "  --work-items N  CTAs, one tensor-core issuer each (default: one per SM)\n"
-      << "  --rounds N      eight-MMA batches per CTA (default: 8192)\n"
-      << "  --iterations N  timed kernel launches (default: 1000)\n";
-  std::exit(status);
+FlagTable compute_flags(ComputeRun &r, const char *program) {
+  FlagTable t([program](std::ostream &out) {
+    out << "Usage: " << program << " [--work-items N] [--rounds N] [--iterations N]\n"
+        << "  --work-items N  CTAs, one tensor-core issuer each (default: one per SM)\n"
+        << "  --rounds N      eight-MMA batches per CTA (default: 8192)\n"
+        << "  --iterations N  timed kernel launches (default: 1000)\n";
+  });
+  t.count("--work-items", false, &r.work_items).count("--rounds", false, &r.rounds).count("--iterations", false, &r.iterations);
+  return t;
 }
 
-Options parse(int argc, char **argv) {
-  Options o;
-  for (int i = 1; i < argc; ++i) {
-    const std::string_view arg(argv[i]);
-    if (arg == "--help" || arg == "-h") usage(argv[0], 0);
-    if (i + 1 == argc) throw std::invalid_argument(std::string(arg) + " requires a value");
-    if (arg == "--work-items") o.work_items = positive<size_t>(argv[++i], "--work-items");
-    else if (arg == "--rounds") o.rounds = positive<unsigned>(argv[++i], "--rounds");
-    else if (arg == "--iterations") o.iterations = positive<unsigned>(argv[++i], "--iterations");
-    else throw std::invalid_argument("unknown option: " + std::string(arg));
-  }
-  return o;
+int calibrate(ComputeRun r) {
+  const int sms = device_attribute(cudaDevAttrMultiProcessorCount);
+  if (!r.work_items) r.work_items = static_cast<size_t>(sms);
+  if (r.work_items > 0x7fffffffu) throw std::invalid_argument("--work-items is too large");
+  std::cout << "Device: " << device_name() << '\n'
+            << "Driver: " << driver_version() << '\n'
+            << "Compute units: " << sms << '\n';
+  const double flop = static_cast<double>(r.work_items) * r.rounds * kMmasPerRound * kMmaFlop;
+  std::cout << "MMA shape: 128x256x16 BF16, " << kMmaFlop << " FLOP/instruction\n"
+            << "Launch: " << r.work_items << " CTAs x " << r.rounds << " rounds x " << kMmasPerRound
+            << " MMA = " << std::fixed << std::setprecision(3) << flop / 1.0e12 << " TFLOP/launch\n";
+
+  DeviceArray<float> sums(r.work_items);
+  cuda_check(cudaMemset(sums.get(), 0, r.work_items * sizeof(float)), "clear sink");
+  LaunchTimer timer;
+  const auto once = [&] {
+    return timer.seconds([&] {
+      xpu_check(xpu_peak_compute(sums.get(), static_cast<uint32_t>(r.work_items), r.rounds, nullptr), "xpu_peak_compute");
+    });
+  };
+  for (int w = 0; w < 3; ++w) once();
+  std::vector<double> tflops;
+  for (unsigned it = 0; it < r.iterations; ++it) tflops.push_back(flop / once() / 1e12);
+  uint32_t device_flags = 0;
+  xpu_check(xpu_device_status(&device_flags), "xpu_device_status");
+  if (device_flags) throw std::runtime_error("tensor-core wait timed out on the device");
+
+  // Each element of the two accumulators starts at 0 and 1 and gains 4 per
+  // MMA (ones . quarter-ones over K = 16); the CTA checksum adds one element
+  // of each: 1 + 8 x 4 x rounds.
+  const float want = 1.0f + 4.0f * static_cast<float>(kMmasPerRound) * static_cast<float>(r.rounds);
+  const float slack = std::max(1.0f, 1.0e-5f * want);
+  float ends[2] = {0.0f, 0.0f};
+  cuda_check(cudaMemcpy(&ends[0], sums.get(), sizeof(float), cudaMemcpyDeviceToHost), "copy sink");
+  cuda_check(cudaMemcpy(&ends[1], sums.get() + r.work_items - 1, sizeof(float), cudaMemcpyDeviceToHost), "copy sink");
+  for (float got : ends)
+    if (std::abs(got - want) > slack) throw std::runtime_error("MMA checksum verification failed");
+
+  const RateSummary s = summarize(std::move(tflops));
+  const auto line = [](const char *label, double v) {
+    std::cout << std::fixed << std::setprecision(2) << label << v << " TFLOP/s (" << 100.0 * v / kNominalTFlops
+              << "% of " << std::setprecision(1) << kNominalTFlops << " TFLOP/s)\n";
+  };
+  line("Median BF16 compute: ", s.median);
+  line("Best BF16 compute:   ", s.best);
+  std::cout << "Checksum: PASS\n";
+  return 0;
 }
 
 }  // namespace
 
 extern "C" int run_peak_compute_dpas(int argc, char **argv) {
-  try {
-    Options o = parse(argc, argv);
-    const int sms = device_attribute(cudaDevAttrMultiProcessorCount);
-    if (o.work_items == 0) o.work_items = static_cast<size_t>(sms);
-    if (o.work_items > 0x7fffffffu) throw std::invalid_argument("--work-items is too large");
-    const std::string device = device_name(), driver = driver_version();
-    std::cout << "Device: " << device << '\n'
-              << "Driver: " << driver << '\n'
-              << "Compute units: " << sms << '\n';
-    DeviceArray<float> sink(o.work_items);
-    cuda_check(cudaMemset(sink.get(), 0, o.work_items * sizeof(float)), "clear sink");
-    const long double total_flops = static_cast<long double>(o.work_items) * o.rounds * kMmasPerRound * kFlopsPerMma;
-    std::cout << "MMA shape: 128x256x16 BF16, " << kFlopsPerMma << " FLOP/instruction\n"
-              << "Launch: " << o.work_items << " CTAs x " << o.rounds << " rounds x " << kMmasPerRound
-              << " MMA = " << std::fixed << std::setprecision(3) << static_cast<double>(total_flops / 1.0e12L)
-              << " TFLOP/launch\n";
-    auto launch = [&] {
-      xpu_check(xpu_peak_compute(sink.get(), static_cast<uint32_t>(o.work_items), o.rounds, nullptr),
-                "xpu_peak_compute");
-    };
-    LaunchTimer timer;
-    for (unsigned i = 0; i < 3; ++i) timer.seconds(launch);
-    std::vector<double> tflops;
-    for (unsigned i = 0; i < o.iterations; ++i)
-      tflops.push_back(static_cast<double>(total_flops) / timer.seconds(launch) / 1e12);
-    uint32_t flags = 0;
-    xpu_check(xpu_device_status(&flags), "xpu_device_status");
-    if (flags) throw std::runtime_error("tensor-core wait timed out on the device");
-    float first = 0.0f, last = 0.0f;
-    cuda_check(cudaMemcpy(&first, sink.get(), sizeof(float), cudaMemcpyDeviceToHost), "copy sink");
-    cuda_check(cudaMemcpy(&last, sink.get() + o.work_items - 1, sizeof(float), cudaMemcpyDeviceToHost), "copy sink");
-    // Accumulator initial offsets 0 + 1, plus 4 per MMA in each element.
-    const float expected = 1.0f + static_cast<float>(kMmasPerRound) * o.rounds * 4.0f;
-    const float tolerance = std::max(1.0f, expected * 1.0e-5f);
-    if (std::abs(first - expected) > tolerance || std::abs(last - expected) > tolerance)
-      throw std::runtime_error("MMA checksum verification failed");
-    std::sort(tflops.begin(), tflops.end());
-    const double median = median_sorted(tflops), best = tflops.back();
-    std::cout << std::fixed << std::setprecision(2) << "Median BF16 compute: " << median << " TFLOP/s ("
-              << (100.0 * median / kPeakTFlops) << "% of " << std::setprecision(1) << kPeakTFlops << " TFLOP/s)\n"
-              << std::setprecision(2) << "Best BF16 compute:   " << best << " TFLOP/s (" << (100.0 * best / kPeakTFlops)
-              << "% of " << std::setprecision(1) << kPeakTFlops << " TFLOP/s)\n"
-              << "Checksum: PASS\n";
-    return 0;
-  } catch (const std::exception &e) {
-    std::cerr << "Error: " << e.what() << '\n';
-  }
-  return 1;
+  return guarded_main([&] {
+    ComputeRun r;
+    if (!compute_flags(r, argv[0]).parse(argc, argv)) return 0;
+    return calibrate(r);
+  });
 }
 
 #ifdef XPU_STANDALONE_HOST

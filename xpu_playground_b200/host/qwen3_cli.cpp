@@ -1,6 +1,6 @@
 // `qwen3` command: greedy generation from a safetensors checkpoint on one
-// B200, with the reference program's flags, input format, stopping rule and
-// JSON output (qwen3/main.cpp:15-110, 330-370):
+// B200. Its flags, input format, stopping rule, messages and JSON output are
+// the reference program's interface (qwen3/main.cpp:15-110, 330-370):
 //
 //   qwen3 --model-dir DIR --input-ids FILE|- --max-new-tokens N [--max-seq-len N]
 //         [--device N]
@@ -11,95 +11,103 @@
 // stderr and exit 1. Unlike the reference (Qwen3-8B only, 508 synchronous
 // launches per token), any Qwen3 checkpoint with head_dim 128 runs, and
 // prompt plus generation run device-resident with one host synchronisation.
+#include <cctype>
 #include <cstdint>
-#include <cstdlib>
 #include <fstream>
 #include <iostream>
-#include <limits>
+#include <iterator>
+#include <sstream>
 #include <stdexcept>
 #include <string>
 #include <vector>
 
+#include "cli.hpp"
 #include "xpu_cuda.h"
 
 namespace {
 
-constexpr uint32_t kMaximumContext = 40960;  // qwen3/model.hpp:18
+using namespace xpu_cli;
 
-struct Options {
+constexpr uint32_t kMaximumContext = 40960;  // qwen3/model.hpp:18
+constexpr const char *kUsage =
+    "Usage: qwen3 --model-dir DIR --input-ids FILE|- --max-new-tokens N [--max-seq-len N] [--device N]";
+
+struct Request {
   std::string model_dir, input_ids;
-  uint32_t max_new_tokens = 0, max_sequence = kMaximumContext;
-  bool has_max_new_tokens = false;
-  int device = 0;
+  uint32_t max_new_tokens = 0, max_sequence = kMaximumContext, device = 0;
+  bool max_new_tokens_given = false;
 };
 
-const char *kUsage = "Usage: qwen3 --model-dir DIR --input-ids FILE|- --max-new-tokens N [--max-seq-len N] [--device N]";
+std::runtime_error usage_error(const std::string &what) { return std::runtime_error(what + "\n" + kUsage); }
 
-[[noreturn]] void usage_error(const std::string &message) { throw std::runtime_error(message + "\n" + kUsage); }
-
-uint32_t parse_u32(const std::string &text, const std::string &option, bool allow_zero) {
-  size_t used = 0;
-  unsigned long long v = 0;
+// The command line; false after --help.
+bool read_request(int argc, char **argv, Request &q) {
+  FlagTable t([](std::ostream &out) { out << kUsage << '\n'; });
+  uint32_t new_tokens = 0;
+  t.lenient_counts()
+      .text("--model-dir", &q.model_dir)
+      .text("--input-ids", &q.input_ids)
+      .count("--max-new-tokens", true, &new_tokens)
+      .count("--max-seq-len", false, &q.max_sequence)
+      .count("--device", true, &q.device);
   try {
-    v = std::stoull(text, &used);
-  } catch (...) {
-    usage_error("invalid value for " + option + ": " + text);
-  }
-  if (used != text.size() || text.empty() || text[0] == '-' || v > std::numeric_limits<uint32_t>::max() ||
-      (!allow_zero && v == 0))
-    usage_error("invalid value for " + option + ": " + text);
-  return static_cast<uint32_t>(v);
-}
-
-Options parse(int argc, char **argv) {
-  Options o;
-  for (int i = 1; i < argc; ++i) {
-    const std::string opt = argv[i];
-    if (opt == "-h" || opt == "--help") {
-      std::cout << kUsage << '\n';
-      std::exit(0);
+    if (!t.parse(argc, argv)) return false;
+  } catch (const FlagError &e) {
+    switch (e.problem) {
+      case FlagProblem::kNoValue: throw usage_error("missing value for " + e.flag);
+      case FlagProblem::kUnknown: throw usage_error("unknown option: " + e.flag);
+      default: throw usage_error("invalid value for " + e.flag + ": " + e.value);
     }
-    if (i + 1 == argc) usage_error("missing value for " + opt);
-    const std::string value = argv[++i];
-    if (opt == "--model-dir") o.model_dir = value;
-    else if (opt == "--input-ids") o.input_ids = value;
-    else if (opt == "--max-new-tokens") { o.max_new_tokens = parse_u32(value, opt, true); o.has_max_new_tokens = true; }
-    else if (opt == "--max-seq-len") o.max_sequence = parse_u32(value, opt, false);
-    else if (opt == "--device") o.device = static_cast<int>(parse_u32(value, opt, true));
-    else usage_error("unknown option: " + opt);
   }
-  if (o.model_dir.empty()) usage_error("--model-dir is required");
-  if (o.input_ids.empty()) usage_error("--input-ids is required");
-  if (!o.has_max_new_tokens) usage_error("--max-new-tokens is required");
-  if (o.max_sequence > kMaximumContext) usage_error("--max-seq-len cannot exceed 40960");
-  return o;
+  q.max_new_tokens_given = t.given("--max-new-tokens");
+  q.max_new_tokens = new_tokens;
+  if (q.model_dir.empty()) throw usage_error("--model-dir is required");
+  if (q.input_ids.empty()) throw usage_error("--input-ids is required");
+  if (!q.max_new_tokens_given) throw usage_error("--max-new-tokens is required");
+  if (q.max_sequence > kMaximumContext) throw usage_error("--max-seq-len cannot exceed 40960");
+  return true;
 }
 
-std::vector<uint32_t> read_ids(const Options &o, uint32_t vocab) {
-  std::ifstream file;
-  std::istream *in = &std::cin;
-  if (o.input_ids != "-") {
-    file.open(o.input_ids);
-    if (!file) throw std::runtime_error("cannot open input token file: " + o.input_ids);
-    in = &file;
+// One whitespace-free word of the id list -> token id. A word that does not
+// start like a number (optional sign, then a digit) or does not fit 64 bits
+// is not an id at all; a number with trailing characters, a negative one or
+// one past the vocabulary is outside the id range.
+uint32_t word_to_id(const std::string &word, uint32_t vocab) {
+  const size_t digits_at = (word[0] == '+' || word[0] == '-') ? 1 : 0;
+  if (digits_at >= word.size() || !std::isdigit(static_cast<unsigned char>(word[digits_at])))
+    throw std::runtime_error("invalid input token ID: " + word);
+  size_t end = digits_at;
+  while (end < word.size() && std::isdigit(static_cast<unsigned char>(word[end]))) ++end;
+  uint64_t value = 0;
+  if (!read_count(std::string_view(word).substr(0, end), true, value))
+    throw std::runtime_error("invalid input token ID: " + word);
+  if (end != word.size() || value >= vocab)
+    throw std::runtime_error("input token ID is outside [0, " + std::to_string(vocab - 1) + "]: " + word);
+  return static_cast<uint32_t>(value);
+}
+
+std::vector<uint32_t> read_prompt(const Request &q, uint32_t vocab) {
+  std::string text;
+  if (q.input_ids == "-") {
+    text.assign(std::istreambuf_iterator<char>(std::cin), std::istreambuf_iterator<char>());
+    if (std::cin.bad()) throw std::runtime_error("failed while reading input token IDs");
+  } else {
+    std::ifstream file(q.input_ids, std::ios::binary);
+    if (!file) throw std::runtime_error("cannot open input token file: " + q.input_ids);
+    text.assign(std::istreambuf_iterator<char>(file), std::istreambuf_iterator<char>());
+    if (file.bad()) throw std::runtime_error("failed while reading input token IDs");
   }
   std::vector<uint32_t> ids;
-  std::string tok;
-  while (*in >> tok) {
-    size_t used = 0;
-    unsigned long long v = 0;
-    try {
-      v = std::stoull(tok, &used);
-    } catch (...) {
-      throw std::runtime_error("invalid input token ID: " + tok);
-    }
-    if (used != tok.size() || tok[0] == '-' || v >= vocab)
-      throw std::runtime_error("input token ID is outside [0, " + std::to_string(vocab - 1) + "]: " + tok);
-    ids.push_back(static_cast<uint32_t>(v));
+  size_t at = 0;
+  while (true) {
+    at = text.find_first_not_of(" \t\n\v\f\r", at);
+    if (at == std::string::npos) break;
+    const size_t stop = std::min(text.find_first_of(" \t\n\v\f\r", at), text.size());
+    ids.push_back(word_to_id(text.substr(at, stop - at), vocab));
+    at = stop;
   }
-  if (!in->eof()) throw std::runtime_error("failed while reading input token IDs");
   if (ids.empty()) throw std::runtime_error("at least one input token ID is required");
-  if (ids.size() > o.max_sequence || o.max_new_tokens > o.max_sequence - ids.size())
+  if (ids.size() > q.max_sequence || q.max_new_tokens > q.max_sequence - ids.size())
     throw std::runtime_error("prompt plus requested generation exceeds --max-seq-len");
   return ids;
 }
@@ -108,31 +116,43 @@ void check(int status, const char *what) {
   if (status != XPU_OK) throw std::runtime_error(std::string(what) + ": " + xpu_last_error());
 }
 
+// Owns the engine handle for the lifetime of one run.
+struct EngineHandle {
+  xpu_qwen3_engine *e = nullptr;
+  ~EngineHandle() {
+    if (e) xpu_qwen3_destroy(e);
+  }
+};
+
+std::string generate(const Request &q) {
+  xpu_qwen3_shape shape{};
+  check(xpu_qwen3_read_config(q.model_dir.c_str(), &shape), "config");
+  const std::vector<uint32_t> prompt = read_prompt(q, shape.vocab_size);
+  EngineHandle engine;
+  check(xpu_qwen3_create(&shape, q.max_sequence, static_cast<int>(q.device), 0, 1, &engine.e), "engine");
+  check(xpu_qwen3_load_checkpoint(engine.e, q.model_dir.c_str()), "checkpoint");
+  std::vector<uint32_t> out(q.max_new_tokens ? q.max_new_tokens : 1);
+  uint32_t produced = 0;
+  if (q.max_new_tokens)
+    check(xpu_qwen3_generate(engine.e, prompt.data(), static_cast<uint32_t>(prompt.size()), q.max_new_tokens, 1,
+                             out.data(), &produced),
+          "generate");
+  std::ostringstream json;
+  json << "{\"generated_ids\":[";
+  for (uint32_t i = 0; i < produced; ++i) json << (i ? "," : "") << out[i];
+  json << "]}\n";
+  return json.str();
+}
+
 }  // namespace
 
 int main(int argc, char **argv) {
-  xpu_qwen3_engine *engine = nullptr;
   try {
-    const Options o = parse(argc, argv);
-    xpu_qwen3_shape shape{};
-    check(xpu_qwen3_read_config(o.model_dir.c_str(), &shape), "config");
-    const std::vector<uint32_t> prompt = read_ids(o, shape.vocab_size);
-    check(xpu_qwen3_create(&shape, o.max_sequence, o.device, 0, 1, &engine), "engine");
-    check(xpu_qwen3_load_checkpoint(engine, o.model_dir.c_str()), "checkpoint");
-    std::vector<uint32_t> out(o.max_new_tokens ? o.max_new_tokens : 1);
-    uint32_t count = 0;
-    if (o.max_new_tokens)
-      check(xpu_qwen3_generate(engine, prompt.data(), static_cast<uint32_t>(prompt.size()), o.max_new_tokens, 1,
-                               out.data(), &count),
-            "generate");
-    xpu_qwen3_destroy(engine);
-    engine = nullptr;
-    std::cout << "{\"generated_ids\":[";
-    for (uint32_t i = 0; i < count; ++i) std::cout << (i ? "," : "") << out[i];
-    std::cout << "]}\n";
+    Request q;
+    if (!read_request(argc, argv, q)) return 0;
+    std::cout << generate(q);
     return 0;
   } catch (const std::exception &e) {
-    if (engine) xpu_qwen3_destroy(engine);
     std::cerr << "qwen3: " << e.what() << '\n';
     return 1;
   }
