@@ -50,10 +50,10 @@ sys.path.insert(0, str(ROOT))
 METRIC = "Qwen3 decode tok/s @1/2/4/8 B200; GEMV GB/s & GEMM TFLOP/s vs roofline"
 FALLBACK_HBM_GBS = 6650.0  # profiling recipe's fallback, used only without MEASURED_PEAKS.json
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of k_step divided by
-# its algorithmic bytes, from the ncu capture summarised in
-# profiles/k_step_qwen3-8b_decode.md (2.0334 GB read + 3.6 MB written for 2.0333 GB
-# of algorithmic bytes on the 8B-shaped 2-layer step; traffic grows with the
-# weights streamed, so the ratio carries over to 36 layers).
+# its algorithmic bytes, measured by ncu on the 8B-shaped 2-layer step
+# (2.0334 GB read + 3.6 MB written for 2.0333 GB of algorithmic bytes at a
+# 2051-position context); traffic grows with the weights streamed, so the
+# ratio carries over to 36 layers.
 TRAFFIC_RATIO = 1.002
 
 
@@ -72,6 +72,8 @@ def parse_args():
     ap.add_argument("--no-small", action="store_true", help="skip the Qwen3-0.6B decode measurement in extra")
     ap.add_argument("--batch", type=int, default=16,
                     help="sequences of the batched-decode measurement in extra (0: skip)")
+    ap.add_argument("--record-tokens", metavar="PATH",
+                    help="write this run's greedy tokens as the stored run the token check compares with")
     return ap.parse_args()
 
 
@@ -150,12 +152,18 @@ def seeded_prompt(n: int, vocab: int, seed: int = 7) -> list[int]:
     return [int(t) for t in np.random.default_rng(seed).integers(0, vocab, size=n)]
 
 
+def row_shard(m: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [r0, r1) of an m-row matrix that rank `rank` of `world` holds."""
+    return m * rank // world, m * (rank + 1) // world
+
+
 def gemv_extra(torch, device, rank: int = 0, world: int = 1) -> dict:
     """GEMV GB/s at BASELINE configs[0]/[1] shapes (seeded uniform inputs,
     matrix read once per launch, inputs rotated so nothing stays in L2). With
     world > 1 the 16384 x 16384 matrices are row-sharded: rank r holds rows
-    [r M / world, (r + 1) M / world), and GB/s is the whole matrix over the
-    max-over-ranks time; the 4096 x 4096 GEMV stays on rank 0."""
+    [r M / world, (r + 1) M / world) of the one seeded matrix, and GB/s is
+    the whole matrix over the max-over-ranks time; the 4096 x 4096 GEMV stays
+    on rank 0."""
     import torch.distributed as dist
 
     from xpu_playground_b200 import _lib, kernels
@@ -168,15 +176,16 @@ def gemv_extra(torch, device, rank: int = 0, world: int = 1) -> dict:
         if world > 1 and not sharded and rank != 0:
             continue
         m_full = m
-        if sharded:
-            m = m_full // world
+        r0, r1 = row_shard(m_full, world, rank) if sharded else (0, m_full)
+        m = r1 - r0
         copies = max(1, (512 << 20) // (2 * m * k))  # > L2 worth of matrices, used round-robin
         mats = []
         for c in range(copies):
-            A = torch.empty(m, k, dtype=dt, device=device)
-            # the rank's rows of the same seeded matrix every world size would use
-            _lib.check(L.xpu_fill_uniform16(code, A.data_ptr(), m * k, 11 + c + 1000 * rank * int(sharded), 1, None))
-            mats.append(A)
+            # every rank fills the whole seeded matrix and keeps a view of its
+            # rows, so the shards are the rows of one matrix at every N
+            full = torch.empty(m_full, k, dtype=dt, device=device)
+            _lib.check(L.xpu_fill_uniform16(code, full.data_ptr(), m_full * k, 11 + c, 1, None))
+            mats.append(full[r0:r1])
         x = torch.empty(k, dtype=dt, device=device)
         _lib.check(L.xpu_fill_uniform16(code, x.data_ptr(), k, 12, 2, None))
         y = torch.empty(m, dtype=dt, device=device)
@@ -215,7 +224,9 @@ def gemv_extra(torch, device, rank: int = 0, world: int = 1) -> dict:
 def gemm_extra(torch, device, peak_tflops: float) -> dict:
     """GEMM TFLOP/s at BASELINE configs[2] shapes (seeded uniform[-1, 1]
     operands; 5 warm-up launches, then 20 back-to-back launches timed with
-    CUDA events; operands are L2-resident, the kernel is tensor-bound)."""
+    CUDA events; operands are L2-resident, the kernel is tensor-bound), and
+    beside each the vendor library on the same operands and shape
+    (torch.matmul, i.e. cuBLAS), timed the same way."""
     from xpu_playground_b200 import _lib, kernels
     L = _lib.load()
     out = {}
@@ -239,11 +250,25 @@ def gemm_extra(torch, device, peak_tflops: float) -> dict:
         e1.synchronize()
         sec = e0.elapsed_time(e1) * 1e-3 / reps
         tf = 2.0 * m * n * k / sec / 1e12
-        out[name] = {"TFLOP/s": round(tf, 1), "us": round(sec * 1e6, 2),
-                     "frac_of_measured_bf16_peak": round(tf / peak_tflops, 4)}
         if kernels.device_status():
             raise SystemExit("GEMM device error")
-        del A, B, C
+        C2 = torch.empty_like(C)
+        for _ in range(5):
+            torch.matmul(A, B, out=C2)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            torch.matmul(A, B, out=C2)
+        e1.record()
+        e1.synchronize()
+        sec_lib = e0.elapsed_time(e1) * 1e-3 / reps
+        tf_lib = 2.0 * m * n * k / sec_lib / 1e12
+        out[name] = {"TFLOP/s": round(tf, 1), "us": round(sec * 1e6, 2),
+                     "frac_of_measured_bf16_peak": round(tf / peak_tflops, 4),
+                     "cublas": {"TFLOP/s": round(tf_lib, 1), "us": round(sec_lib * 1e6, 2),
+                                "call": "torch.matmul on the same operands"},
+                     "vs_cublas": round(tf / tf_lib, 4)}
+        del A, B, C, C2
     return out
 
 
@@ -256,7 +281,7 @@ def batch_extra(torch, device, shape, context: int, batch: int, steps: int, warm
 
     max_seq = context + warmup + steps + 8
     eng = Qwen3Engine(shape, max_seq, device=device.index or 0, max_batch=batch)
-    eng.init_synthetic(2026)
+    eng.init_synthetic(WEIGHT_SEED)
     prompts = [seeded_prompt(context, shape.vocab, seed=7 + s) for s in range(batch)]
     eng.batch_generate(prompts, 1)  # prefill: context batched steps
     stream = torch.cuda.ExternalStream(eng.info().stream, device=device)
@@ -301,7 +326,7 @@ def small_extra(torch, device, warmup: int) -> dict:
 
     shape, prompt_len, steps = PRESETS["qwen3-0.6b"], 128, 128
     eng = Qwen3Engine(shape, prompt_len + warmup + steps + 8, device=device.index or 0)
-    eng.init_synthetic(2026)
+    eng.init_synthetic(WEIGHT_SEED)
     eng.prefill(seeded_prompt(prompt_len, shape.vocab))
     stream = torch.cuda.ExternalStream(eng.info().stream, device=device)
     eng.enqueue_steps(warmup)
@@ -336,12 +361,48 @@ def measured_tflops() -> float:
 
 
 def decode_config(args, shape) -> dict:
-    """The workload keys both arms report (the reference arm times the same
-    model shape, prompt length and decode steps on the host)."""
+    """The workload both arms report, identically (the reference arm times
+    the same model shape and prompt length on the host)."""
     return {"workload": f"{args.preset}-shaped greedy decode, batch 1, {args.context}-token prompt then "
                         f"{args.steps} timed decode steps",
             "layers": shape.layers, "hidden": shape.hidden, "heads": f"{shape.q_heads}/{shape.kv_heads}",
-            "intermediate": shape.intermediate, "vocab": shape.vocab, "tied_lm_head": shape.tied}
+            "intermediate": shape.intermediate, "vocab": shape.vocab, "tied_lm_head": shape.tied,
+            "context": args.context,
+            "l2": "inputs larger than L2: each step streams all weights (15.4 GB for the 8B shape) once"}
+
+
+WEIGHT_SEED = 2026
+GOLDEN_TOKENS = ROOT / "tests" / "golden" / "decode_tokens_qwen3-8b.json"
+
+
+def token_digest(ids: list[int]) -> str:
+    import hashlib
+    import struct
+    return hashlib.sha256(struct.pack(f"<{len(ids)}I", *ids)).hexdigest()
+
+
+def check_tokens(args, first: int, ids: list[int]) -> dict:
+    """The run's greedy tokens against the stored one-GPU run of the same
+    weights seed, prompt and prefill (tests/golden/decode_tokens_qwen3-8b.json,
+    written by `bench.py --record-tokens` on one GPU): the common prefix must
+    be identical."""
+    info = {"first_position": first, "count": len(ids), "sha256": token_digest(ids), "ids": ids,
+            "prefill": "token by token through the decode step (xpu_qwen3_generate), at every N"}
+    try:
+        gold = json.loads(GOLDEN_TOKENS.read_text())
+    except (OSError, ValueError):
+        info["golden"] = None
+        return info
+    same_run = (gold.get("preset") == args.preset and gold.get("context") == args.context and
+                gold.get("weight_seed") == WEIGHT_SEED and gold.get("first_position") == first)
+    if not same_run:
+        info["golden"] = None
+        return info
+    n = min(len(ids), len(gold["ids"]))
+    info["golden"] = {"file": str(GOLDEN_TOKENS.relative_to(ROOT)), "n_gpus": gold.get("n_gpus"),
+                      "compared": n, "sha256_of_compared": token_digest(gold["ids"][:n]),
+                      "match": ids[:n] == gold["ids"][:n]}
+    return info
 
 
 def run_ours(args) -> None:
@@ -362,7 +423,7 @@ def run_ours(args) -> None:
     max_seq = args.context + W + K + E + 8
     mode = args.mode if world == 1 else "persistent"  # tensor parallel runs the persistent step
     eng = Qwen3Engine(shape, max_seq, device=local, tp_rank=rank, tp_size=world, mode=mode)
-    eng.init_synthetic(2026)
+    eng.init_synthetic(WEIGHT_SEED)
     if world > 1:
         eng.connect_tensor_parallel(dist.new_group(backend="gloo"))
     prompt = seeded_prompt(args.context, shape.vocab)
@@ -375,8 +436,10 @@ def run_ours(args) -> None:
         prefill_info = {"tokens": args.context, "seconds": round(t_pre, 4),
                         "tok_s": round(args.context / t_pre, 1), "positions_per_step": 16,
                         "timing": "host wall clock around xpu_qwen3_prefill (synchronous)"}
-    else:
-        eng.generate(prompt, 1)  # tensor parallel: device-resident prefill, token by token
+    # The decode that is timed and checked follows the same prefill at every
+    # N (the prompt token by token through the decode step, device-resident),
+    # so its greedy tokens can be compared across GPU counts bit for bit.
+    eng.generate(prompt, 1)
     stream = torch.cuda.ExternalStream(eng.info().stream, device=device)
     eng.enqueue_steps(W)
     eng.synchronize()
@@ -419,6 +482,14 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
+    first = args.context - 1  # the prompt's last position holds the first generated token
+    tokens = check_tokens(args, first, eng.token_log(first, pos1 + E - first))
+    if args.record_tokens and rank == 0:
+        Path(args.record_tokens).write_text(json.dumps(
+            {"preset": args.preset, "context": args.context, "weight_seed": WEIGHT_SEED,
+             "prompt": "bench.seeded_prompt(context, vocab) (numpy default_rng(7))", "n_gpus": world,
+             "first_position": first, "ids": tokens["ids"], "sha256": tokens["sha256"]}) + "\n")
+
     mid_context = (pos0 + pos1) // 2
     bytes_step = eng.bytes_per_token(mid_context)
     achieved = bytes_step / (ms * 1e-3) / 1e9
@@ -439,62 +510,68 @@ def run_ours(args) -> None:
         extra.update(gemv_extra(torch, device, rank, world))
         if rank == 0:
             extra.update(gemm_extra(torch, device, measured_tflops()))
-        if rank == 0 and not args.no_cpu_baseline:
-            # the reference's host loops on this box's cores, beside the GPU numbers
-            from oracle.cpu_baseline import gemm_cpu_baseline, gemv_cpu_baseline
-            for key, (m, k) in (("gemv_4096_bf16", (4096, 4096)), ("gemv_16384_bf16", (16384, 16384))):
-                if key in extra:
-                    extra[key]["cpu_baseline"] = gemv_cpu_baseline(m, k)
-            if "gemm_4096_bf16" in extra:
-                extra["gemm_4096_bf16"]["cpu_baseline"] = gemm_cpu_baseline(4096, 4096, 4096)
-    cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
-        from oracle.cpu_baseline import hf_decode_baseline
-        cpu = hf_decode_baseline(shape, args.context, steps=4)
-        cpu.pop("per_token_s", None)
-        cpu["value"] = round(cpu["value"], 3)
-
-    if rank == 0:
-        value = 1000.0 / ms
-        line = {
-            "metric": METRIC,
-            "value": round(value, 2),
-            "unit": "tok/s",
-            "n_gpus": world,
-            "steps": K,
-            "warmup": W,
-            "ms_per_step": round(ms, 4),
-            "higher_is_better": True,
-            "scaling": "strong",
-            "vs_baseline": None,
-            "dtype": "bf16",
-            "data": "synthetic (seeded N(0,0.02) bf16 weights, seeded uniform prompt ids)",
-            "config": {
-                **decode_config(args, shape),
-                "context_tokens": [pos0, pos1],
-                "decode_mode": mode,
-                "parallelism": "single GPU" if world == 1 else f"tp{world} (tensor parallel, one sequence)",
-                "l2": "inputs larger than L2: each step streams all weights (15.4 GB) once",
-            },
-            "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 24,
-                    "d2h_bytes_per_step": 32},
-            "roofline": {
-                "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4),
-                "traffic": round(TRAFFIC_RATIO * bytes_step) if TRAFFIC_RATIO else None,
-                "kernel": "k_step (persistent decode step)" if args.mode == "persistent" else "decode graph",
-                "algorithmic_bytes_per_launch": bytes_step,
-                "peak_source": f"{peak_kind} HBM copy bandwidth",
-            },
-            "cpu_baseline": cpu,
-            "clocks": clock_info,
-            "gpu_launches": K * eng.info().kernels_per_step,
-            "extra": extra,
-        }
-        print(json.dumps(line))
+    launches = K * eng.info().kernels_per_step
     eng.close()
     if world > 1:
         dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    # The host-core baselines run on rank 0 after every GPU rank is done, on
+    # the threads this process may use.
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import oracle as orc
+        from oracle.cpu_baseline import gemm_cpu_baseline, gemv_cpu_baseline, hf_decode_baseline, host_threads
+        orc.set_threads(host_threads())
+        for key, (m, k) in (("gemv_4096_bf16", (4096, 4096)), ("gemv_16384_bf16", (16384, 16384))):
+            if key in extra:
+                extra[key]["cpu_baseline"] = gemv_cpu_baseline(m, k)
+        if "gemm_4096_bf16" in extra:
+            extra["gemm_4096_bf16"]["cpu_baseline"] = gemm_cpu_baseline(4096, 4096, 4096)
+        cpu = hf_decode_baseline(shape, args.context)
+        cpu.pop("per_token_s", None)
+        cpu["value"] = round(cpu["value"], 3)
+
+    value = 1000.0 / ms
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) bf16 weights, seeded uniform prompt ids)",
+        "config": decode_config(args, shape),
+        "run": {
+            "context_tokens": [pos0, pos1],
+            "decode_mode": mode,
+            "parallelism": "single GPU" if world == 1 else f"tp{world} (tensor parallel, one sequence)",
+        },
+        "e2e": {"value": round(1000.0 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 24,
+                "d2h_bytes_per_step": 32},
+        "roofline": {
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4),
+            "traffic": round(TRAFFIC_RATIO * bytes_step) if TRAFFIC_RATIO else None,
+            "kernel": "k_step (persistent decode step)" if mode == "persistent" else "decode graph",
+            "algorithmic_bytes_per_launch": bytes_step,
+            "peak_source": f"{peak_kind} HBM copy bandwidth",
+        },
+        "cpu_baseline": cpu,
+        "clocks": clock_info,
+        "gpu_launches": launches,
+        "tokens": tokens,
+        "extra": extra,
+    }
+    print(json.dumps(line), flush=True)
+    if tokens.get("golden") and not tokens["golden"]["match"]:
+        sys.exit(f"greedy tokens differ from the stored one-GPU run ({tokens['golden']['file']})")
 
 
 def run_reference(args) -> None:
@@ -506,7 +583,7 @@ def run_reference(args) -> None:
 
     shape = PRESETS[args.preset]
     t0 = time.time()
-    cpu = hf_decode_baseline(shape, args.context, steps=max(2, min(args.steps, 6)))
+    cpu = hf_decode_baseline(shape, args.context)
     value = cpu["value"]
     cpu.pop("per_token_s", None)
     line = {
@@ -522,13 +599,14 @@ def run_reference(args) -> None:
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (random N(0,0.02) bf16 weights, seeded prompt ids)",
-        "config": {**decode_config(args, shape), "parallelism": "host CPU (rank 0 alone)"},
+        "data": "synthetic (seeded N(0,0.02) bf16 weights, seeded uniform prompt ids)",
+        "config": decode_config(args, shape),
+        "run": {"parallelism": "host CPU (rank 0 alone)"},
         "cpu_baseline": dict(cpu, value=round(value, 3)),
         "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": round(time.time() - t0, 1),
     }
-    print(json.dumps(line))
+    print(json.dumps(line), flush=True)
 
 
 def main():

@@ -145,9 +145,11 @@ int xpu_qwen_attention(const uint16_t *query, const uint16_t *key_cache,
  * larger requests return XPU_ERR_INVALID. The array costs 6 MiB on each device
  * where this code is loaded, until exit. The first call on a device looks up
  * the array's device address (cudaGetSymbolAddress), so make that first call
- * before any stream capture. All calls share the one array: calls that can
- * overlap on the GPU (different streams, or different threads on one device)
- * race on it and must be ordered by the caller. */
+ * before any stream capture; after a cudaDeviceReset the next call looks it up
+ * again. All calls share the one array: calls that can overlap on the GPU
+ * (different streams, or different threads on one device) race on it and
+ * must be ordered by the caller (the qwen3::LevelZeroRuntime class does this
+ * for its attention launches with a per-device lock). */
 int xpu_qwen_attention_noalloc(const uint16_t *query, const uint16_t *key_cache,
                                const uint16_t *value_cache, uint16_t *output, uint32_t position,
                                uint32_t query_heads, uint32_t key_value_heads, void *stream);
@@ -278,6 +280,14 @@ int xpu_qwen3_set_mode(xpu_qwen3_engine *engine, int mode);
  * per-CTA globaltimer stamps (ns) of the last step's phase boundaries,
  * [cta][event]; *count = total stamps available (0 when tracing is off). */
 int xpu_qwen3_trace(xpu_qwen3_engine *engine, uint64_t *host_ns, uint32_t capacity, uint32_t *count);
+/* Greedy token of every step at positions [first_position, first_position +
+ * count): entry p is the token the step at position p produced (the prompt's
+ * last position holds the first generated token), as main.cpp:345-352 would
+ * print them; written by every decode path (decode, generate, device-resident
+ * steps, prefill). No counterpart call in the reference, whose engine returns
+ * each token from decode(). */
+int xpu_qwen3_token_log(xpu_qwen3_engine *engine, uint32_t first_position, uint32_t count,
+                        uint32_t *host_out);
 /* bf16 logits of the last step (this rank's vocab_rows rows). */
 int xpu_qwen3_logits(xpu_qwen3_engine *engine, uint16_t *host_out, uint32_t count);
 int xpu_qwen3_info(xpu_qwen3_engine *engine, xpu_qwen3_info_t *info);

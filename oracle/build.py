@@ -26,7 +26,10 @@ HERE = Path(__file__).resolve().parent
 BUILD = HERE / "_build"
 REF_OUT = HERE / "_ref"
 LIB = BUILD / "liboracle.so"
-REFERENCE = Path(os.environ.get("XPU_REFERENCE_TREE", "/root/reference"))
+# The reference checkout: XPU_REFERENCE_TREE, else a directory named
+# "reference" beside this repository (absent on GPU boxes: the prebuilt
+# oracle/_ref files are used there).
+REFERENCE = Path(os.environ.get("XPU_REFERENCE_TREE", str(HERE.parent.parent / "reference")))
 
 
 def _stale(target: Path, sources: list[Path]) -> bool:

@@ -5,24 +5,52 @@ transformers' Qwen3ForCausalLM in bf16 with eager attention, greedy,
 KV-cached (reference.py:11-45). This module times that model on the host's
 cores for a bounded sample of the benchmark workload:
 
-* the model is built with the benchmark's layer shapes and vocabulary, but
-  with `sample_layers` (two depths, default 1 and 3) instead of all layers,
-  with random bf16 weights (timing does not depend on their values);
-* each sample model prefills the benchmark's prompt length in one batched
-  forward (as reference.py's generate does) and then times `steps` cached
-  one-token decode steps;
-* per-token time is fitted as fixed + layers * per_layer from the two depths
-  and evaluated at the full depth: tok/s = 1 / (fixed + L * per_layer).
+* one model is built with the benchmark's layer shapes and vocabulary and
+  the deepest sample depth (default 8 layers), random bf16 weights (timing
+  does not depend on their values);
+* for each sample depth d (default 1, 2, 4, 8) the model runs its first d
+  layers: it prefills the benchmark's prompt length in one batched forward
+  (as reference.py's generate does), then times `repeats` runs of `steps`
+  cached one-token decode steps; the depth's time is its fastest run (the
+  host is shared with other jobs, whose interference only ever adds time);
+* per-token time is a least-squares line fixed + d * per_layer through the
+  depths, evaluated at the full depth: tok/s = 1 / (fixed + L * per_layer).
+  The line's worst relative residual and each depth's repeat spread are
+  reported with the value.
 
-Used by bench.py's cpu_baseline leg and its --impl reference arm.
+The thread count is the host threads this process may run on (its CPU
+affinity, capped by a cgroup CPU quota when one is set), stated as `cores`.
+Used by bench.py's cpu_baseline leg and its --impl reference arm, with the
+same arguments in both.
 """
 
 from __future__ import annotations
 
 import os
+import statistics
 import time
 
 from xpu_playground_b200.qwen3_config import HEAD_DIM, Qwen3Shape
+
+SAMPLE_DEPTHS = (1, 2, 4, 8)
+SAMPLE_STEPS = 16
+SAMPLE_REPEATS = 5
+
+
+def host_threads() -> int:
+    """CPUs this process may use: its affinity set, capped by a cgroup v2
+    CPU quota (cpu.max) when one is set."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        n = os.cpu_count() or 1
+    try:
+        quota, period = open("/sys/fs/cgroup/cpu.max").read().split()[:2]
+        if quota != "max":
+            n = min(n, max(1, int(int(quota) / int(period))))
+    except (OSError, ValueError):
+        pass
+    return max(1, n)
 
 
 def _build(shape: Qwen3Shape, layers: int):
@@ -51,13 +79,23 @@ def _build(shape: Qwen3Shape, layers: int):
     return model.eval()
 
 
-def _time_depth(shape: Qwen3Shape, layers: int, context: int, steps: int) -> float:
-    """Seconds per cached decode step at `context` prompt tokens."""
+def _use_depth(model, layers, layer_types, depth: int) -> None:
+    """Make the model run only its first `depth` decoder layers."""
+    model.model.layers = layers[:depth]
+    model.config.num_hidden_layers = depth
+    if layer_types is not None:
+        model.config.layer_types = list(layer_types[:depth])
+
+
+def _time_steps(model, shape: Qwen3Shape, context: int, steps: int, repeats: int) -> list[float]:
+    """Seconds per cached decode step after one `context`-token prefill:
+    `repeats` consecutive runs of `steps` steps (the context grows by
+    `steps` per run, a negligible change at benchmark lengths)."""
     import torch
 
-    model = _build(shape, layers)
     g = torch.Generator().manual_seed(1)
     ids = torch.randint(0, shape.vocab, (1, context), generator=g)
+    runs = []
     with torch.no_grad():
         out = model(input_ids=ids, use_cache=True, logits_to_keep=1)
         past = out.past_key_values
@@ -66,38 +104,65 @@ def _time_depth(shape: Qwen3Shape, layers: int, context: int, steps: int) -> flo
         # one untimed step, then the timed ones
         out = model(input_ids=tok, position_ids=torch.tensor([[pos]]), past_key_values=past, use_cache=True)
         past, tok, pos = out.past_key_values, out.logits[:, -1].argmax(-1, keepdim=True), pos + 1
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            out = model(input_ids=tok, position_ids=torch.tensor([[pos]]), past_key_values=past, use_cache=True)
-            past, tok, pos = out.past_key_values, out.logits[:, -1].argmax(-1, keepdim=True), pos + 1
-        dt = (time.perf_counter() - t0) / steps
-    del model, past, out
-    return dt
+        for _ in range(repeats):
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                out = model(input_ids=tok, position_ids=torch.tensor([[pos]]), past_key_values=past,
+                            use_cache=True)
+                past, tok, pos = out.past_key_values, out.logits[:, -1].argmax(-1, keepdim=True), pos + 1
+            runs.append((time.perf_counter() - t0) / steps)
+    del past, out
+    return runs
 
 
-def hf_decode_baseline(shape: Qwen3Shape, context: int, steps: int = 6,
-                       sample_layers: tuple[int, int] = (1, 3), threads: int | None = None) -> dict:
+def fit_line(points: dict[int, float]) -> tuple[float, float, float]:
+    """Least-squares t = fixed + d * per_layer through (d, t); returns
+    (fixed, per_layer, worst relative residual)."""
+    ds = sorted(points)
+    n = len(ds)
+    md = sum(ds) / n
+    mt = sum(points[d] for d in ds) / n
+    sdd = sum((d - md) ** 2 for d in ds)
+    per_layer = sum((d - md) * (points[d] - mt) for d in ds) / sdd if sdd else 0.0
+    fixed = mt - per_layer * md
+    resid = max(abs(fixed + d * per_layer - points[d]) / points[d] for d in ds)
+    return fixed, per_layer, resid
+
+
+def hf_decode_baseline(shape: Qwen3Shape, context: int, steps: int = SAMPLE_STEPS,
+                       depths: tuple[int, ...] = SAMPLE_DEPTHS, repeats: int = SAMPLE_REPEATS,
+                       threads: int | None = None) -> dict:
     import torch
 
-    threads = threads or os.cpu_count() or 1
+    threads = threads or host_threads()
     torch.set_num_threads(threads)
     t_start = time.perf_counter()
-    l0, l1 = sample_layers
-    t0 = _time_depth(shape, l0, context, steps)
-    t1 = _time_depth(shape, l1, context, steps)
-    per_layer = max((t1 - t0) / (l1 - l0), 0.0)
-    fixed = max(t0 - l0 * per_layer, 0.0)
+    model = _build(shape, max(depths))
+    layers, layer_types = model.model.layers, getattr(model.config, "layer_types", None)
+    best, spreads = {}, {}
+    for d in depths:
+        _use_depth(model, layers, layer_types, d)
+        reps = _time_steps(model, shape, context, steps, repeats)
+        best[d] = min(reps)
+        spreads[d] = (max(reps) - min(reps)) / statistics.median(reps)
+    del model, layers
+    fixed, per_layer, resid = fit_line(best)
     per_token = fixed + shape.layers * per_layer
+    depth_ms = ", ".join(f"{d}: {best[d] * 1e3:.2f} ms" for d in depths)
     return {
         "value": 1.0 / per_token,
         "unit": "tok/s",
         "cores": threads,
         "kind": "port",
-        "sample": (f"transformers Qwen3ForCausalLM bf16 eager (qwen3/reference.py's model) on the host: "
-                   f"{l0}- and {l1}-layer models with this shape, {context}-token batched prefill, "
-                   f"{steps} timed cached decode steps each; per-token time fitted as fixed + layers * "
-                   f"per_layer ({fixed * 1e3:.1f} ms + {shape.layers} x {per_layer * 1e3:.2f} ms) "
-                   f"at {shape.layers} layers; {time.perf_counter() - t_start:.0f} s of host time"),
+        "sample": (f"transformers Qwen3ForCausalLM bf16 eager (qwen3/reference.py's model) on {threads} host "
+                   f"threads: the model's first d layers for d in {list(depths)} (this shape), "
+                   f"{context}-token batched prefill, then {repeats} runs of {steps} timed cached decode steps, "
+                   f"fastest run per depth ({depth_ms}); per-token time = least-squares fixed + d x per_layer "
+                   f"({fixed * 1e3:.2f} ms + {shape.layers} x {per_layer * 1e3:.3f} ms) at {shape.layers} "
+                   f"layers; {time.perf_counter() - t_start:.0f} s of host time"),
+        "fit": {"fixed_ms": round(fixed * 1e3, 3), "per_layer_ms": round(per_layer * 1e3, 4),
+                "worst_residual": round(resid, 4),
+                "repeat_spread": {str(d): round(spreads[d], 4) for d in depths}},
         "per_token_s": per_token,
     }
 

@@ -87,6 +87,7 @@ SIGNATURES: dict[str, tuple] = {
     "xpu_qwen3_synchronize": (i32, [vp]),
     "xpu_qwen3_set_mode": (i32, [vp, i32]),
     "xpu_qwen3_trace": (i32, [vp, vp, u32, vp]),
+    "xpu_qwen3_token_log": (i32, [vp, u32, u32, vp]),
     "xpu_qwen3_logits": (i32, [vp, vp, u32]),
     "xpu_qwen3_info": (i32, [vp, vp]),
     "xpu_qwen3_bytes_per_token": (u64, [vp, u32]),

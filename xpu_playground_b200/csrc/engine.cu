@@ -427,6 +427,13 @@ class Qwen3Engine {
     for (uint32_t i = 0; i < n; ++i) launch_one(s);
   }
 
+  // Greedy tokens of positions [first, first + count) from the step log.
+  void token_log(uint32_t first, uint32_t count, uint32_t *host) {
+    if (static_cast<uint64_t>(first) + count > max_seq_) throw InvalidArg("token log range exceeds the maximum sequence");
+    CK(cudaMemcpyAsync(host, log_ + first, count * sizeof(uint32_t), cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+  }
+
   void logits(uint16_t *host, uint32_t count) {
     if (count > d_.V_l) throw InvalidArg("logit count exceeds this rank's vocabulary rows");
     CK(cudaMemcpyAsync(host, logits_, count * 2ull, cudaMemcpyDeviceToHost, stream_));
@@ -1232,6 +1239,13 @@ int xpu_qwen3_get_state(xpu_qwen3_engine *engine, uint32_t *token, uint32_t *pos
 
 int xpu_qwen3_enqueue_steps(xpu_qwen3_engine *engine, uint32_t steps, void *stream) {
   return guarded([&] { eng(engine).enqueue_steps(steps, static_cast<cudaStream_t>(stream)); });
+}
+
+int xpu_qwen3_token_log(xpu_qwen3_engine *engine, uint32_t first_position, uint32_t count, uint32_t *host_out) {
+  return guarded([&] {
+    if (count && !host_out) throw xpu::InvalidArg("xpu_qwen3_token_log: null pointer");
+    if (count) eng(engine).token_log(first_position, count, host_out);
+  });
 }
 
 int xpu_qwen3_logits(xpu_qwen3_engine *engine, uint16_t *host_out, uint32_t count) {

@@ -6,7 +6,7 @@
 The default run builds a seeded synthetic model, places the decode state at
 `--context` cached positions (the KV cache contents do not change the work),
 and runs `--warm` + 1 decode steps, so that the step to capture under
-`ncu -k regex:k_step -s <warm> -c 1` is the last one. Weight initialisation
+`ncu --clock-control none -k regex:k_step -s <warm> -c 1` is the last one. Weight initialisation
 launches one fill kernel per tensor before that.
 
 Under torchrun the ranks run one tensor-parallel engine and rank 0 reports:

@@ -157,6 +157,13 @@ class Qwen3Engine:
                                                 ctypes.byref(err)))
         return tok.value, pos.value, err.value
 
+    def token_log(self, first_position: int, count: int) -> list[int]:
+        """Greedy tokens the steps at positions [first, first + count)
+        produced (xpu_qwen3_token_log)."""
+        out = np.zeros(max(count, 1), np.uint32)
+        _lib.check(self.lib.xpu_qwen3_token_log(self._h, first_position, count, out.ctypes.data))
+        return [int(t) for t in out[:count]]
+
     def set_mode(self, mode: str) -> None:
         """"persistent" (one cooperative kernel per token) or "graph"."""
         _lib.check(self.lib.xpu_qwen3_set_mode(self._h, {"persistent": 0, "graph": 1}[mode]))
