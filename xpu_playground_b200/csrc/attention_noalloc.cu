@@ -12,8 +12,15 @@
 // of kNoAllocScratchBytes (6 MiB: enough for 32 query heads at 40,960
 // positions). It occupies that much memory on every device where this code
 // is loaded, until the process exits. In host code the variable's name is
-// only a host-side stand-in, so its device address is looked up once per
-// device with cudaGetSymbolAddress (with that device current) and cached.
+// only a host-side stand-in, so its device address is looked up with
+// cudaGetSymbolAddress (with that device current) on the first call for a
+// device and cached; the first call on a device therefore does this set-up
+// and should come before any stream capture. The cache is keyed by the
+// device's current context as well, so a cudaDeviceReset (which gives the
+// device a new context, with the array at a possibly different address)
+// makes the next call look the address up again.
+#include <cuda.h>
+
 #include <mutex>
 #include <string>
 
@@ -29,23 +36,56 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mutex;
-float *g_scratch_ptr[kMaxDevices] = {};
+struct ScratchAddress {
+  unsigned long long context = 0;  // driver id of the context the address belongs to
+  float *ptr = nullptr;
+};
+ScratchAddress g_scratch[kMaxDevices];
 
-// Device address of the scratch array on the current device (looked up on
-// the first call for that device).
+typedef CUresult (*CtxGetCurrentFn)(CUcontext *);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long *);
+
+// Driver id of the context current on this thread; 0 when there is none or
+// the driver does not report it (then the address is looked up every call).
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
+// Device address of the scratch array on the current device: looked up on
+// the first call for that device (and again after its context changed).
 cudaError_t noalloc_scratch(float **out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (!g_scratch_ptr[dev]) {
+  ScratchAddress &slot = g_scratch[dev];
+  const unsigned long long context = current_context_id();
+  if (!slot.ptr || context == 0 || context != slot.context) {
     void *p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_attention_scratch);
     if (e != cudaSuccess) return e;
-    g_scratch_ptr[dev] = static_cast<float *>(p);
+    slot.ptr = static_cast<float *>(p);
+    slot.context = current_context_id();  // the lookup made the context current if it was not
   }
-  *out = g_scratch_ptr[dev];
+  *out = slot.ptr;
   return cudaSuccess;
 }
 

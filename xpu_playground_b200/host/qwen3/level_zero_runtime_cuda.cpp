@@ -14,7 +14,9 @@
 // frees them in the destructor; copies and launches are synchronous; a
 // fragment that matches no kernel or several throws; arguments are checked
 // by count and size against the kernel's parameter list; CUDA failures throw
-// std::runtime_error with the call, file and line.
+// std::runtime_error with the call, file and line. Attention launches are
+// serialised per device across runtime objects (they share the library's
+// attention scratch); every other launch runs concurrently as before.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -71,6 +73,7 @@ struct Entry {
   const char *name;                  // the reference module's kernel names contain these
   std::vector<std::size_t> sizes;    // parameter sizes, in order
   Launcher launch;
+  bool shared_scratch = false;       // runs on the library's per-device scratch array
 };
 
 constexpr std::size_t P = sizeof(void *), U = sizeof(std::uint32_t), F = sizeof(float);
@@ -109,7 +112,8 @@ const std::vector<Entry> &entries() {
          return xpu_qwen_attention_noalloc(a.get<const uint16_t *>(0), a.get<const uint16_t *>(1),
                                            a.get<const uint16_t *>(2), a.get<uint16_t *>(3), a.get<uint32_t>(4),
                                            work_items, kKvHeadsRef, s);
-       }},
+       },
+       true},
       {"QwenAddLevelZeroEntry", {P, P, U},
        [](const Args &a, std::uint32_t, cudaStream_t s) {
          return xpu_qwen_add(a.get<uint16_t *>(0), a.get<const uint16_t *>(1), a.get<uint32_t>(2), s);
@@ -135,6 +139,14 @@ struct State {
 
 std::mutex g_mutex;
 std::map<const LevelZeroRuntime *, std::unique_ptr<State>> g_states;
+
+// Attention runs on one scratch array per device shared by every caller of
+// xpu_qwen_attention_noalloc, so two runtimes on one device (each on its own
+// stream, possibly driven from two threads) must not have attention in
+// flight at the same time: a launch of such an entry holds its device's
+// lock until its stream has drained.
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_locks[kMaxScratchDevices];
 
 State &state_of(const LevelZeroRuntime *rt) {
   std::lock_guard<std::mutex> lock(g_mutex);
@@ -233,6 +245,12 @@ void LevelZeroRuntime::launch(const std::string &entry_fragment, std::uint32_t w
                                " bytes) for " + entry_fragment + ": expected " +
                                std::to_string(selected->sizes[i]) + " bytes");
   CUDA_CHECK(cudaSetDevice(st.device));
+  std::unique_lock<std::mutex> scratch_lock;
+  if (selected->shared_scratch) {
+    if (st.device < 0 || st.device >= kMaxScratchDevices)
+      throw std::runtime_error("device ordinal beyond the scratch lock table: " + std::to_string(st.device));
+    scratch_lock = std::unique_lock<std::mutex>(g_scratch_locks[st.device]);
+  }
   xpu_check(selected->launch(Args{arguments}, work_items, st.stream), entry_fragment);
   const cudaError_t e = cudaStreamSynchronize(st.stream);
   if (e != cudaSuccess) throw_cuda(e, entry_fragment.c_str(), __FILE__, __LINE__);
