@@ -52,12 +52,20 @@ struct DecodeState {
 // Every rank owns one exchange region in its device memory; every rank
 // writes into every region (its own and its peers', the latter over NVLink
 // through CUDA IPC mappings):
-//   part[2][8][H]   FP32 canonical-chunk partials of o_proj (0) and down (1):
+//   part[2][8][H]   canonical-chunk partials of o_proj (0) and down (1), one
+//                   64-bit word per value: the FP32 bits in the low half and
+//                   the epoch of the exchange that wrote it in the high half;
 //                   rank r writes chunks [8 r / tp, 8 (r + 1) / tp)
-//   flag[kMaxTp]    flag[r] = the last exchange epoch rank r has published
 //   lm[kMaxTp]      lm[r] = rank r's lm_head candidate for the current step
 // Exchange k (1-based) of a step has epoch x_base + k; a step makes
-// 2 * layers + 1 of them, so epochs only grow and never need clearing.
+// 2 * layers + 1 of them, so epochs only grow and never need clearing. A
+// value and its epoch travel in one aligned 64-bit store, which reaches the
+// reader whole (single-copy atomic), so a reader that sees the epoch it
+// expects has the value too: no fence, flag or barrier is needed between
+// the partial stores and their use. A slot is rewritten only after every
+// rank has read it: the next write of slot 0 (1) follows the other slot's
+// exchange, whose data every rank produces only after all of its CTAs have
+// passed the grid barrier that follows their reads of slot 0 (1).
 constexpr uint32_t kMaxTp = 8;
 
 struct LmSlot {
@@ -69,14 +77,12 @@ struct LmSlot {
 };
 
 struct TpLinks {
-  float *part[kMaxTp];                // region base of rank q ([2][8][H] floats)
-  unsigned long long *flag[kMaxTp];   // flag array of rank q
+  unsigned long long *part[kMaxTp];   // region base of rank q ([2][8][H] words)
   LmSlot *lm[kMaxTp];                 // lm slots of rank q
 };
 
-__host__ __device__ inline size_t tp_region_part_bytes(uint32_t H) { return static_cast<size_t>(2) * 8 * H * 4; }
-__host__ __device__ inline size_t tp_region_flag_offset(uint32_t H) { return tp_region_part_bytes(H); }
-__host__ __device__ inline size_t tp_region_lm_offset(uint32_t H) { return tp_region_flag_offset(H) + 8 * kMaxTp; }
+__host__ __device__ inline size_t tp_region_part_bytes(uint32_t H) { return static_cast<size_t>(2) * 8 * H * 8; }
+__host__ __device__ inline size_t tp_region_lm_offset(uint32_t H) { return tp_region_part_bytes(H); }
 __host__ __device__ inline size_t tp_region_bytes(uint32_t H) { return tp_region_lm_offset(H) + sizeof(LmSlot) * kMaxTp; }
 
 struct DecodeDims {

@@ -129,24 +129,6 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long
 }
 __device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
-// Waits (bounded) until every rank's flag in this rank's region reaches
-// epoch; false on a timeout (error bit 4 set) or when another waiter failed.
-__device__ inline bool wait_rank_flags(const DecodeDims &d, const DecodeBuffers &b, unsigned long long epoch) {
-  const unsigned long long *own = b.tp.flag[d.tp_rank];
-  const long long start = clock64();
-  for (uint32_t q = 0; q < d.tp_size; ++q) {
-    while (ld_relaxed_sys(own + q) < epoch) {
-      if (*reinterpret_cast<volatile uint32_t *>(&b.state->error) & kErrPipelineTimeout) return false;
-      if (clock64() - start > kWaitCycles) {
-        flag_error(b.state, kErrPipelineTimeout);
-        return false;
-      }
-    }
-  }
-  fence_acq_rel_sys();
-  return true;
-}
-
 // ------------------------------------------------------------------ QKV ----
 // Items: (tile, split) of [Wq; Wk; Wv]; partial sums to part_qkv[split][row].
 __device__ inline bool qkv_items(const DecodeDims &d, const DecodeBuffers &b, const StreamSmem &sm,
@@ -286,11 +268,19 @@ __device__ inline bool rowpar_items(const DecodeDims &d, const DecodeBuffers &b,
 }
 
 // Tensor-parallel variant: this rank's canonical-chunk partials go to every
-// rank's exchange region (slot `which`: 0 o_proj, 1 down), 4 rows per 16-byte
-// store; the residual is applied after the cross-rank barrier by
-// stage_residual_rms.
+// rank's exchange region (slot `which`: 0 o_proj, 1 down), each value as a
+// 64-bit word (epoch << 32 | FP32 bits) so that it carries its own
+// readiness; lane q of a warp writes the warp's 4 rows to rank q. The
+// residual is applied by stage_residual_rms once all words have arrived.
+__device__ __forceinline__ void st_relaxed_sys_v2(unsigned long long *p, unsigned long long a, unsigned long long b) {
+  asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+__device__ __forceinline__ unsigned long long tagged(float v, uint32_t epoch) {
+  return (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(v);
+}
+
 __device__ inline bool rowpar_items_tp(const DecodeDims &d, const DecodeBuffers &b, const StreamSmem &sm,
-                                       const StreamGeom &g, uint32_t &it, uint32_t which) {
+                                       const StreamGeom &g, uint32_t &it, uint32_t which, uint32_t epoch) {
   const uint32_t lane = lane_id(), cw = cwarp();
   for (uint32_t item = blockIdx.x; item < g.items(); item += gridDim.x) {
     const uint32_t tile = item / g.kparts, part = item % g.kparts, chunk = d.chunk0 + part;
@@ -298,32 +288,72 @@ __device__ inline bool rowpar_items_tp(const DecodeDims &d, const DecodeBuffers 
     if (!stream_consume_item<bf16>(sm, g, sm.xs + part * (g.kt / 8), it, acc)) return false;
     const uint32_t row = tile * kStageRows + kRowsPerWarp * cw;
     if (lane < d.tp_size) {
-      const size_t off = (static_cast<size_t>(which) * kCanonChunks + chunk) * d.H + row;
-      *reinterpret_cast<float4 *>(b.tp.part[lane] + off) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      unsigned long long *dst = b.tp.part[lane] + (static_cast<size_t>(which) * kCanonChunks + chunk) * d.H + row;
+      st_relaxed_sys_v2(dst, tagged(acc[0], epoch), tagged(acc[1], epoch));
+      st_relaxed_sys_v2(dst + 2, tagged(acc[2], epoch), tagged(acc[3], epoch));
     }
   }
   return true;
 }
 
-// After the cross-rank barrier: x_new = bf16(x_old + bf16(sum of the 8
-// canonical chunks of exchange slot `which`, in chunk order)) - the same
-// arithmetic as rowpar_finish - staged into xs and RMS-normalised with w
-// (as stage_rms); CTA 0 also stores x_new to x_out for the next residual.
-__device__ inline void stage_residual_rms(const DecodeDims &d, const DecodeBuffers &b, uint32_t which,
-                                          const bf16 *x_old, bf16 *x_out, const bf16 *w, uint4 *xs,
-                                          float *scratch) {
-  const uint32_t t = ctid(), H = d.H;
-  const float *part = b.tp.part[d.tp_rank] + static_cast<size_t>(which) * kCanonChunks * H;
-  float ss = 0.f;
-  for (uint32_t c = t; c < H / 8; c += kConsumerThreads) {
-    float y[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (uint32_t k = 0; k < kCanonChunks; ++k) {
-      const float4 lo = __ldcg(reinterpret_cast<const float4 *>(part + static_cast<size_t>(k) * H + 8 * c));
-      const float4 hi = __ldcg(reinterpret_cast<const float4 *>(part + static_cast<size_t>(k) * H + 8 * c + 4));
-      y[0] = __fadd_rn(y[0], lo.x); y[1] = __fadd_rn(y[1], lo.y); y[2] = __fadd_rn(y[2], lo.z); y[3] = __fadd_rn(y[3], lo.w);
-      y[4] = __fadd_rn(y[4], hi.x); y[5] = __fadd_rn(y[5], hi.y); y[6] = __fadd_rn(y[6], hi.z); y[7] = __fadd_rn(y[7], hi.w);
+__device__ __forceinline__ void ld_relaxed_sys_v2(const unsigned long long *p, unsigned long long &a,
+                                                  unsigned long long &b) {
+  asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// Waits (bounded) until chunks [k0, k0 + 4) of rows [8c, 8c + 8) in exchange
+// slot `slot` carry `epoch` (all 32 words requested before the first
+// check), and adds them to y in chunk order. False on a timeout (error bit
+// 4 set) or when another waiter failed.
+__device__ __forceinline__ bool take_chunks(const DecodeBuffers &b, const unsigned long long *slot, uint32_t H,
+                                            uint32_t c, uint32_t k0, uint32_t epoch, float (&y)[8]) {
+  unsigned long long v[4][8];
+  const long long start = clock64();
+  while (true) {
+#pragma unroll
+    for (uint32_t k = 0; k < 4; ++k)
+#pragma unroll
+      for (uint32_t j = 0; j < 8; j += 2)
+        ld_relaxed_sys_v2(slot + static_cast<size_t>(k0 + k) * H + 8 * c + j, v[k][j], v[k][j + 1]);
+    bool ready = true;
+#pragma unroll
+    for (uint32_t k = 0; k < 4; ++k)
+#pragma unroll
+      for (uint32_t j = 0; j < 8; ++j) ready &= static_cast<uint32_t>(v[k][j] >> 32) == epoch;
+    if (ready) break;
+    if (*reinterpret_cast<volatile uint32_t *>(&b.state->error) & kErrPipelineTimeout) return false;
+    if (clock64() - start > kWaitCycles) {
+      flag_error(b.state, kErrPipelineTimeout);
+      return false;
     }
+  }
+#pragma unroll
+  for (uint32_t k = 0; k < 4; ++k)
+#pragma unroll
+    for (uint32_t j = 0; j < 8; ++j) y[j] = __fadd_rn(y[j], __uint_as_float(static_cast<uint32_t>(v[k][j])));
+  return true;
+}
+
+// Tensor parallel, after a row-parallel exchange: as every rank's words of
+// exchange `epoch` arrive, x_new = bf16(x_old + bf16(sum of the 8 canonical
+// chunks of slot `which`, in chunk order)) - the arithmetic of the
+// single-GPU residual epilogue (rowpar_finish) - staged into xs and
+// RMS-normalised with w exactly as stage_rms does; CTA 0 also stores x_new
+// to x_out for the next residual. Every CTA reads every word itself: a
+// second, local round (one CTA per row range publishing its sums) measured
+// slower, since it queues a dependent round trip behind the NVLink arrival.
+// False (in every thread of the CTA) on a timeout.
+__device__ inline bool stage_residual_rms(const DecodeDims &d, const DecodeBuffers &b, uint32_t which, uint32_t epoch,
+                                          const bf16 *x_old, bf16 *x_out, const bf16 *w, uint4 *xs, float *scratch,
+                                          int *s_fail) {
+  const uint32_t t = ctid(), lane = lane_id(), cw = cwarp(), H = d.H;
+  const unsigned long long *slot = b.tp.part[d.tp_rank] + static_cast<size_t>(which) * kCanonChunks * H;
+  float ss = 0.f;
+  bool ok = true;  // after a timeout this thread stops waiting but still joins every barrier
+  for (uint32_t c = t; c < H / 8; c += kConsumerThreads) {
     const uint4 xv = ldcg16(x_old + 8 * c);
+    float y[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    ok = ok && take_chunks(b, slot, H, c, 0, epoch, y) && take_chunks(b, slot, H, c, 4, epoch, y);
     const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w};
     uint32_t o[4];
 #pragma unroll
@@ -334,7 +364,23 @@ __device__ inline void stage_residual_rms(const DecodeDims &d, const DecodeBuffe
     if (blockIdx.x == 0) reinterpret_cast<uint4 *>(x_out)[c] = nv;
     ss = sq8(nv, ss);
   }
-  ss = consumer_sum(ss, scratch);
+  // consumer_sum's tree, with every warp's "gave up" carried along, so the
+  // CTA agrees on failure without another memory round trip
+  ss = warp_sum(ss);
+  const bool bad = __any_sync(kFullMask, !ok);
+  consumer_sync();
+  if (lane == 0) {
+    scratch[cw] = ss;
+    s_fail[cw] = bad;
+  }
+  consumer_sync();
+  ss = 0.f;
+  int failed = 0;
+#pragma unroll
+  for (int i = 0; i < kConsumerWarps; ++i) {
+    ss += scratch[i];
+    failed |= s_fail[i];
+  }
   const float r = 1.0f / sqrtf(ss / static_cast<float>(H) + d.eps);
   const uint4 *w4 = reinterpret_cast<const uint4 *>(w);
   for (uint32_t c = t; c < H / 8; c += kConsumerThreads) {
@@ -350,6 +396,7 @@ __device__ inline void stage_residual_rms(const DecodeDims &d, const DecodeBuffe
     xs[c] = make_uint4(o[0], o[1], o[2], o[3]);
   }
   consumer_sync();
+  return !failed;
 }
 
 // Residual epilogue of every row tile this CTA completed:
@@ -490,8 +537,8 @@ __device__ inline bool lm_items_and_argmax(const DecodeDims &d, const DecodeBuff
             fbad |= __ldcg(&own[q].bad);
           }
         }
-        st->x_base += x_advance;
       }
+      st->x_base += x_advance;
       const uint32_t next = (fbad || fb.index == 0xffffffffu) ? 0xffffffffu : fb.index;
       if (next == 0xffffffffu) st->error |= 1u;
       st->next = next;

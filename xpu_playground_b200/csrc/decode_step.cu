@@ -28,14 +28,16 @@
 //
 // Tensor parallelism (tp_size > 1): o_proj and down write this rank's
 // canonical-chunk partials into every rank's exchange region (NVLink stores
-// through CUDA IPC mappings), then pass a cross-rank barrier: the grid
-// barrier's last arriving CTA publishes the exchange epoch to every rank's
-// flag slot, and every CTA waits until all ranks' flags carry it. Each CTA
-// then sums the 8 chunks in canonical order itself (stage_residual_rms: the
-// same arithmetic as the single-GPU residual epilogue, so every tp_size
-// yields identical bits) and stages the next RMSNorm input. The lm_head
-// candidates are exchanged the same way and combined with the lowest index
-// winning ties.
+// through CUDA IPC mappings), each value in a 64-bit word tagged with the
+// exchange's epoch, and no barrier follows: each CTA stages the next
+// RMSNorm input (stage_residual_rms) waiting word by word until every
+// rank's partials have arrived, summing the 8 chunks in canonical order
+// with the arithmetic of the single-GPU residual epilogue and staging, so
+// every tp_size yields identical bits. (On one GPU the finish-and-barrier
+// form above is faster: there the word protocol's extra memory round trips
+// cost as much as the barrier they replace.) The lm_head
+// candidates are exchanged once per step through epoch-flagged slots and
+// combined with the lowest index winning ties.
 #include <cstdlib>
 #include <vector>
 
@@ -114,31 +116,13 @@ __device__ bool grid_barrier(unsigned long long *counter, unsigned long long tar
   return *flag != 0;
 }
 
-// Cross-rank barrier: this rank's grid barrier, whose last arriving CTA
-// publishes `epoch` to every rank's flag slot after a system-scope fence;
-// every CTA then waits until all ranks' flags reach epoch, which makes every
-// rank's remote stores issued before the barrier visible here.
-__device__ bool tp_barrier(const StepParams &p, unsigned long long target, unsigned long long epoch, int *flag) {
-  consumer_sync();
-  if (ctid() == 0) {
-    __threadfence_system();  // cumulative over the CTA's peer stores (ordered by the consumer barrier)
-    const unsigned long long old = atomicAdd(p.bar, 1ull);
-    if (old + 1 == target) {
-      __threadfence_system();
-      for (uint32_t q = 0; q < p.d.tp_size; ++q) st_relaxed_sys(p.b.tp.flag[q] + p.d.tp_rank, epoch);
-    }
-    *flag = wait_rank_flags(p.d, p.b, epoch);
-  }
-  consumer_sync();
-  return *flag != 0;
-}
-
 template <int G>
 __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constant__ StepParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   __shared__ uint8_t s_last[kMaxLocalItems];
   __shared__ LmShared ls;
   __shared__ int bflag;
+  __shared__ int s_fail[kConsumerWarps];
   const DecodeDims &d = p.d;
   const DecodeBuffers &b = p.b;
   DecodeState *st = b.state;
@@ -194,11 +178,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constan
     ++nbar;
     return grid_barrier(p.bar, bar_base + static_cast<unsigned long long>(nbar) * gridDim.x, st, &bflag);
   };
-  auto xbarrier = [&]() -> bool {
-    ++nbar;
-    ++nx;
-    return tp_barrier(p, bar_base + static_cast<unsigned long long>(nbar) * gridDim.x, x_base + nx, &bflag);
-  };
+  // epoch of the next cross-rank exchange (its words carry the low 32 bits)
+  auto next_epoch = [&]() -> uint32_t { return static_cast<uint32_t>(x_base + (++nx)); };
   // Attention arrival counters only grow: every item of kv head h arrives
   // once per layer, so layer l of this step completes at base[h] + (l + 1) *
   // ipk. The bases are read before this CTA's first grid barrier; no CTA
@@ -240,12 +221,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constan
     stage_attn_parts(d, b, p.g.o, npc, n, sm.xs);
     stamp();
     if (tp) {
-      if (!rowpar_items_tp(d, b, sm, p.g.o, it, 0)) { flag_error(st, kErrPipelineTimeout); return; }
+      const uint32_t ep = next_epoch();
+      if (!rowpar_items_tp(d, b, sm, p.g.o, it, 0, ep)) { flag_error(st, kErrPipelineTimeout); return; }
       stamp();
       stamp();
-      if (!xbarrier()) return;
-      stamp();
-      stage_residual_rms(d, b, 0, b.x, b.x2, w.post_norm, sm.xs, sm.scratch);
+      stamp();  // (no barrier: the staging below waits for the exchanged words themselves)
+      if (!stage_residual_rms(d, b, 0, ep, b.x, b.x2, w.post_norm, sm.xs, sm.scratch, s_fail)) return;
     } else {
       if (!rowpar_items(d, b, sm, p.g.o, it)) { flag_error(st, kErrPipelineTimeout); return; }
       stamp();
@@ -264,13 +245,13 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constan
     stage_copy(b.h, d.I_l, sm.xs);
     stamp();
     if (tp) {
-      if (!rowpar_items_tp(d, b, sm, p.g.down, it, 1)) { flag_error(st, kErrPipelineTimeout); return; }
+      const uint32_t ep = next_epoch();
+      if (!rowpar_items_tp(d, b, sm, p.g.down, it, 1, ep)) { flag_error(st, kErrPipelineTimeout); return; }
       stamp();
       stamp();
-      if (!xbarrier()) return;
       stamp();
       const bf16 *next_norm = l + 1 < p.n_layers ? p.layers[l + 1].in_norm : b.final_norm;
-      stage_residual_rms(d, b, 1, b.x2, b.x, next_norm, sm.xs, sm.scratch);
+      if (!stage_residual_rms(d, b, 1, ep, b.x2, b.x, next_norm, sm.xs, sm.scratch, s_fail)) return;
     } else {
       if (!rowpar_items(d, b, sm, p.g.down, it)) { flag_error(st, kErrPipelineTimeout); return; }
       stamp();
@@ -282,6 +263,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_step(const __grid_constan
   }
   if (!tp) stage_rms(b.x, b.final_norm, d.H, d.eps, sm.xs, sm.scratch);
   stamp();
+  // (tensor parallel: one more exchange, of the lm_head candidates)
   if (!lm_items_and_argmax(d, b, sm, p.g.lm, it, ls, pos, static_cast<uint64_t>(nbar) * gridDim.x,
                            tp ? x_base + nx + 1 : 0, tp ? nx + 1 : 0))
     flag_error(st, kErrPipelineTimeout);

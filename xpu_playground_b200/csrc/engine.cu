@@ -341,8 +341,7 @@ class Qwen3Engine {
         peer_regions_.push_back(ptr);
         base = static_cast<uint8_t *>(ptr);
       }
-      links.part[q] = reinterpret_cast<float *>(base);
-      links.flag[q] = reinterpret_cast<unsigned long long *>(base + tp_region_flag_offset(H));
+      links.part[q] = reinterpret_cast<unsigned long long *>(base);
       links.lm[q] = reinterpret_cast<LmSlot *>(base + tp_region_lm_offset(H));
     }
     b_.tp = links;

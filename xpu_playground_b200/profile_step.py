@@ -9,7 +9,8 @@ and runs `--warm` + 1 decode steps, so that the step to capture under
 `ncu --clock-control none -k regex:k_step -s <warm> -c 1` is the last one. Weight initialisation
 launches one fill kernel per tensor before that.
 
-Under torchrun the ranks run one tensor-parallel engine and rank 0 reports:
+Under torchrun the ranks run one tensor-parallel engine and rank 0 prints
+every rank's report:
 
     python -m torch.distributed.run --nproc-per-node 8 --master-addr 127.0.0.1 \
         -m xpu_playground_b200.profile_step --preset qwen3-8b --trace
@@ -61,7 +62,6 @@ def main() -> None:
     if args.trace:
         os.environ["XPU_STEP_TRACE"] = "1"
 
-    from . import _lib
     from .qwen3 import Qwen3Engine
     from .qwen3_config import PRESETS
 
@@ -84,43 +84,90 @@ def main() -> None:
     eng.enqueue_steps(args.warm + 1)
     eng.synchronize()
     tok, pos, err = eng.state()
+    report = [f"{args.preset}: position {pos}, last token {tok}, error {err}, tp {world}, rank {rank}, "
+              f"kernels/step {eng.info().kernels_per_step}, fill launches {len(shape.tensor_names())}"]
+    stamps = None
+    if args.trace:
+        report += trace_table(eng, shape.layers)
+        stamps = trace_stamps(eng, shape.layers)
     if world > 1:
+        # every rank's table, printed by rank 0 in rank order
+        reports = [None] * world
+        dist.all_gather_object(reports, report)
+        every = [None] * world
+        dist.all_gather_object(every, stamps)
         dist.barrier()
-        if rank != 0:
-            dist.barrier()
-            eng.close()
-            dist.destroy_process_group()
-            return
-    print(f"{args.preset}: position {pos}, last token {tok}, error {err}, tp {world}, "
-          f"kernels/step {eng.info().kernels_per_step}, fill launches {len(shape.tensor_names())}")
-    if not args.trace:
-        if world > 1:
-            dist.barrier()
-            dist.destroy_process_group()
-        return
+        eng.close()
+        dist.destroy_process_group()
+    else:
+        reports, every = [report], [stamps]
+        eng.close()
+    if rank == 0:
+        for r in reports:
+            print("\n".join(r))
+        if args.trace and world > 1:
+            print("\n".join(exchange_skew(every, shape.layers)))
+
+
+def trace_stamps(eng, L: int) -> np.ndarray:
+    """Raw globaltimer stamps of the last step, [cta][event] (ns)."""
+    from . import _lib
     n = ctypes.c_uint32()
     _lib.check(eng.lib.xpu_qwen3_trace(eng._h, None, 0, ctypes.byref(n)))
     buf = np.zeros(n.value, np.uint64)
     _lib.check(eng.lib.xpu_qwen3_trace(eng._h, buf.ctypes.data, n.value, ctypes.byref(n)))
-    L = shape.layers
+    return buf.reshape(-1, 1 + 24 * L + 2).astype(np.int64)
+
+
+def exchange_skew(every: list, L: int) -> list[str]:
+    """Cross-rank view of the two exchanges per layer (globaltimer stamps of
+    different GPUs compared directly, so rank clock offsets show up too):
+    per exchange, the spread over ranks of the time the rank's last CTA
+    finished its partial stores, and how long after the last rank's last
+    store each rank's CTAs finished staging (first / last CTA)."""
+    out = ["exchange skew (us, mean over layers): stores-done spread over ranks | staging done after the last "
+           "rank's last store, first CTA / last CTA per rank"]
+    # o_proj: phase 3 items end = event 1+24l+4*3+1; its staging ends at gate_up stage = 1+24l+4*4+0
+    # down:   phase 5 items end = 1+24l+4*5+1; staging ends at next qkv stage = 1+24(l+1)+0 (last layer: skip)
+    for name, ph, nxt in (("o_proj", 3, lambda l: 1 + 24 * l + 16), ("down", 5, lambda l: 1 + 24 * (l + 1))):
+        spread, first_after, last_after = [], [], []
+        for l in range(L - 1):
+            e_items = 1 + 24 * l + 4 * ph + 1
+            done = np.array([t[:, e_items].max() for t in every])
+            ready_first = np.array([t[:, nxt(l)].min() for t in every])
+            ready_last = np.array([t[:, nxt(l)].max() for t in every])
+            spread.append(done.max() - done.min())
+            first_after.append(ready_first - done.max())
+            last_after.append(ready_last - done.max())
+        fa, la = np.mean(first_after, axis=0) / 1e3, np.mean(last_after, axis=0) / 1e3
+        out.append(f"{name:7s} spread {np.mean(spread) / 1e3:6.2f} | " +
+                   "  ".join(f"r{r} {fa[r]:5.2f}/{la[r]:5.2f}" for r in range(len(every))))
+    return out
+
+
+def trace_table(eng, L: int) -> list[str]:
+    """Per phase of the last persistent step: mean/max over CTAs (averaged
+    over layers) of staging, items, finishing and barrier time."""
+    from . import _lib
+    n = ctypes.c_uint32()
+    _lib.check(eng.lib.xpu_qwen3_trace(eng._h, None, 0, ctypes.byref(n)))
+    buf = np.zeros(n.value, np.uint64)
+    _lib.check(eng.lib.xpu_qwen3_trace(eng._h, buf.ctypes.data, n.value, ctypes.byref(n)))
     events = 1 + 24 * L + 2
     t = buf.reshape(-1, events).astype(np.int64)
     t -= t[:, 0].min()
-    print(f"step span {t[:, -1].max() / 1e3:.1f} us over {t.shape[0]} CTAs; "
-          f"per layer {(t[:, 1 + 24 * L] - t[:, 1]).max() / L / 1e3:.1f} us")
+    out = [f"step span {t[:, -1].max() / 1e3:.1f} us over {t.shape[0]} CTAs; "
+           f"per layer {(t[:, 1 + 24 * L] - t[:, 1]).max() / L / 1e3:.1f} us"]
     for ph in range(6):
         cells = []
         for k in range(4):
             e = np.array([1 + 24 * l + 4 * ph + k for l in range(L)])
             dur = t[:, e] - t[:, e - 1]
             cells.append(f"{PARTS[k]} {dur.mean() / 1e3:6.2f}/{dur.max(axis=0).mean() / 1e3:6.2f}")
-        print(f"{PHASES[ph]:8s} " + "  ".join(cells))
+        out.append(f"{PHASES[ph]:8s} " + "  ".join(cells))
     lm = t[:, -1] - t[:, -3]
-    print(f"lm_head  total {lm.mean() / 1e3:.1f}/{lm.max() / 1e3:.1f} us (mean/max over CTAs)")
-    if world > 1:
-        dist.barrier()
-        eng.close()
-        dist.destroy_process_group()
+    out.append(f"lm_head  total {lm.mean() / 1e3:.1f}/{lm.max() / 1e3:.1f} us (mean/max over CTAs)")
+    return out
 
 
 def batch_profile(args) -> None:
