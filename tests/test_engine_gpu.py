@@ -107,8 +107,10 @@ def test_set_tensor_equals_init_synthetic():
 # accumulation in another order) differs from transformers itself on the
 # 0.6B fixture by full-logit max-abs 0.055 and mean-abs 0.0098, top-64
 # max-abs 0.047: the noise floor between two correct implementations of a
-# deep bf16 model. The engine must stay within 1.5x of it.
-FULL_MAXABS, FULL_MEANABS, TOP_MAXABS = 0.08, 0.015, 0.07
+# deep bf16 model. The engine measures 0.0547 / 0.0094 / 0.047 against the
+# fixture on B200 (and 0.059 / 0.0095 / 0.047 against the C restatement
+# over 256 steps): it is held to the floor plus ~10%.
+FULL_MAXABS, FULL_MEANABS, TOP_MAXABS = 0.06, 0.0105, 0.052
 
 
 @pytest.mark.parametrize("fixture", ["hf_tiny.npz", "hf_tiny-tied.npz", "hf_qwen3-0p6b.npz",
