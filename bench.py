@@ -429,13 +429,23 @@ def run_ours(args) -> None:
     prompt = seeded_prompt(args.context, shape.vocab)
     prefill_info = None
     if world == 1:
+        # The prompt through both prefill paths (each synchronous, host wall
+        # clock): dense (every position through each layer together, tcgen05
+        # GEMMs against the stored weights) after one untimed warm-up call,
+        # and chunked (16 positions per batched step).
         eng.synchronize()
+        eng.prefill_dense(prompt)
         t_pre = time.perf_counter()
-        eng.prefill(prompt)  # chunked prefill: 16 positions per batched tcgen05 step (synchronous)
-        t_pre = time.perf_counter() - t_pre
-        prefill_info = {"tokens": args.context, "seconds": round(t_pre, 4),
-                        "tok_s": round(args.context / t_pre, 1), "positions_per_step": 16,
-                        "timing": "host wall clock around xpu_qwen3_prefill (synchronous)"}
+        eng.prefill_dense(prompt)
+        t_dense = time.perf_counter() - t_pre
+        t_pre = time.perf_counter()
+        eng.prefill(prompt)
+        t_chunk = time.perf_counter() - t_pre
+        prefill_info = {"tokens": args.context, "seconds": round(t_dense, 4),
+                        "tok_s": round(args.context / t_dense, 1), "path": "xpu_qwen3_prefill_dense",
+                        "chunked": {"seconds": round(t_chunk, 4), "tok_s": round(args.context / t_chunk, 1),
+                                    "positions_per_step": 16, "path": "xpu_qwen3_prefill"},
+                        "timing": "host wall clock around each synchronous call"}
     # The decode that is timed and checked follows the same prefill at every
     # N (the prompt token by token through the decode step, device-resident),
     # so its greedy tokens can be compared across GPU counts bit for bit.

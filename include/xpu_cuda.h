@@ -59,6 +59,12 @@ int xpu_gemv(int dtype, const void *matrix, const void *vector, void *output, ui
  */
 int xpu_gemm(int dtype, const void *a, const void *b, void *c, uint32_t m, uint32_t n, uint32_t k,
              void *stream);
+/* C[m,n] = A[m,k] . W^T with W row-major [n,k] (the layout of a Linear
+ * weight), FP32 accumulation, on the same tcgen05 kernel as xpu_gemm with the
+ * second operand read K-major. No counterpart in the reference (its gemm
+ * takes B as [k,n]); the dense prefill's projections use it. n and k
+ * multiples of 8, operands 16-byte aligned. */
+int xpu_gemm_bt(int dtype, const void *a, const void *w, void *c, uint32_t m, uint32_t n, uint32_t k, void *stream);
 
 /* Sticky device-side error word of this library's asynchronous kernels,
  * read and cleared (synchronises the device). Bit 0: a GEMM pipeline wait
@@ -325,6 +331,16 @@ uint64_t xpu_qwen3_bytes_per_token(xpu_qwen3_engine *engine, uint32_t context);
  * so xpu_qwen3_enqueue_steps / xpu_qwen3_decode carry on from there. One
  * GPU only. */
 int xpu_qwen3_prefill(xpu_qwen3_engine *engine, const uint32_t *prompt, uint32_t prompt_len, uint32_t *next_token);
+/* Dense prefill of the batch-1 sequence (no counterpart in the reference,
+ * which feeds the prompt token by token, qwen3/main.cpp:343-344): every
+ * prompt position goes through each layer together - the projections as
+ * tcgen05 GEMMs over all positions against the stored weights (compute-bound),
+ * causal attention over the cache - in segments of up to 2048 positions.
+ * Same result contract as xpu_qwen3_prefill (greedy token after the prompt
+ * returned, engine left at position prompt_len), with the last position's
+ * logits in xpu_qwen3_logits. One GPU (tp_size 1). */
+int xpu_qwen3_prefill_dense(xpu_qwen3_engine *engine, const uint32_t *prompt, uint32_t prompt_len,
+                            uint32_t *next_token);
 int xpu_qwen3_create_batched(const xpu_qwen3_shape *shape, uint32_t maximum_sequence, int device,
                              uint32_t max_batch, xpu_qwen3_engine **out);
 int xpu_qwen3_batch_decode(xpu_qwen3_engine *engine, uint32_t batch, const uint32_t *tokens,

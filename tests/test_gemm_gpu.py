@@ -105,3 +105,23 @@ def test_gemm_rejects_bad_arguments():
         call("xpu_gemm", 0, a.data_ptr(), a.data_ptr(), a.data_ptr(), 0, 8, 8, None)
     with pytest.raises(XpuError):
         call("xpu_gemm", 7, a.data_ptr(), a.data_ptr(), a.data_ptr(), 8, 8, 8, None)
+
+
+@pytest.mark.parametrize("fp16", [False, True], ids=["bf16", "fp16"])
+@pytest.mark.parametrize("m,n,k", [(256, 256, 128), (300, 512, 4096), (2048, 6144, 4096), (37, 24576, 1024),
+                                   (5, 128, 264)])
+def test_gemm_bt_against_fp32(fp16, m, n, k):
+    """C = A . W^T with W stored [n, k] (xpu_gemm_bt, the dense prefill's
+    projection): 1e-2 relative Frobenius of the FP32 product, every element
+    within one 16-bit rounding plus the accumulation-order allowance."""
+    dt = torch.float16 if fp16 else torch.bfloat16
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
+    A = torch.empty(m, k, device="cuda").uniform_(-1, 1, generator=g).to(dt)
+    W = torch.empty(n, k, device="cuda").uniform_(-1, 1, generator=g).to(dt)
+    C = kernels.gemm_bt(A, W)
+    ref = A.float() @ W.float().t()
+    got = C.float()
+    assert (torch.linalg.norm(got - ref) / torch.linalg.norm(ref)).item() < 1e-2
+    step = 2.0 ** -10 if fp16 else 2.0 ** -7
+    assert torch.all((got - ref).abs() <= ref.abs() * step + 1e-5 * k + 1e-6).item()
+    assert kernels.device_status() == 0

@@ -54,6 +54,7 @@ SIGNATURES: dict[str, tuple] = {
     "xpu_abi_version": (i32, []),
     "xpu_gemv": (i32, [i32, vp, vp, vp, u32, u32, vp]),
     "xpu_gemm": (i32, [i32, vp, vp, vp, u32, u32, u32, vp]),
+    "xpu_gemm_bt": (i32, [i32, vp, vp, vp, u32, u32, u32, vp]),
     "xpu_device_status": (i32, [ctypes.POINTER(u32)]),
     "xpu_peak_mem_fill": (i32, [vp, u64, vp]),
     "xpu_peak_mem_read": (i32, [vp, vp, u32, vp]),
@@ -93,6 +94,7 @@ SIGNATURES: dict[str, tuple] = {
     "xpu_qwen3_bytes_per_token": (u64, [vp, u32]),
     "xpu_qwen3_create_batched": (i32, [vp, u32, i32, u32, vp]),
     "xpu_qwen3_prefill": (i32, [vp, vp, u32, vp]),
+    "xpu_qwen3_prefill_dense": (i32, [vp, vp, u32, vp]),
     "xpu_qwen3_batch_decode": (i32, [vp, u32, vp, vp, vp]),
     "xpu_qwen3_batch_generate": (i32, [vp, u32, vp, vp, u32, i32, vp, vp]),
     "xpu_qwen3_batch_set_state": (i32, [vp, u32, vp, vp]),

@@ -82,6 +82,18 @@ int xpu_gemm(int dtype, const void *a, const void *b, void *c, uint32_t m, uint3
   })
 }
 
+int xpu_gemm_bt(int dtype, const void *a, const void *w, void *c, uint32_t m, uint32_t n, uint32_t k, void *stream) {
+  XPU_GUARD({
+    XPU_REQUIRE(a && w && c, "xpu_gemm_bt: null pointer");
+    XPU_REQUIRE(m > 0 && n > 0 && k > 0, "xpu_gemm_bt: m, n and k must be positive");
+    XPU_REQUIRE(n % 8 == 0 && k % 8 == 0, "xpu_gemm_bt: n and k must be multiples of 8");
+    XPU_REQUIRE(aligned16(a) && aligned16(w) && aligned16(c), "xpu_gemm_bt: operands must be 16-byte aligned");
+    if (dtype != XPU_BF16 && dtype != XPU_FP16)
+      return fail(XPU_ERR_INVALID, "xpu_gemm_bt: dtype must be XPU_BF16 or XPU_FP16");
+    return cuda_status(gemm_launch_ex(dtype == XPU_FP16, true, a, w, c, m, n, k, as_stream(stream)), "xpu_gemm_bt");
+  })
+}
+
 int xpu_device_status(uint32_t *flags) {
   XPU_GUARD({
     XPU_REQUIRE(flags, "xpu_device_status: null pointer");

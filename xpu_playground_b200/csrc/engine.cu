@@ -579,6 +579,75 @@ class Qwen3Engine {
     return tail.next;
   }
 
+  // Dense prefill (compute-bound): the prompt's positions go through each
+  // layer together, in segments of up to kPrefillSegment positions, the
+  // projections as tcgen05 GEMMs against the stored weights (prefill.cu);
+  // then the lm_head GEMV and argmax of the last position. Leaves the engine
+  // at position n with the greedy token after the prompt, which is returned,
+  // and the last position's logits in logits() (single GPU).
+  static constexpr uint32_t kPrefillSegment = 2048;
+
+  uint32_t dense_prefill(const uint32_t *prompt, uint32_t n) {
+    if (tp_ > 1) throw InvalidArg("dense prefill runs on one GPU (tp_size 1)");
+    if (n == 0) throw InvalidArg("at least one prompt token is required");
+    if (n > max_seq_) throw InvalidArg("prompt exceeds the maximum sequence");
+    for (uint32_t i = 0; i < n; ++i)
+      if (prompt[i] >= shape_.vocab_size) throw InvalidArg("prompt token id outside the vocabulary");
+    if (!loaded_) throw InvalidArg("no weights: call init_synthetic, load a checkpoint or set every tensor");
+    CK(cudaSetDevice(device_));
+    const uint32_t H = d_.H, I = d_.I_l, QH = d_.QH_l, KVH = d_.KVH_l, R = (QH + 2 * KVH) * kHD;
+    const uint32_t cap = std::min(max_seq_, kPrefillSegment);
+    if (!pf_x_) {
+      pf_x_ = dev_alloc<uint16_t>(static_cast<uint64_t>(cap) * H);
+      pf_xn_ = dev_alloc<uint16_t>(static_cast<uint64_t>(cap) * std::max(H, I));
+      pf_big_ = dev_alloc<uint16_t>(static_cast<uint64_t>(cap) * std::max(R, 2 * I));
+      pf_q_ = dev_alloc<uint16_t>(static_cast<uint64_t>(cap) * QH * kHD);
+      pf_att_ = dev_alloc<uint16_t>(static_cast<uint64_t>(cap) * QH * kHD);
+      pf_o_ = dev_alloc<uint16_t>(static_cast<uint64_t>(cap) * H);
+      pf_tok_ = dev_alloc<uint32_t>(cap + 1);
+    }
+    const float eps = d_.eps;
+    cudaStream_t s = stream_;
+    for (uint32_t p0 = 0; p0 < n; p0 += cap) {
+      const uint32_t M = std::min(cap, n - p0);
+      CK(cudaMemcpyAsync(pf_tok_, prompt + p0, M * sizeof(uint32_t), cudaMemcpyHostToDevice, s));
+      CK(prefill_embed(embed_, pf_tok_, pf_x_, M, H, s));
+      CK(prefill_rms(pf_x_, layers_[0].in_norm, pf_xn_, M, H, eps, s));
+      for (size_t l = 0; l < layers_.size(); ++l) {
+        const Layer &L = layers_[l];
+        CK(gemm_launch_ex(false, true, pf_xn_, L.wqkv, pf_big_, M, R, H, s));
+        CK(prefill_heads(pf_big_, L.q_norm, L.k_norm, cos_, sin_, pf_q_, L.kcache, L.vcache, p0, M, QH, KVH, eps, s));
+        CK(prefill_attention(pf_q_, L.kcache, L.vcache, pf_att_, p0, M, QH, KVH, s, pf_tc_));
+        CK(gemm_launch_ex(false, true, pf_att_, L.wo, pf_o_, M, H, QH * kHD, s));
+        CK(prefill_add_rms(pf_x_, pf_o_, L.post_norm, pf_xn_, M, H, eps, s));
+        CK(gemm_launch_ex(false, true, pf_xn_, L.wgu, pf_big_, M, 2 * I, H, s));
+        CK(prefill_swiglu(pf_big_, pf_xn_, M, I, s));  // h into the (wider) xn buffer
+        CK(gemm_launch_ex(false, true, pf_xn_, L.wd, pf_o_, M, H, I, s));
+        const uint16_t *next_norm = l + 1 < layers_.size() ? layers_[l + 1].in_norm : final_norm_;
+        CK(prefill_add_rms(pf_x_, pf_o_, next_norm, pf_xn_, M, H, eps, s));
+      }
+      if (p0 + M == n) {
+        const uint16_t *last = pf_xn_ + static_cast<uint64_t>(M - 1) * H;
+        CK(gemv_launch(reinterpret_cast<const __nv_bfloat16 *>(lm_head_), reinterpret_cast<const __nv_bfloat16 *>(last),
+                       reinterpret_cast<__nv_bfloat16 *>(logits_), d_.V_l, H, s));
+        CK(qwen_argmax_launch(logits_, pf_tok_ + cap, d_.V_l, s));
+      }
+    }
+    uint32_t next = 0;
+    CK(cudaMemcpyAsync(&next, pf_tok_ + cap, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    if (take_device_error()) throw InvalidArg("a prefill GEMM pipeline timed out");
+    if (next == 0xffffffffu) throw InvalidArg("prefill met a NaN/Inf logit");
+    *host_state_ = DecodeState{};
+    host_state_->token = next;
+    host_state_->next = next;
+    host_state_->position = n;
+    write_state();
+    CK(cudaMemcpyAsync(log_ + (n - 1), &next, sizeof(uint32_t), cudaMemcpyHostToDevice, s));
+    CK(cudaStreamSynchronize(s));
+    return next;
+  }
+
   // Set sequences 0..n-1 (token, position) without running; enqueue_steps
   // then advances them device-resident.
   void batch_set_state(uint32_t n, const uint32_t *tokens, const uint32_t *positions) {
@@ -1098,6 +1167,11 @@ class Qwen3Engine {
   SeqState *host_seq_ = nullptr;
   uint32_t *host_berr_ = nullptr;
   unsigned long long *btrace_ = nullptr;  // batched step trace (XPU_BATCH_TRACE=1)
+  // dense prefill buffers (one segment of up to kPrefillSegment positions)
+  uint16_t *pf_x_ = nullptr, *pf_xn_ = nullptr, *pf_big_ = nullptr, *pf_q_ = nullptr, *pf_att_ = nullptr,
+           *pf_o_ = nullptr;
+  uint32_t *pf_tok_ = nullptr;
+  bool pf_tc_ = getenv("XPU_PF_CUDA_CORE") == nullptr;  // experiment switch (attention products)
   std::map<uint32_t, cudaGraphExec_t> prefill_exec_;  // chunked-prefill graphs by chunk size
   SeqState *host_prefill_ = nullptr;                 // pinned per-chunk step states
   uint32_t prefill_cap_ = 0;
@@ -1238,6 +1312,14 @@ int xpu_qwen3_get_state(xpu_qwen3_engine *engine, uint32_t *token, uint32_t *pos
 
 int xpu_qwen3_enqueue_steps(xpu_qwen3_engine *engine, uint32_t steps, void *stream) {
   return guarded([&] { eng(engine).enqueue_steps(steps, static_cast<cudaStream_t>(stream)); });
+}
+
+int xpu_qwen3_prefill_dense(xpu_qwen3_engine *engine, const uint32_t *prompt, uint32_t prompt_len,
+                            uint32_t *next_token) {
+  return guarded([&] {
+    if (!prompt || !next_token) throw xpu::InvalidArg("xpu_qwen3_prefill_dense: null pointer");
+    *next_token = eng(engine).dense_prefill(prompt, prompt_len);
+  });
 }
 
 int xpu_qwen3_token_log(xpu_qwen3_engine *engine, uint32_t first_position, uint32_t count, uint32_t *host_out) {

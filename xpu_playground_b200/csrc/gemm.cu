@@ -24,8 +24,10 @@
 //              rounds to bf16/fp16 and stores with row/column predication,
 //              then frees the accumulator buffer for the tile after next.
 // A is K-major (row-major [M,K]); B is used MN-major straight from its
-// row-major [K,N] layout (instruction descriptor b_major = MN), so neither
-// operand is transposed or padded in memory: TMA zero-fills out-of-range
+// row-major [K,N] layout (instruction descriptor b_major = MN) - or, for
+// C = A . W^T with W row-major [N,K] (prefill projections against the
+// stored weights), K-major like A - so neither operand is transposed or
+// padded in memory: TMA zero-fills out-of-range
 // rows/columns/K and the epilogue masks the edge tiles. No load uses
 // multicast; the even CTA signals the odd CTA's barriers by their cluster
 // addresses.
@@ -65,13 +67,14 @@ constexpr int kEpilogueWarps = 8;
 constexpr int kGemmThreads = 64 + 32 * kEpilogueWarps;
 constexpr unsigned kErrGemmTimeout = 1u;
 
-// Instruction descriptor, kind::f16: FP32 accumulator, A K-major, B MN-major.
-__host__ __device__ constexpr uint32_t instr_desc(bool fp16, uint32_t m, uint32_t n) {
+// Instruction descriptor, kind::f16: FP32 accumulator, A K-major, B MN-major
+// (row-major [K,N]) or, with b_kmajor, K-major (row-major [N,K]: C = A . B^T).
+__host__ __device__ constexpr uint32_t instr_desc(bool fp16, uint32_t m, uint32_t n, bool b_kmajor = false) {
   return (1u << 4) |                          // D format F32
          ((fp16 ? 0u : 1u) << 7) |            // A format: F16 = 0, BF16 = 1
          ((fp16 ? 0u : 1u) << 10) |           // B format
          (0u << 15) |                         // A K-major
-         (1u << 16) |                         // B MN-major
+         ((b_kmajor ? 0u : 1u) << 16) |       // B MN-major (1) or K-major (0)
          ((n >> 3) << 17) |                   // N / 8
          ((m >> 4) << 24);                    // M / 16
 }
@@ -139,7 +142,9 @@ __device__ __forceinline__ TileCoord tile_coord(uint32_t t, uint32_t tiles_m, ui
   return {first + local % rows, local / rows};
 }
 
-template <bool FP16>
+// BK: B is K-major (W[N,K] row-major, C = A . W^T); its per-CTA half of the
+// tile (128 N rows x 128 K) is staged exactly like A's (two 128 x 64 boxes).
+template <bool FP16, bool BK>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, uint16_t *C,
           uint32_t M, uint32_t N, uint32_t K) {
@@ -196,14 +201,19 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
           const int32_t xk = static_cast<int32_t>(k * kBK);
           tma_load_pair(st, &map_a, xk, ya, bar);
           tma_load_pair(st + kABoxBytes, &map_a, xk + static_cast<int32_t>(kSwz), ya, bar);
-          tma_load_pair(st + kABytes, &map_b, xb, xk, bar);
-          tma_load_pair(st + kABytes + kBBoxBytes, &map_b, xb + static_cast<int32_t>(kSwz), xk, bar);
+          if (BK) {
+            tma_load_pair(st + kABytes, &map_b, xk, xb, bar);
+            tma_load_pair(st + kABytes + kABoxBytes, &map_b, xk + static_cast<int32_t>(kSwz), xb, bar);
+          } else {
+            tma_load_pair(st + kABytes, &map_b, xb, xk, bar);
+            tma_load_pair(st + kABytes + kBBoxBytes, &map_b, xb + static_cast<int32_t>(kSwz), xk, bar);
+          }
         }
       }
     }
   } else if (warp == 1) {
     if (rank == 0 && lane == 0) {
-      const uint32_t idesc = instr_desc(FP16, kBM, kBN);
+      const uint32_t idesc = instr_desc(FP16, kBM, kBN, BK);
       uint32_t g = 0, i = 0;
       for (uint32_t t = pair; t < tiles && !has_failed(&failed); t += pairs, ++i) {
         const uint32_t b = i & 1, use_b = i >> 1;
@@ -215,13 +225,15 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
           if (!mbar_wait(&full[s], use & 1)) { failed = 1; break; }
           tc_fence_after();
           const uint32_t sa = smem_addr(ring + s * kStageBytes), sb = sa + kABytes;
-          const uint64_t da = smem_desc(sa, 16, 1024), db = smem_desc(sb, kBBoxBytes, 1024);
+          const uint64_t da = smem_desc(sa, 16, 1024), db = BK ? smem_desc(sb, 16, 1024) : smem_desc(sb, kBBoxBytes, 1024);
 #pragma unroll
           for (uint32_t kk = 0; kk < kBK / 16; ++kk) {
             // K step of 16: +32 bytes inside A's 128-byte swizzled rows (the
-            // next A box every 4 steps), +2 eight-row groups of B.
+            // next A box every 4 steps); B the same when K-major, else +2
+            // eight-row groups of its MN-major boxes.
             const uint32_t a_off = (kk / 4) * kABoxBytes + (kk % 4) * 32u;
-            mma_pair(d, da + (a_off >> 4), db + ((kk * 2048u) >> 4), idesc, (k | kk) != 0);
+            const uint32_t b_off = BK ? a_off : kk * 2048u;
+            mma_pair(d, da + (a_off >> 4), db + (b_off >> 4), idesc, (k | kk) != 0);
           }
           mma_commit_pair(cluster_addr(&empty[s], 0));
           mma_commit_pair(cluster_addr(&empty[s], 1));
@@ -313,8 +325,14 @@ size_t gemm_smem_bytes() { return kStages * kStageBytes + 1024; }
 
 cudaError_t gemm_launch(bool fp16, const void *A, const void *B, void *C, uint32_t M, uint32_t N, uint32_t K,
                         cudaStream_t stream) {
+  return gemm_launch_ex(fp16, false, A, B, C, M, N, K, stream);
+}
+
+cudaError_t gemm_launch_ex(bool fp16, bool b_kmajor, const void *A, const void *B, void *C, uint32_t M, uint32_t N,
+                           uint32_t K, cudaStream_t stream) {
   const bool tma_ok = (K % 8 == 0) && (N % 8 == 0) && aligned16(A) && aligned16(B) && aligned16(C);
   if (!tma_ok) {
+    if (b_kmajor) return cudaErrorInvalidValue;  // the A . B^T form needs the TMA path
     const dim3 grid((N + 31) / 32, (M + 31) / 32);
     if (fp16)
       k_gemm_simple<__half><<<grid, 256, 0, stream>>>(static_cast<const __half *>(A), static_cast<const __half *>(B),
@@ -328,10 +346,12 @@ cudaError_t gemm_launch(bool fp16, const void *A, const void *B, void *C, uint32
   CUtensorMap map_a, map_b;
   cudaError_t e = make_tmap_2d_u16_swizzled(&map_a, A, K, M, K, kSwz, kHalfM);
   if (e != cudaSuccess) return e;
-  e = make_tmap_2d_u16_swizzled(&map_b, B, N, K, N, kSwz, kBK);
+  e = b_kmajor ? make_tmap_2d_u16_swizzled(&map_b, B, K, N, K, kSwz, kHalfN)
+               : make_tmap_2d_u16_swizzled(&map_b, B, N, K, N, kSwz, kBK);
   if (e != cudaSuccess) return e;
   const size_t smem = gemm_smem_bytes();
-  auto kernel = fp16 ? k_gemm_tc<true> : k_gemm_tc<false>;
+  auto kernel = fp16 ? (b_kmajor ? k_gemm_tc<true, true> : k_gemm_tc<true, false>)
+                     : (b_kmajor ? k_gemm_tc<false, true> : k_gemm_tc<false, false>);
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
 
@@ -352,11 +372,11 @@ cudaError_t gemm_launch(bool fp16, const void *A, const void *B, void *C, uint32
   e = cudaGetDevice(&device);
   if (e != cudaSuccess) return e;
   static std::mutex cache_mutex;
-  static int resident_pairs[2][64] = {};
+  static int resident_pairs[4][64] = {};
   int pairs = 0;
   {
     std::lock_guard<std::mutex> lock(cache_mutex);
-    int &cached = resident_pairs[fp16 ? 1 : 0][device & 63];
+    int &cached = resident_pairs[(fp16 ? 1 : 0) + (b_kmajor ? 2 : 0)][device & 63];
     if (cached == 0) {
       cfg.gridDim = dim3(2);
       e = cudaOccupancyMaxActiveClusters(&cached, kernel, &cfg);

@@ -46,6 +46,18 @@ def gemv(matrix: torch.Tensor, vector: torch.Tensor, out: torch.Tensor | None = 
     return out
 
 
+def gemm_bt(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """C[m,n] = A[m,k] . W^T for W [n,k] (row-major, contiguous, bf16 or fp16)."""
+    m, k = a.shape
+    n, k2 = w.shape
+    if k2 != k or a.dtype != w.dtype:
+        raise ValueError("gemm_bt: A is [m,k] and W is [n,k] of the same dtype")
+    if out is None:
+        out = torch.empty(m, n, dtype=a.dtype, device=a.device)
+    call("xpu_gemm_bt", _dtype_code(a), _ptr(a), _ptr(w), _ptr(out), m, n, k, _stream(stream))
+    return out
+
+
 def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
          stream=None) -> torch.Tensor:
     """C[m,n] = A[m,k] . B[k,n] (row-major, contiguous, bf16 or fp16)."""

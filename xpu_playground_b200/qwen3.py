@@ -194,6 +194,16 @@ class Qwen3Engine:
         _lib.check(self.lib.xpu_qwen3_prefill(self._h, p.ctypes.data, p.size, ctypes.byref(out)))
         return out.value
 
+    def prefill_dense(self, prompt: list[int]) -> int:
+        """Dense prefill (every position through each layer together, tcgen05
+        GEMMs; xpu_qwen3_prefill_dense): returns the greedy token after the
+        prompt, leaves the state at position len(prompt) and the last
+        position's logits in logits()."""
+        p = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = ctypes.c_uint32()
+        _lib.check(self.lib.xpu_qwen3_prefill_dense(self._h, p.ctypes.data, p.size, ctypes.byref(out)))
+        return out.value
+
     # ----------------------------------------------------- batched decode ----
     def batch_decode(self, tokens: list[int], positions: list[int]) -> list[int]:
         """One step of len(tokens) sequences (xpu_qwen3_batch_decode)."""
