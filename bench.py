@@ -373,6 +373,7 @@ def decode_config(args, shape) -> dict:
 
 WEIGHT_SEED = 2026
 GOLDEN_TOKENS = ROOT / "tests" / "golden" / "decode_tokens_qwen3-8b.json"
+PREFILL_PATH = "xpu_qwen3_prefill_dense"  # the prefill the checked decode continues from
 
 
 def token_digest(ids: list[int]) -> str:
@@ -394,7 +395,8 @@ def check_tokens(args, first: int, ids: list[int]) -> dict:
         info["golden"] = None
         return info
     same_run = (gold.get("preset") == args.preset and gold.get("context") == args.context and
-                gold.get("weight_seed") == WEIGHT_SEED and gold.get("first_position") == first)
+                gold.get("weight_seed") == WEIGHT_SEED and gold.get("first_position") == first and
+                gold.get("prefill") == PREFILL_PATH)
     if not same_run:
         info["golden"] = None
         return info
@@ -427,29 +429,40 @@ def run_ours(args) -> None:
     if world > 1:
         eng.connect_tensor_parallel(dist.new_group(backend="gloo"))
     prompt = seeded_prompt(args.context, shape.vocab)
-    prefill_info = None
+    chunked = None
     if world == 1:
-        # The prompt through both prefill paths (each synchronous, host wall
-        # clock): dense (every position through each layer together, tcgen05
-        # GEMMs against the stored weights) after one untimed warm-up call,
-        # and chunked (16 positions per batched step).
+        # The 16-positions-per-step chunked prefill, for comparison (one GPU;
+        # synchronous, host wall clock); the dense prefill below replaces its
+        # KV cache.
         eng.synchronize()
-        eng.prefill_dense(prompt)
-        t_pre = time.perf_counter()
-        eng.prefill_dense(prompt)
-        t_dense = time.perf_counter() - t_pre
         t_pre = time.perf_counter()
         eng.prefill(prompt)
         t_chunk = time.perf_counter() - t_pre
-        prefill_info = {"tokens": args.context, "seconds": round(t_dense, 4),
-                        "tok_s": round(args.context / t_dense, 1), "path": "xpu_qwen3_prefill_dense",
-                        "chunked": {"seconds": round(t_chunk, 4), "tok_s": round(args.context / t_chunk, 1),
-                                    "positions_per_step": 16, "path": "xpu_qwen3_prefill"},
-                        "timing": "host wall clock around each synchronous call"}
-    # The decode that is timed and checked follows the same prefill at every
-    # N (the prompt token by token through the decode step, device-resident),
-    # so its greedy tokens can be compared across GPU counts bit for bit.
-    eng.generate(prompt, 1)
+        chunked = {"seconds": round(t_chunk, 4), "tok_s": round(args.context / t_chunk, 1),
+                   "positions_per_step": 16, "path": "xpu_qwen3_prefill"}
+    # Dense prefill at every N (every position through each layer together,
+    # tcgen05 GEMMs against the stored weights; under tensor parallelism the
+    # row-parallel sums cross NVLink): one untimed call, then the timed one,
+    # host wall clock around the synchronous call, max over ranks. The timed
+    # decode continues from its KV cache, and the dense prefill computes the
+    # same bits at every tensor-parallel size, so the greedy tokens compared
+    # across GPU counts cover prefill and decode.
+    eng.synchronize()
+    eng.prefill_dense(prompt)
+    if world > 1:
+        dist.barrier()
+    t_pre = time.perf_counter()
+    eng.prefill_dense(prompt)
+    t_dense = time.perf_counter() - t_pre
+    if world > 1:
+        t = torch.tensor([t_dense], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_dense = float(t.item())
+    prefill_info = {"tokens": args.context, "seconds": round(t_dense, 4), "tok_s": round(args.context / t_dense, 1),
+                    "path": PREFILL_PATH, "n_gpus": world,
+                    "timing": "host wall clock around the synchronous call (prompt upload and token read included)"}
+    if chunked:
+        prefill_info["chunked"] = chunked
     stream = torch.cuda.ExternalStream(eng.info().stream, device=device)
     eng.enqueue_steps(W)
     eng.synchronize()
@@ -497,7 +510,8 @@ def run_ours(args) -> None:
     if args.record_tokens and rank == 0:
         Path(args.record_tokens).write_text(json.dumps(
             {"preset": args.preset, "context": args.context, "weight_seed": WEIGHT_SEED,
-             "prompt": "bench.seeded_prompt(context, vocab) (numpy default_rng(7))", "n_gpus": world,
+             "prompt": "bench.seeded_prompt(context, vocab) (numpy default_rng(7))", "prefill": PREFILL_PATH,
+             "n_gpus": world,
              "first_position": first, "ids": tokens["ids"], "sha256": tokens["sha256"]}) + "\n")
 
     mid_context = (pos0 + pos1) // 2

@@ -338,7 +338,12 @@ int xpu_qwen3_prefill(xpu_qwen3_engine *engine, const uint32_t *prompt, uint32_t
  * causal attention over the cache - in segments of up to 2048 positions.
  * Same result contract as xpu_qwen3_prefill (greedy token after the prompt
  * returned, engine left at position prompt_len), with the last position's
- * logits in xpu_qwen3_logits. One GPU (tp_size 1). */
+ * logits (this rank's vocabulary shard) in xpu_qwen3_logits. Tensor parallel
+ * engines (connected with xpu_qwen3_tp_connect) call it on every rank with
+ * the same prompt; o_proj and down are summed over 8 fixed K chunks in a
+ * fixed order, so every tp_size returns the same token and logits bits and
+ * writes the same KV cache. A rank whose peers do not join within ~2 s
+ * returns XPU_ERR_TIMEOUT and the engines must be recreated. */
 int xpu_qwen3_prefill_dense(xpu_qwen3_engine *engine, const uint32_t *prompt, uint32_t prompt_len,
                             uint32_t *next_token);
 int xpu_qwen3_create_batched(const xpu_qwen3_shape *shape, uint32_t maximum_sequence, int device,

@@ -64,7 +64,8 @@ def test_token_check_against_a_stored_run(tmp_path, monkeypatch):
     ids = [5, 6, 7, 8]
     gold = tmp_path / "g.json"
     gold.write_text(json.dumps({"preset": "qwen3-8b", "context": 2048, "weight_seed": bench.WEIGHT_SEED,
-                                "first_position": 2047, "n_gpus": 1, "ids": [5, 6, 7, 8, 9, 10]}))
+                                "first_position": 2047, "prefill": bench.PREFILL_PATH, "n_gpus": 1,
+                                "ids": [5, 6, 7, 8, 9, 10]}))
     monkeypatch.setattr(bench, "GOLDEN_TOKENS", gold)
     monkeypatch.setattr(bench, "ROOT", tmp_path)
     info = bench.check_tokens(args, 2047, ids)
@@ -72,6 +73,10 @@ def test_token_check_against_a_stored_run(tmp_path, monkeypatch):
     assert info["sha256"] == bench.token_digest(ids) != bench.token_digest([5, 6, 7, 9])
     assert not bench.check_tokens(args, 2047, [5, 6, 7, 9])["golden"]["match"]
     assert bench.check_tokens(args, 100, ids)["golden"] is None  # another run: not compared
+    stale = json.loads(gold.read_text())
+    stale["prefill"] = "token by token"
+    gold.write_text(json.dumps(stale))
+    assert bench.check_tokens(args, 2047, ids)["golden"] is None  # another prefill: not compared
 
 
 def test_row_shards_cover_the_matrix_once():

@@ -1,14 +1,15 @@
 """Dense prefill (xpu_qwen3_prefill_dense: every prompt position through
 each layer together, tcgen05 GEMMs against the stored weights, causal
-attention over the cache) against the CPU oracles, under the same gates as
-the token-by-token and chunked paths:
+attention over the cache) against the CPU oracles:
 
 * the C restatement of the transformers forward: the last prompt position's
-  logits (a 50-token prompt, and one of 2100 tokens that takes two
-  segments) and the decode steps that follow;
+  logits (a 50-token prompt, one of 2100 tokens that takes two segments, and
+  the 8B layer shapes) and the decode steps that follow, under logit_gate;
 * qwen3/reference.py's model (transformers golden fixtures): the golden
   token stream's first `prefix` positions prefilled densely, the remaining
-  positions decoded teacher-forced under the fixture gates.
+  positions decoded teacher-forced under the fixture gates, with the
+  per-logit two-bf16-step rule of logit_gate applied to the top-64 and
+  full-logit checks (top_gate).
 """
 
 from pathlib import Path
@@ -18,7 +19,7 @@ import pytest
 
 from oracle import oracle as orc
 from oracle.qwen3_ref import CDecoder, prompt_ids, seeded_weights
-from tests.test_engine_gpu import (FULL_MAXABS, FULL_MEANABS, TOP_MAXABS, logit_gate, near_tie)
+from tests.test_engine_gpu import (FULL_MEANABS, TOP_MAXABS, logit_gate, near_tie)
 from xpu_playground_b200.qwen3 import Qwen3Engine
 from xpu_playground_b200.qwen3_config import PRESETS
 
@@ -27,7 +28,19 @@ GOLDEN = Path(__file__).resolve().parent / "golden"
 f = orc.bf16_to_float
 
 
-@pytest.mark.parametrize("preset,n,steps", [("tiny", 50, 64), ("tiny-tied", 50, 64), ("tiny", 2100, 2110)])
+def top_gate(ref_top):
+    """Per top-64 logit: TOP_MAXABS, or two bf16 steps of the reference value
+    where that is larger - logit_gate's rule for two correct FP32-
+    accumulating implementations. The dense GEMMs sum in another order than
+    the decode GEMVs, so K/V entries land a rounding apart; on the 8B-shaped
+    fixture a logit of 6.0 then moves by two steps (0.0625), above the
+    absolute 0.052 that the decode-only path stays under."""
+    step = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(ref_top), 1e-30))) - 7)
+    return np.maximum(TOP_MAXABS, 2 * step)
+
+
+@pytest.mark.parametrize("preset,n,steps", [("tiny", 50, 64), ("tiny-tied", 50, 64), ("tiny", 2100, 2110),
+                                            ("qwen3-8b-l2", 16, 32)])
 def test_dense_prefill_matches_c_oracle(preset, n, steps):
     shape = PRESETS[preset]
     seed = 4321
@@ -80,12 +93,15 @@ def test_dense_prefill_then_decode_matches_transformers(fixture, prefix):
         else:
             idx = fx["top_idx"][pos]
             ref_top = f(fx["top_bits"][pos]).astype(np.float64)
-            top_dev = np.abs(f(lg[idx]) - ref_top).max()
-            assert top_dev <= TOP_MAXABS, f"position {pos}: top-64 max-abs {top_dev}"
+            dev = np.abs(f(lg[idx]) - ref_top)
+            assert np.all(dev <= top_gate(ref_top)), f"position {pos}: top-64 max-abs {dev.max()}"
             if pos in full:
+                # per logit the full-logit rule of logit_gate (two bf16 steps
+                # of the reference value above 2e-2), and the mean-abs gate
+                bad, worst = logit_gate(lg, fx["logits"][full[pos]])
                 d = np.abs(f(lg).astype(np.float64) - f(fx["logits"][full[pos]]))
-                assert d.max() <= FULL_MAXABS and d.mean() <= FULL_MEANABS, \
-                    f"position {pos}: full max-abs {d.max()}, mean-abs {d.mean()}"
+                assert bad == 0 and d.mean() <= FULL_MEANABS, \
+                    f"position {pos}: {bad} logits off, max-abs {worst}, mean-abs {d.mean()}"
             if nxt != ids[pos]:
                 where = np.nonzero(idx == nxt)[0]
                 assert where.size and ref_top[0] - ref_top[where[0]] <= TOP_MAXABS, f"position {pos}"

@@ -96,6 +96,65 @@ def test_tp_matches_single_gpu(preset, world):
         assert np.array_equal(logits, ref_logits[rank * shard:(rank + 1) * shard]), f"rank {rank} logits differ"
 
 
+def _prefill_then_decode(eng, prompt, n_new):
+    """Dense prefill of the prompt, then n_new - 1 host-driven decode steps:
+    the greedy tokens, the prefill's last-position logits and the last
+    step's logits."""
+    toks = [eng.prefill_dense(prompt)]
+    first_logits = eng.logits()
+    for i in range(n_new - 1):
+        toks.append(eng.decode(toks[-1], len(prompt) + i))
+    return toks, first_logits, eng.logits()
+
+
+def _rank_prefill(rank, world, port, preset, prompt, n_new, max_seq, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        eng = Qwen3Engine(PRESETS[preset], max_seq, device=rank, tp_rank=rank, tp_size=world)
+        eng.init_synthetic(SEED)
+        eng.connect_tensor_parallel()
+        eng.prefill_dense(prompt[:7])  # an earlier prompt: the exchange epochs carry on across calls
+        q.put((rank, _prefill_then_decode(eng, prompt, n_new), None))
+        dist.barrier()
+        eng.close()
+    except Exception as e:
+        q.put((rank, repr(e), None))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("preset,world,plen", [("tiny", 2, 50), ("tiny", 2, 2100), ("qwen3-8b-l2", 2, 300),
+                                               ("qwen3-0.6b", 4, 129), ("qwen3-8b-l2", 4, 300),
+                                               ("qwen3-8b-l2", 8, 300)])
+def test_tp_dense_prefill_matches_single_gpu(preset, world, plen):
+    """Dense prefill under tensor parallelism (row-parallel subtree sums and
+    normalised rows exchanged over NVLink) computes the same bits as one GPU:
+    the greedy token after the prompt, the prompt's last logits, and the
+    decode steps that continue from the KV cache it wrote. 2100 positions
+    take two segments."""
+    if NGPU < world:
+        pytest.skip(f"needs {world} GPUs")
+    shape = PRESETS[preset]
+    prompt = prompt_ids(plen, shape.vocab, seed=9)
+    n_new, max_seq = 12, plen + 16
+    with Qwen3Engine(shape, max_seq, device=0) as eng:
+        eng.init_synthetic(SEED)
+        ref_toks, ref_first, ref_last = _prefill_then_decode(eng, prompt, n_new)
+    results = _run_ranks(_rank_prefill, world, preset, prompt, n_new, max_seq)
+    shard = shape.vocab // world
+    for rank in range(world):
+        got, _ = results[rank]
+        assert not isinstance(got, str), got
+        toks, first, last = got
+        assert toks == ref_toks, f"rank {rank} tokens differ from tp=1"
+        part = slice(rank * shard, (rank + 1) * shard)
+        assert np.array_equal(first, ref_first[part]), f"rank {rank} prefill logits differ"
+        assert np.array_equal(last, ref_last[part]), f"rank {rank} decode logits differ"
+
+
 def test_tp_loads_checkpoint_shards(tmp_path):
     """Each rank streams only its shards of a sharded safetensors checkpoint;
     tp=2 then matches one GPU on the same weights."""

@@ -85,6 +85,67 @@ __host__ __device__ inline size_t tp_region_part_bytes(uint32_t H) { return stat
 __host__ __device__ inline size_t tp_region_lm_offset(uint32_t H) { return tp_region_part_bytes(H); }
 __host__ __device__ inline size_t tp_region_bytes(uint32_t H) { return tp_region_lm_offset(H) + sizeof(LmSlot) * kMaxTp; }
 
+// ---- dense prefill exchange (prefill.cu) ----
+// The row-parallel prefill projections (o_proj, down) are the 8 canonical K
+// chunks, each its own FP32 accumulation, summed in one fixed tree
+// ((c0 + c1) + (c2 + c3)) + ((c4 + c5) + (c6 + c7)): a rank sums the subtree
+// of the chunks it holds, then the owner of each row sums the ranks'
+// subtrees, so every tensor-parallel size (1, 2, 4, 8) yields the same bits.
+// Tensor parallel: behind the decode exchange, every rank's region holds
+//   flag[5]          epochs: subtree sums published (o_proj 0, down 1),
+//                    normalised rows published (o_proj 2, down 3), the
+//                    other ranks' rows of a segment copied in (4)
+//   lm[kMaxTp]       lm_head candidates of the last prompt position
+//   part[2][cap][H]  FP32 subtree sums of this rank (o_proj, down)
+//   xn[cap][H]       bf16 normalised rows: the owner of a row writes it, the
+//                    other ranks copy it in before their next GEMM
+// Rows are owned in contiguous runs of ceil(M / tp). Flags only grow (one
+// epoch per exchange, the same sequence on every rank), so nothing is cleared.
+constexpr uint32_t kPfFlags = 5;
+constexpr size_t kPfHeaderBytes = 4096;
+constexpr size_t kPfLmOffset = 256;
+__host__ __device__ inline size_t pf_region_offset(uint32_t H) { return (tp_region_bytes(H) + 4095) / 4096 * 4096; }
+__host__ __device__ inline size_t pf_part_offset(uint32_t H) { return pf_region_offset(H) + kPfHeaderBytes; }
+__host__ __device__ inline size_t pf_xn_offset(uint32_t H, uint32_t cap) {
+  return pf_part_offset(H) + 2ull * cap * H * sizeof(float);
+}
+__host__ __device__ inline size_t pf_region_end(uint32_t H, uint32_t cap) {
+  return pf_xn_offset(H, cap) + static_cast<size_t>(cap) * H * 2;
+}
+
+// Inputs of one tree sum: n (1, 2, 4 or 8) FP32 arrays of the same shape,
+// summed as the bottom-up pairwise tree over them in index order.
+struct PfTree {
+  const float *in[kCanonChunks];
+  uint32_t n;
+};
+
+// Flags that must reach `epoch` before the data behind them is read (a
+// bounded wait; a timeout sets bit 0 of *err and the reader skips its rows).
+struct PfWait {
+  const unsigned long long *flag[kMaxTp];
+  uint32_t count;
+  unsigned long long epoch;
+  uint32_t *err;
+};
+
+// Copy of the other ranks' normalised rows into this rank's xn.
+struct PfGather {
+  const uint16_t *src[kMaxTp];             // xn of rank q
+  const unsigned long long *flag[kMaxTp];  // rank q's "rows published" flag
+  unsigned long long epoch;
+  uint32_t tp, rank, rows_per;
+  uint32_t *err;
+};
+
+// Cross-rank greedy pick of the last prompt position.
+struct PfPick {
+  LmSlot *slots[kMaxTp];  // lm slot array of rank q
+  unsigned long long epoch;
+  uint32_t tp, rank, v_offset;
+  uint32_t *err;
+};
+
 struct DecodeDims {
   uint32_t H;           // hidden size
   uint32_t I_l;         // intermediate rows held by this rank
@@ -169,5 +230,18 @@ uint32_t step_trace(const StepPlan *plan, uint64_t *host, uint32_t capacity);
 // Re-arms the grid barrier (after a failed step or on reset).
 cudaError_t step_reset(const StepPlan *plan, cudaStream_t s);
 uint32_t pos_chunks(uint32_t max_seq);
+
+// Dense prefill exchange kernels (prefill.cu).
+cudaError_t prefill_presum(const PfTree &t, float *out, uint64_t elems, cudaStream_t s);
+cudaError_t prefill_signal(unsigned long long *flag, unsigned long long epoch, cudaStream_t s);
+// Holds the stream until every flag of w reaches its epoch (bounded).
+cudaError_t prefill_wait(const PfWait &w, cudaStream_t s);
+// Rows [row0, row0 + rows): o = bf16(tree sum), x = bf16(x + o), xn = RMSNorm(x).
+cudaError_t prefill_reduce_rms(const PfTree &t, const PfWait &w, uint16_t *x, const uint16_t *norm, uint16_t *xn,
+                               uint32_t row0, uint32_t rows, uint32_t H, float eps, cudaStream_t s);
+cudaError_t prefill_gather(const PfGather &g, uint16_t *xn, uint32_t M, uint32_t H, cudaStream_t s);
+// Greedy token of one logit row (this rank's vocabulary shard), combined
+// across ranks when tp > 1: lowest index on ties, 0xffffffff on NaN/Inf.
+cudaError_t prefill_pick(const uint16_t *logits, uint32_t V_l, const PfPick &p, uint32_t *out, cudaStream_t s);
 
 }  // namespace xpu

@@ -331,6 +331,7 @@ class Qwen3Engine {
     CK(cudaSetDevice(device_));
     TpLinks links{};
     const uint32_t H = d_.H;
+    region_base_.assign(tp_, nullptr);
     for (uint32_t q = 0; q < tp_; ++q) {
       uint8_t *base = xregion_;
       if (q != rank_) {
@@ -341,6 +342,7 @@ class Qwen3Engine {
         peer_regions_.push_back(ptr);
         base = static_cast<uint8_t *>(ptr);
       }
+      region_base_[q] = base;
       links.part[q] = reinterpret_cast<unsigned long long *>(base);
       links.lm[q] = reinterpret_cast<LmSlot *>(base + tp_region_lm_offset(H));
     }
@@ -582,34 +584,109 @@ class Qwen3Engine {
   // Dense prefill (compute-bound): the prompt's positions go through each
   // layer together, in segments of up to kPrefillSegment positions, the
   // projections as tcgen05 GEMMs against the stored weights (prefill.cu);
-  // then the lm_head GEMV and argmax of the last position. Leaves the engine
-  // at position n with the greedy token after the prompt, which is returned,
-  // and the last position's logits in logits() (single GPU).
+  // then the lm_head GEMV and greedy pick of the last position. o_proj and
+  // down are the canonical K chunks summed in a fixed tree (decode.cuh), so
+  // every tensor-parallel size computes the same bits: under tensor
+  // parallelism each rank sums its own chunks, the owner of each row sums the
+  // ranks' subtrees over NVLink, and the normalised rows are copied to the
+  // other ranks before the next GEMM. Leaves the engine at position n with
+  // the greedy token after the prompt, which is returned, and the last
+  // position's logits (this rank's vocabulary shard) in logits().
   static constexpr uint32_t kPrefillSegment = 2048;
+  uint32_t prefill_cap() const { return std::min(max_seq_, kPrefillSegment); }
 
   uint32_t dense_prefill(const uint32_t *prompt, uint32_t n) {
-    if (tp_ > 1) throw InvalidArg("dense prefill runs on one GPU (tp_size 1)");
     if (n == 0) throw InvalidArg("at least one prompt token is required");
     if (n > max_seq_) throw InvalidArg("prompt exceeds the maximum sequence");
     for (uint32_t i = 0; i < n; ++i)
       if (prompt[i] >= shape_.vocab_size) throw InvalidArg("prompt token id outside the vocabulary");
     if (!loaded_) throw InvalidArg("no weights: call init_synthetic, load a checkpoint or set every tensor");
+    if (broken_)
+      throw InvalidArg("a tensor-parallel exchange timed out earlier: destroy and recreate the engines on every rank");
+    if (tp_ > 1 && !connected_) throw InvalidArg("tensor-parallel engine not connected: call xpu_qwen3_tp_connect");
     CK(cudaSetDevice(device_));
     const uint32_t H = d_.H, I = d_.I_l, QH = d_.QH_l, KVH = d_.KVH_l, R = (QH + 2 * KVH) * kHD;
-    const uint32_t cap = std::min(max_seq_, kPrefillSegment);
+    const uint32_t cap = prefill_cap(), chunks_l = d_.chunks_l;
+    const uint64_t plane = static_cast<uint64_t>(cap) * H;
     if (!pf_x_) {
-      pf_x_ = dev_alloc<uint16_t>(static_cast<uint64_t>(cap) * H);
-      pf_xn_ = dev_alloc<uint16_t>(static_cast<uint64_t>(cap) * std::max(H, I));
+      pf_x_ = dev_alloc<uint16_t>(plane);
       pf_big_ = dev_alloc<uint16_t>(static_cast<uint64_t>(cap) * std::max(R, 2 * I));
+      pf_h_ = dev_alloc<uint16_t>(static_cast<uint64_t>(cap) * I);
       pf_q_ = dev_alloc<uint16_t>(static_cast<uint64_t>(cap) * QH * kHD);
       pf_att_ = dev_alloc<uint16_t>(static_cast<uint64_t>(cap) * QH * kHD);
-      pf_o_ = dev_alloc<uint16_t>(static_cast<uint64_t>(cap) * H);
+      // canonical-chunk partials (at tp 8 each rank holds one chunk, which
+      // the GEMM writes straight into the exchange region)
+      if (tp_ == 1 || chunks_l > 1) pf_chunks_ = dev_alloc<float>(chunks_l * plane);
+      pf_xn_ = tp_ == 1 ? dev_alloc<uint16_t>(plane)
+                        : reinterpret_cast<uint16_t *>(xregion_ + pf_xn_offset(H, cap));
       pf_tok_ = dev_alloc<uint32_t>(cap + 1);
+      pf_err_ = dev_alloc<uint32_t>(1);
+      CK(cudaMemset(pf_err_, 0, sizeof(uint32_t)));
     }
     const float eps = d_.eps;
     cudaStream_t s = stream_;
     for (uint32_t p0 = 0; p0 < n; p0 += cap) {
       const uint32_t M = std::min(cap, n - p0);
+      const uint32_t rows_per = (M + tp_ - 1) / tp_;
+      const uint32_t row0 = std::min(M, rank_ * rows_per), rows = std::min(M, row0 + rows_per) - row0;
+      // Row-parallel projection `which` (0 o_proj, 1 down) of A [M][K_l]
+      // against W [H][K_l], then x += its sum over all chunks and xn =
+      // RMSNorm(x) with `norm`, for every row on every rank.
+      auto rowpar = [&](uint32_t which, const uint16_t *A, const uint16_t *W, uint32_t K_l, const uint16_t *norm) {
+        const uint32_t Kc = K_l / chunks_l;
+        PfTree tree{};
+        PfWait wait{};
+        if (tp_ == 1) {
+          CK(gemm_chunks_launch(A, W, pf_chunks_, M, H, Kc, chunks_l, s));
+          tree.n = chunks_l;
+          for (uint32_t c = 0; c < chunks_l; ++c) tree.in[c] = pf_chunks_ + c * static_cast<uint64_t>(M) * H;
+          CK(prefill_reduce_rms(tree, wait, pf_x_, norm, pf_xn_, 0, M, H, eps, s));
+          return;
+        }
+        const unsigned long long epoch = ++pf_epoch_;
+        float *mine = pf_part(rank_, which);
+        if (chunks_l == 1) {
+          CK(gemm_chunks_launch(A, W, mine, M, H, Kc, 1, s));
+        } else {
+          CK(gemm_chunks_launch(A, W, pf_chunks_, M, H, Kc, chunks_l, s));
+          PfTree own{};
+          own.n = chunks_l;
+          for (uint32_t c = 0; c < chunks_l; ++c) own.in[c] = pf_chunks_ + c * static_cast<uint64_t>(M) * H;
+          CK(prefill_presum(own, mine, static_cast<uint64_t>(M) * H, s));
+        }
+        CK(prefill_signal(pf_flag(rank_, which), epoch, s));
+        tree.n = tp_;
+        wait.count = tp_;
+        wait.epoch = epoch;
+        wait.err = pf_err_;
+        for (uint32_t q = 0; q < tp_; ++q) {
+          tree.in[q] = pf_part(q, which);
+          wait.flag[q] = pf_flag(q, which);
+        }
+        CK(prefill_reduce_rms(tree, wait, pf_x_, norm, pf_xn_, row0, rows, H, eps, s));
+        CK(prefill_signal(pf_flag(rank_, 2 + which), epoch, s));
+        PfGather g{};
+        for (uint32_t q = 0; q < tp_; ++q) {
+          g.src[q] = reinterpret_cast<const uint16_t *>(region_base_[q] + pf_xn_offset(H, cap));
+          g.flag[q] = pf_flag(q, 2 + which);
+        }
+        g.epoch = epoch;
+        g.tp = tp_;
+        g.rank = rank_;
+        g.rows_per = rows_per;
+        g.err = pf_err_;
+        CK(prefill_gather(g, pf_xn_, M, H, s));
+      };
+      if (tp_ > 1 && p0 > 0) {
+        // every rank has copied the previous segment's last rows from this
+        // one before this rank overwrites its xn
+        PfWait w{};
+        w.count = tp_;
+        w.epoch = pf_epoch_;
+        w.err = pf_err_;
+        for (uint32_t q = 0; q < tp_; ++q) w.flag[q] = pf_flag(q, 4);
+        CK(prefill_wait(w, s));
+      }
       CK(cudaMemcpyAsync(pf_tok_, prompt + p0, M * sizeof(uint32_t), cudaMemcpyHostToDevice, s));
       CK(prefill_embed(embed_, pf_tok_, pf_x_, M, H, s));
       CK(prefill_rms(pf_x_, layers_[0].in_norm, pf_xn_, M, H, eps, s));
@@ -617,26 +694,39 @@ class Qwen3Engine {
         const Layer &L = layers_[l];
         CK(gemm_launch_ex(false, true, pf_xn_, L.wqkv, pf_big_, M, R, H, s));
         CK(prefill_heads(pf_big_, L.q_norm, L.k_norm, cos_, sin_, pf_q_, L.kcache, L.vcache, p0, M, QH, KVH, eps, s));
-        CK(prefill_attention(pf_q_, L.kcache, L.vcache, pf_att_, p0, M, QH, KVH, s, pf_tc_));
-        CK(gemm_launch_ex(false, true, pf_att_, L.wo, pf_o_, M, H, QH * kHD, s));
-        CK(prefill_add_rms(pf_x_, pf_o_, L.post_norm, pf_xn_, M, H, eps, s));
+        CK(prefill_attention(pf_q_, L.kcache, L.vcache, pf_att_, p0, M, QH, KVH, s));
+        rowpar(0, pf_att_, L.wo, QH * kHD, L.post_norm);
         CK(gemm_launch_ex(false, true, pf_xn_, L.wgu, pf_big_, M, 2 * I, H, s));
-        CK(prefill_swiglu(pf_big_, pf_xn_, M, I, s));  // h into the (wider) xn buffer
-        CK(gemm_launch_ex(false, true, pf_xn_, L.wd, pf_o_, M, H, I, s));
-        const uint16_t *next_norm = l + 1 < layers_.size() ? layers_[l + 1].in_norm : final_norm_;
-        CK(prefill_add_rms(pf_x_, pf_o_, next_norm, pf_xn_, M, H, eps, s));
+        CK(prefill_swiglu(pf_big_, pf_h_, M, I, s));
+        rowpar(1, pf_h_, L.wd, I, l + 1 < layers_.size() ? layers_[l + 1].in_norm : final_norm_);
       }
+      if (tp_ > 1 && p0 + M < n) CK(prefill_signal(pf_flag(rank_, 4), pf_epoch_, s));
       if (p0 + M == n) {
         const uint16_t *last = pf_xn_ + static_cast<uint64_t>(M - 1) * H;
         CK(gemv_launch(reinterpret_cast<const __nv_bfloat16 *>(lm_head_), reinterpret_cast<const __nv_bfloat16 *>(last),
                        reinterpret_cast<__nv_bfloat16 *>(logits_), d_.V_l, H, s));
-        CK(qwen_argmax_launch(logits_, pf_tok_ + cap, d_.V_l, s));
+        PfPick pick{};
+        pick.tp = tp_;
+        pick.rank = rank_;
+        pick.v_offset = d_.v_offset;
+        pick.err = pf_err_;
+        if (tp_ > 1) {
+          pick.epoch = ++pf_epoch_;
+          for (uint32_t q = 0; q < tp_; ++q)
+            pick.slots[q] = reinterpret_cast<LmSlot *>(region_base_[q] + pf_region_offset(H) + kPfLmOffset);
+        }
+        CK(prefill_pick(logits_, d_.V_l, pick, pf_tok_ + cap, s));
       }
     }
-    uint32_t next = 0;
+    uint32_t next = 0, err = 0;
     CK(cudaMemcpyAsync(&next, pf_tok_ + cap, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(&err, pf_err_, sizeof(uint32_t), cudaMemcpyDeviceToHost, s));
     CK(cudaStreamSynchronize(s));
-    if (take_device_error()) throw InvalidArg("a prefill GEMM pipeline timed out");
+    if (take_device_error()) throw DeviceTimeout("a prefill GEMM pipeline timed out");
+    if (err) {
+      broken_ = true;  // the ranks' exchange epochs may now disagree
+      throw DeviceTimeout("a tensor-parallel prefill exchange timed out: destroy and recreate the engines on every rank");
+    }
     if (next == 0xffffffffu) throw InvalidArg("prefill met a NaN/Inf logit");
     *host_state_ = DecodeState{};
     host_state_->token = next;
@@ -988,8 +1078,10 @@ class Qwen3Engine {
     b_.x = dev_alloc<bf16>(H);
     b_.x2 = dev_alloc<bf16>(H);
     if (tp_ > 1) {
-      xregion_ = dev_alloc<uint8_t>(tp_region_bytes(static_cast<uint32_t>(H)));
-      CK(cudaMemset(xregion_, 0, tp_region_bytes(static_cast<uint32_t>(H))));
+      // decode exchange, then the dense prefill exchange of one segment
+      const size_t bytes = pf_region_end(static_cast<uint32_t>(H), prefill_cap());
+      xregion_ = dev_alloc<uint8_t>(bytes);
+      CK(cudaMemset(xregion_, 0, bytes));
     }
     b_.q = dev_alloc<bf16>(qr);
     b_.attn = dev_alloc<bf16>(qr);
@@ -1167,11 +1259,22 @@ class Qwen3Engine {
   SeqState *host_seq_ = nullptr;
   uint32_t *host_berr_ = nullptr;
   unsigned long long *btrace_ = nullptr;  // batched step trace (XPU_BATCH_TRACE=1)
-  // dense prefill buffers (one segment of up to kPrefillSegment positions)
-  uint16_t *pf_x_ = nullptr, *pf_xn_ = nullptr, *pf_big_ = nullptr, *pf_q_ = nullptr, *pf_att_ = nullptr,
-           *pf_o_ = nullptr;
-  uint32_t *pf_tok_ = nullptr;
-  bool pf_tc_ = getenv("XPU_PF_CUDA_CORE") == nullptr;  // experiment switch (attention products)
+  // dense prefill buffers (one segment of up to kPrefillSegment positions);
+  // under tensor parallelism xn, the subtree sums and the flags live in the
+  // exchange regions (decode.cuh)
+  uint16_t *pf_x_ = nullptr, *pf_xn_ = nullptr, *pf_big_ = nullptr, *pf_h_ = nullptr, *pf_q_ = nullptr,
+           *pf_att_ = nullptr;
+  float *pf_chunks_ = nullptr;            // [chunks_l][M][H] canonical-chunk partials
+  uint32_t *pf_tok_ = nullptr, *pf_err_ = nullptr;
+  unsigned long long pf_epoch_ = 0;       // prefill exchanges so far (the same on every rank)
+  std::vector<uint8_t *> region_base_;    // exchange region of rank q (own or IPC-mapped)
+  float *pf_part(uint32_t q, uint32_t which) const {
+    return reinterpret_cast<float *>(region_base_[q] + pf_part_offset(d_.H)) +
+           static_cast<uint64_t>(which) * prefill_cap() * d_.H;
+  }
+  unsigned long long *pf_flag(uint32_t q, uint32_t which) const {
+    return reinterpret_cast<unsigned long long *>(region_base_[q] + pf_region_offset(d_.H)) + which;
+  }
   std::map<uint32_t, cudaGraphExec_t> prefill_exec_;  // chunked-prefill graphs by chunk size
   SeqState *host_prefill_ = nullptr;                 // pinned per-chunk step states
   uint32_t prefill_cap_ = 0;

@@ -90,6 +90,16 @@ __device__ __forceinline__ void tma_load_pair(void *dst, const CUtensorMap *map,
       : "memory");
 }
 
+// 3D form (split GEMM: x = K inside a chunk, y = chunk, z = row).
+__device__ __forceinline__ void tma_load_pair3(void *dst, const CUtensorMap *map, int32_t x, int32_t y, int32_t z,
+                                               uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3, %4}], [%5];" ::"r"(smem_addr(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(cluster_bar)
+      : "memory");
+}
+
 __device__ __forceinline__ void mma_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
@@ -144,10 +154,15 @@ __device__ __forceinline__ TileCoord tile_coord(uint32_t t, uint32_t tiles_m, ui
 
 // BK: B is K-major (W[N,K] row-major, C = A . W^T); its per-CTA half of the
 // tile (128 N rows x 128 K) is staged exactly like A's (two 128 x 64 boxes).
-template <bool FP16, bool BK>
+// SPLIT (with BK): K is cut into `chunks` chunks of K columns each and every
+// chunk is its own accumulation, written as FP32 C[chunk][M][N]; the maps
+// are 3D (K inside the chunk, chunk, row) so a chunk's last stage reads zeros
+// past its end instead of the next chunk's columns.
+template <bool FP16, bool BK, bool SPLIT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, uint16_t *C,
-          uint32_t M, uint32_t N, uint32_t K) {
+k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, void *C,
+          uint32_t M, uint32_t N, uint32_t K, uint32_t chunks) {
+  static_assert(!SPLIT || BK, "split GEMM is the A . W^T form");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
@@ -159,6 +174,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
   const uint32_t rank = cluster_rank();  // 0 = the CTA that issues the MMAs
   const uint32_t pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
   const uint32_t tiles_m = (M + kBM - 1) / kBM, tiles_n = (N + kBN - 1) / kBN, tiles = tiles_m * tiles_n;
+  const uint32_t work = SPLIT ? tiles * chunks : tiles;  // chunk-major: a chunk's tiles share its panels in L2
   const uint32_t nk = (K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -188,8 +204,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     if (lane == 0) {
       const uint32_t full0 = cluster_addr(&full[0], 0);
       uint32_t g = 0;
-      for (uint32_t t = pair; t < tiles && !has_failed(&failed); t += pairs) {
-        const TileCoord tc = tile_coord(t, tiles_m, tiles_n);
+      for (uint32_t t = pair; t < work && !has_failed(&failed); t += pairs) {
+        const uint32_t chunk = SPLIT ? t / tiles : 0;
+        const TileCoord tc = tile_coord(t - chunk * tiles, tiles_m, tiles_n);
         const int32_t ya = static_cast<int32_t>(tc.m * kBM + rank * kHalfM);
         const int32_t xb = static_cast<int32_t>(tc.n * kBN + rank * kHalfN);
         for (uint32_t k = 0; k < nk; ++k, ++g) {
@@ -199,6 +216,14 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
           const uint32_t bar = full0 + s * 8u;
           uint8_t *st = ring + s * kStageBytes;
           const int32_t xk = static_cast<int32_t>(k * kBK);
+          if (SPLIT) {
+            const int32_t z = static_cast<int32_t>(chunk);
+            tma_load_pair3(st, &map_a, xk, z, ya, bar);
+            tma_load_pair3(st + kABoxBytes, &map_a, xk + static_cast<int32_t>(kSwz), z, ya, bar);
+            tma_load_pair3(st + kABytes, &map_b, xk, z, xb, bar);
+            tma_load_pair3(st + kABytes + kABoxBytes, &map_b, xk + static_cast<int32_t>(kSwz), z, xb, bar);
+            continue;
+          }
           tma_load_pair(st, &map_a, xk, ya, bar);
           tma_load_pair(st + kABoxBytes, &map_a, xk + static_cast<int32_t>(kSwz), ya, bar);
           if (BK) {
@@ -215,7 +240,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     if (rank == 0 && lane == 0) {
       const uint32_t idesc = instr_desc(FP16, kBM, kBN, BK);
       uint32_t g = 0, i = 0;
-      for (uint32_t t = pair; t < tiles && !has_failed(&failed); t += pairs, ++i) {
+      for (uint32_t t = pair; t < work && !has_failed(&failed); t += pairs, ++i) {
         const uint32_t b = i & 1, use_b = i >> 1;
         if (use_b > 0 && !mbar_wait(&acc_empty[b], (use_b - 1) & 1)) { failed = 1; break; }
         tc_fence_after();
@@ -249,19 +274,27 @@ k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUt
     const uint32_t quarter = warp & 3, h = (warp - 2) >> 2;
     const uint32_t release = cluster_addr(&acc_empty[0], 0);
     uint32_t i = 0;
-    for (uint32_t t = pair; t < tiles; t += pairs, ++i) {
+    for (uint32_t t = pair; t < work; t += pairs, ++i) {
       const uint32_t b = i & 1;
       if (!mbar_wait(&acc_full[b], (i >> 1) & 1)) { failed = 1; break; }
       tc_fence_after();
-      const TileCoord tc = tile_coord(t, tiles_m, tiles_n);
+      const uint32_t chunk = SPLIT ? t / tiles : 0;
+      const TileCoord tc = tile_coord(t - chunk * tiles, tiles_m, tiles_n);
       const uint32_t row = tc.m * kBM + rank * kHalfM + quarter * 32 + lane;
 #pragma unroll 1
       for (uint32_t c = h * 128; c < h * 128 + 128; c += 32) {
         uint32_t r[32];
         tmem_ld32(tmem + ((quarter * 32u) << 16) + b * kAccCols + c, r);
         const uint32_t col = tc.n * kBN + c;
-        if (row < M && col < N) {
-          uint16_t *dst = C + static_cast<size_t>(row) * N + col;
+        if (SPLIT && row < M && col < N) {  // FP32 partial of this chunk, unrounded
+          float *dst = static_cast<float *>(C) + (static_cast<size_t>(chunk) * M + row) * N + col;
+#pragma unroll
+          for (uint32_t q = 0; q < 8; ++q) {
+            if (col + 4 * q >= N) break;
+            *reinterpret_cast<uint4 *>(dst + 4 * q) = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+          }
+        } else if (row < M && col < N) {
+          uint16_t *dst = static_cast<uint16_t *>(C) + static_cast<size_t>(row) * N + col;
 #pragma unroll
           for (uint32_t q = 0; q < 4; ++q) {
             if (col + 8 * q >= N) break;
@@ -323,6 +356,53 @@ __global__ void __launch_bounds__(256) k_gemm_simple(const T *A, const T *B, T *
 
 size_t gemm_smem_bytes() { return kStages * kStageBytes + 1024; }
 
+namespace {
+using GemmKernel = void (*)(CUtensorMap, CUtensorMap, void *, uint32_t, uint32_t, uint32_t, uint32_t);
+
+// Persistent 2-CTA launch: as many pairs as can be resident at once (the
+// pairs do not wait on one another, so fewer resident pairs only cost time),
+// cached per kernel kind and device.
+cudaError_t launch_tc(GemmKernel kernel, int kind, const CUtensorMap &map_a, const CUtensorMap &map_b, void *C,
+                      uint32_t M, uint32_t N, uint32_t K, uint32_t chunks, cudaStream_t stream) {
+  const size_t smem = gemm_smem_bytes();
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int device = 0;
+  e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  static std::mutex cache_mutex;
+  static int resident_pairs[5][64] = {};
+  int pairs = 0;
+  {
+    std::lock_guard<std::mutex> lock(cache_mutex);
+    int &cached = resident_pairs[kind][device & 63];
+    if (cached == 0) {
+      cfg.gridDim = dim3(2);
+      e = cudaOccupancyMaxActiveClusters(&cached, kernel, &cfg);
+      if (e != cudaSuccess) return e;
+      if (cached < 1) return cudaErrorLaunchOutOfResources;
+    }
+    pairs = cached;
+  }
+  const uint64_t work = static_cast<uint64_t>((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN) * chunks;
+  cfg.gridDim = dim3(2 * static_cast<uint32_t>(std::min<uint64_t>(work, static_cast<uint64_t>(pairs))));
+  e = cudaLaunchKernelEx(&cfg, kernel, map_a, map_b, C, M, N, K, chunks);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+}  // namespace
+
 cudaError_t gemm_launch(bool fp16, const void *A, const void *B, void *C, uint32_t M, uint32_t N, uint32_t K,
                         cudaStream_t stream) {
   return gemm_launch_ex(fp16, false, A, B, C, M, N, K, stream);
@@ -349,47 +429,22 @@ cudaError_t gemm_launch_ex(bool fp16, bool b_kmajor, const void *A, const void *
   e = b_kmajor ? make_tmap_2d_u16_swizzled(&map_b, B, K, N, K, kSwz, kHalfN)
                : make_tmap_2d_u16_swizzled(&map_b, B, N, K, N, kSwz, kBK);
   if (e != cudaSuccess) return e;
-  const size_t smem = gemm_smem_bytes();
-  auto kernel = fp16 ? (b_kmajor ? k_gemm_tc<true, true> : k_gemm_tc<true, false>)
-                     : (b_kmajor ? k_gemm_tc<false, true> : k_gemm_tc<false, false>);
-  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
+  auto kernel = fp16 ? (b_kmajor ? k_gemm_tc<true, true, false> : k_gemm_tc<true, false, false>)
+                     : (b_kmajor ? k_gemm_tc<false, true, false> : k_gemm_tc<false, false, false>);
+  return launch_tc(kernel, (fp16 ? 1 : 0) + (b_kmajor ? 2 : 0), map_a, map_b, C, M, N, K, 1, stream);
+}
 
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(kGemmThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  // Persistent grid: as many pairs as can be resident at once (the pairs do
-  // not wait on one another, so fewer resident pairs only cost time).
-  int device = 0;
-  e = cudaGetDevice(&device);
+cudaError_t gemm_chunks_launch(const void *A, const void *W, float *C, uint32_t M, uint32_t N, uint32_t Kc,
+                               uint32_t chunks, cudaStream_t stream) {
+  if (M == 0 || N == 0 || Kc == 0 || chunks == 0) return cudaErrorInvalidValue;
+  if (Kc % 8 || N % 8 || !aligned16(A) || !aligned16(W) || !aligned16(C)) return cudaErrorInvalidValue;
+  CUtensorMap map_a, map_b;
+  const uint64_t K = static_cast<uint64_t>(Kc) * chunks;
+  cudaError_t e = make_tmap_3d_u16_swizzled(&map_a, A, Kc, chunks, M, Kc, K, kSwz, kHalfM);
   if (e != cudaSuccess) return e;
-  static std::mutex cache_mutex;
-  static int resident_pairs[4][64] = {};
-  int pairs = 0;
-  {
-    std::lock_guard<std::mutex> lock(cache_mutex);
-    int &cached = resident_pairs[(fp16 ? 1 : 0) + (b_kmajor ? 2 : 0)][device & 63];
-    if (cached == 0) {
-      cfg.gridDim = dim3(2);
-      e = cudaOccupancyMaxActiveClusters(&cached, kernel, &cfg);
-      if (e != cudaSuccess) return e;
-      if (cached < 1) return cudaErrorLaunchOutOfResources;
-    }
-    pairs = cached;
-  }
-  const uint32_t tiles = ((M + kBM - 1) / kBM) * ((N + kBN - 1) / kBN);
-  cfg.gridDim = dim3(2 * std::min<uint32_t>(tiles, static_cast<uint32_t>(pairs)));
-  e = cudaLaunchKernelEx(&cfg, kernel, map_a, map_b, static_cast<uint16_t *>(C), M, N, K);
+  e = make_tmap_3d_u16_swizzled(&map_b, W, Kc, chunks, N, Kc, K, kSwz, kHalfN);
   if (e != cudaSuccess) return e;
-  return cudaGetLastError();
+  return launch_tc(k_gemm_tc<false, true, true>, 4, map_a, map_b, C, M, N, Kc, chunks, stream);
 }
 
 unsigned take_device_error() {

@@ -1,22 +1,29 @@
 // Dense prefill: the prompt's positions go through each layer together, so
 // every projection is a tcgen05 GEMM over all of them (C = X . W^T against
-// the stored weights, gemm_launch_ex) - compute-bound, each weight read once
-// per segment of up to kPrefillSegment positions - instead of the decode
-// step's weight streaming per position. Around the GEMMs, the small kernels
-// here apply the same rounding points as the decode step (those of the
-// transformers Qwen3 bf16 eager forward):
-//   k_pf_embed      x[m] = embed[token[m]]
-//   k_pf_rms        xn[m] = bf16(w * bf16(x * RN(1/RN(sqrt(mean(x^2) + eps)))))
-//   k_pf_heads      per (position, head) of the raw q/k/v rows: q/k RMSNorm
-//                   + RoPE into q / the key cache, v into the value cache
-//   k_pf_attention  causal GQA attention over the cache for the segment's
-//                   queries: s = bf16(bf16(q.k) * scale), exact softmax over
-//                   the whole context (two passes: statistics, then
-//                   probabilities bf16(exp(s - M) * (1 / S)) and p.v in FP32)
-//   k_pf_add_rms    x = bf16(x + y), then xn = RMSNorm(x) with the next norm
-//   k_pf_swiglu     h = bf16(bf16(silu(g)) * u) from the interleaved gate/up
-// The attention is CUDA-core FP32 (one CTA per kv head and block of 16
-// queries; the group's heads share every K/V tile staged in shared memory).
+// the stored weights) - compute-bound, each weight read once per segment of
+// up to kPrefillSegment positions - instead of the decode step's weight
+// streaming per position. Around the GEMMs, the small kernels here apply the
+// same rounding points as the decode step (those of the transformers Qwen3
+// bf16 eager forward):
+//   k_pf_embed        x[m] = embed[token[m]]
+//   k_pf_rms          xn[m] = bf16(w * bf16(x * RN(1/RN(sqrt(mean(x^2) + eps)))))
+//   k_pf_heads        per (position, head) of the raw q/k/v rows: q/k RMSNorm
+//                     + RoPE into q / the key cache, v into the value cache
+//   k_pf_attention_tc causal GQA attention over the cache for the segment's
+//                     queries (mma.sync bf16 products, FP32 accumulation):
+//                     s = bf16(bf16(q.k) * scale), exact softmax over the whole
+//                     context (two passes: statistics, then probabilities
+//                     bf16(exp(s - M) * (1 / S)) and p.v)
+//   k_pf_swiglu       h = bf16(bf16(silu(g)) * u) from the interleaved gate/up
+// and the row-parallel exchange of o_proj and down (canonical K chunks from
+// gemm_chunks_launch, summed in the fixed tree of decode.cuh):
+//   k_pf_presum       a rank's own chunks -> its subtree sum (tp 2, 4)
+//   k_pf_signal       publishes an epoch after the kernels before it
+//   k_pf_reduce_rms   rows this rank owns: x = bf16(x + bf16(tree sum of the
+//                     ranks' subtrees, read over NVLink)), xn = RMSNorm(x)
+//   k_pf_gather       the other ranks' xn rows, copied in over NVLink
+//   k_pf_pick         greedy token of the last position across the ranks'
+//                     vocabulary shards
 #include <cuda_bf16.h>
 
 #include <algorithm>
@@ -69,17 +76,6 @@ __global__ void k_pf_rms(const uint16_t *x, const uint16_t *w, uint16_t *xn, uin
   rms_row(x + m * H, w, xn + m * H, H, eps, scratch);
 }
 
-// x = bf16(x + y) for row m, then xn = RMSNorm(x) with w.
-__global__ void k_pf_add_rms(uint16_t *x, const uint16_t *y, const uint16_t *w, uint16_t *xn, uint32_t H, float eps) {
-  __shared__ float scratch[32];
-  const size_t m = blockIdx.x;
-  uint16_t *xr = x + m * H;
-  const uint16_t *yr = y + m * H;
-  for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) xr[i] = bfb(__fadd_rn(bfv(xr, i), bfv(yr, i)));
-  __syncthreads();
-  rms_row(xr, w, xn + m * H, H, eps, scratch);
-}
-
 // One warp per (position, head) of the raw [q heads; k heads; v heads] row
 // (bf16 GEMM outputs): lane l owns dimensions l, l + 32, l + 64, l + 96, so
 // both rotate-half pairs sit in one lane - the decode step's head epilogue.
@@ -125,143 +121,6 @@ __global__ void k_pf_heads(const uint16_t *qkv, uint32_t rows_qkv, const uint16_
                        : kc + (static_cast<size_t>(pos) * KVH + (head - QH)) * kHD;
 #pragma unroll
   for (int j = 0; j < 4; ++j) dst[lane + 32 * j] = bfb(out[j]);
-}
-
-// ---------------------------------------------------------------- attention
-constexpr uint32_t kPfQ = 16;        // queries per CTA
-constexpr uint32_t kPfKeys = 64;     // keys per staged tile
-constexpr uint32_t kPfThreads = 256;
-
-template <int G>
-struct PfAttnSmem {
-  float qt[kHD][G * kPfQ];        // q, transposed: [dim][row]
-  float kt[kHD][kPfKeys];         // k tile, transposed: [dim][key]
-  float vt[kPfKeys][kHD];         // v tile: [key][dim]
-  float p[kPfKeys][G * kPfQ];     // scores, then probabilities: [key][row]
-  float rmax[G * kPfQ], rsum[G * kPfQ];
-};
-
-// Rows r = g * kPfQ + i: head kvh * G + g, query position p0 + q0 + i.
-template <int G>
-__global__ void __launch_bounds__(kPfThreads) k_pf_attention(const uint16_t *q, const uint16_t *kc, const uint16_t *vc,
-                                                             uint16_t *out, uint32_t p0, uint32_t M, uint32_t QH,
-                                                             uint32_t KVH) {
-  constexpr uint32_t R = G * kPfQ;
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  PfAttnSmem<G> &s = *reinterpret_cast<PfAttnSmem<G> *>(smem_raw);
-  const uint32_t kvh = blockIdx.y, q0 = blockIdx.x * kPfQ, t = threadIdx.x;
-  const uint32_t nq = min(kPfQ, M - q0);
-  const uint32_t last = p0 + q0 + nq - 1;  // last key any row of this CTA sees
-  for (uint32_t e = t; e < R * kHD; e += kPfThreads) {
-    const uint32_t r = e / kHD, dd = e % kHD, g = r / kPfQ, i = r % kPfQ;
-    s.qt[dd][r] = i < nq ? bfv(q, (static_cast<size_t>(q0 + i) * QH + kvh * G + g) * kHD + dd) : 0.f;
-  }
-  // Score micro-tile of this thread: rows rr..rr+RT-1, keys kk..kk+3.
-  constexpr uint32_t RT = R / 16;  // 16 row groups x 16 key groups of 4 keys
-  const uint32_t rr = (t / 16) * RT, kk = (t % 16) * 4;
-  auto tile_scores = [&](uint32_t key0) {
-    float acc[RT][4];
-#pragma unroll
-    for (uint32_t a = 0; a < RT; ++a)
-#pragma unroll
-      for (uint32_t b = 0; b < 4; ++b) acc[a][b] = 0.f;
-    for (uint32_t dd = 0; dd < kHD; ++dd) {
-      float qv[RT], kv[4];
-#pragma unroll
-      for (uint32_t a = 0; a < RT; ++a) qv[a] = s.qt[dd][rr + a];
-#pragma unroll
-      for (uint32_t b = 0; b < 4; ++b) kv[b] = s.kt[dd][kk + b];
-#pragma unroll
-      for (uint32_t a = 0; a < RT; ++a)
-#pragma unroll
-        for (uint32_t b = 0; b < 4; ++b) acc[a][b] = fmaf(qv[a], kv[b], acc[a][b]);
-    }
-#pragma unroll
-    for (uint32_t a = 0; a < RT; ++a) {
-      const uint32_t qpos = p0 + q0 + (rr + a) % kPfQ;
-#pragma unroll
-      for (uint32_t b = 0; b < 4; ++b) {
-        const uint32_t key = key0 + kk + b;
-        s.p[kk + b][rr + a] = key <= qpos ? round_bf16(__fmul_rn(round_bf16(acc[a][b]), kAttnScale)) : -INFINITY;
-      }
-    }
-  };
-  auto load_k = [&](uint32_t key0) {
-    for (uint32_t e = t; e < kPfKeys * kHD; e += kPfThreads) {
-      const uint32_t key = e / kHD, dd = e % kHD, pos = key0 + key;
-      s.kt[dd][key] = pos <= last ? bfv(kc, (static_cast<size_t>(pos) * KVH + kvh) * kHD + dd) : 0.f;
-    }
-  };
-  // pass 1: per-row max and sum of exp over the whole causal context
-  if (t < R) {
-    s.rmax[t] = -INFINITY;
-    s.rsum[t] = 0.f;
-  }
-  for (uint32_t key0 = 0; key0 <= last; key0 += kPfKeys) {
-    __syncthreads();
-    load_k(key0);
-    __syncthreads();
-    tile_scores(key0);
-    __syncthreads();
-    if (t < R) {  // one thread per row: fold the tile into (max, sum)
-      float m = s.rmax[t];
-      for (uint32_t key = 0; key < kPfKeys; ++key) m = fmaxf(m, s.p[key][t]);
-      float l = s.rsum[t] * (s.rmax[t] == -INFINITY ? 0.f : expf(s.rmax[t] - m));
-      for (uint32_t key = 0; key < kPfKeys; ++key) l += s.p[key][t] == -INFINITY ? 0.f : expf(s.p[key][t] - m);
-      s.rmax[t] = m;
-      s.rsum[t] = l;
-    }
-  }
-  __syncthreads();
-  if (t < R) s.rsum[t] = 1.0f / s.rsum[t];
-  // pass 2: probabilities and p.v; thread output tile: rows ro..ro+RT-1 (as
-  // above), dims od..od+7
-  const uint32_t ro = (t / 16) * RT, od = (t % 16) * 8;
-  float o[RT][8];
-#pragma unroll
-  for (uint32_t a = 0; a < RT; ++a)
-#pragma unroll
-    for (uint32_t b = 0; b < 8; ++b) o[a][b] = 0.f;
-  for (uint32_t key0 = 0; key0 <= last; key0 += kPfKeys) {
-    __syncthreads();
-    load_k(key0);
-    for (uint32_t e = t; e < kPfKeys * kHD; e += kPfThreads) {
-      const uint32_t key = e / kHD, dd = e % kHD, pos = key0 + key;
-      s.vt[key][dd] = pos <= last ? bfv(vc, (static_cast<size_t>(pos) * KVH + kvh) * kHD + dd) : 0.f;
-    }
-    __syncthreads();
-    tile_scores(key0);
-    __syncthreads();
-    for (uint32_t e = t; e < kPfKeys * R; e += kPfThreads) {
-      const uint32_t key = e / R, r = e % R;
-      const float sc = s.p[key][r];
-      s.p[key][r] = sc == -INFINITY ? 0.f : round_bf16(__fmul_rn(expf(sc - s.rmax[r]), s.rsum[r]));
-    }
-    __syncthreads();
-    for (uint32_t key = 0; key < kPfKeys; ++key) {
-      float pv[RT], vv[8];
-#pragma unroll
-      for (uint32_t a = 0; a < RT; ++a) pv[a] = s.p[key][ro + a];
-#pragma unroll
-      for (uint32_t b = 0; b < 8; ++b) vv[b] = s.vt[key][od + b];
-#pragma unroll
-      for (uint32_t a = 0; a < RT; ++a)
-#pragma unroll
-        for (uint32_t b = 0; b < 8; ++b) o[a][b] = fmaf(pv[a], vv[b], o[a][b]);
-    }
-  }
-#pragma unroll
-  for (uint32_t a = 0; a < RT; ++a) {
-    const uint32_t r = ro + a, g = r / kPfQ, i = r % kPfQ;
-    if (i >= nq) continue;
-    uint16_t *dst = out + (static_cast<size_t>(q0 + i) * QH + kvh * G + g) * kHD + od;
-    uint4 pk;
-    pk.x = pack_bf16x2(o[a][0], o[a][1]);
-    pk.y = pack_bf16x2(o[a][2], o[a][3]);
-    pk.z = pack_bf16x2(o[a][4], o[a][5]);
-    pk.w = pack_bf16x2(o[a][6], o[a][7]);
-    *reinterpret_cast<uint4 *>(dst) = pk;
-  }
 }
 
 // ---------------------------------------------- attention on tensor cores
@@ -332,18 +191,20 @@ __global__ void __launch_bounds__(TcAttn<G>::THREADS) k_pf_attention_tc(const ui
   auto stage = [&](uint32_t key0, bool with_v) {
     for (uint32_t e = tid; e < kTcKeys * (kHD / 8); e += C::THREADS) {
       const uint32_t key = e / (kHD / 8), c8 = e % (kHD / 8), pos = key0 + key;
-      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-      if (pos <= last) {
-        const size_t off = (static_cast<size_t>(pos) * KVH + kvh) * kHD + 8 * c8;
-        kv = *reinterpret_cast<const uint4 *>(kc + off);
-        if (with_v) vv = *reinterpret_cast<const uint4 *>(vc + off);
-      }
+      uint4 kv = make_uint4(0, 0, 0, 0);
+      if (pos <= last) kv = *reinterpret_cast<const uint4 *>(kc + (static_cast<size_t>(pos) * KVH + kvh) * kHD + 8 * c8);
       *reinterpret_cast<uint4 *>(&s.k[key][8 * c8]) = kv;
-      if (with_v) {
-        const uint16_t *vh = reinterpret_cast<const uint16_t *>(&vv);
+    }
+    if (!with_v) return;
+    // v transposed: consecutive threads take consecutive keys of one 8-dim
+    // slice, so their 2-byte stores share rows of vt instead of one bank
+    for (uint32_t e = tid; e < kTcKeys * (kHD / 8); e += C::THREADS) {
+      const uint32_t c8 = e / kTcKeys, key = e % kTcKeys, pos = key0 + key;
+      uint4 vv = make_uint4(0, 0, 0, 0);
+      if (pos <= last) vv = *reinterpret_cast<const uint4 *>(vc + (static_cast<size_t>(pos) * KVH + kvh) * kHD + 8 * c8);
+      const uint16_t *vh = reinterpret_cast<const uint16_t *>(&vv);
 #pragma unroll
-        for (uint32_t j = 0; j < 8; ++j) s.vt[8 * c8 + j][key] = vh[j];
-      }
+      for (uint32_t j = 0; j < 8; ++j) s.vt[8 * c8 + j][key] = vh[j];
     }
   };
   // scores of this warp's 16 rows x 64 keys: sc[n][c] = n-tile n (keys 8n..),
@@ -450,14 +311,168 @@ __global__ void k_pf_swiglu(const uint16_t *gu, uint16_t *h, uint32_t I, uint64_
   }
 }
 
-template <int G>
-cudaError_t launch_attn(const uint16_t *q, const uint16_t *kc, const uint16_t *vc, uint16_t *out, uint32_t p0,
-                        uint32_t M, uint32_t QH, uint32_t KVH, cudaStream_t s) {
-  const size_t smem = sizeof(PfAttnSmem<G>);
-  cudaError_t e = cudaFuncSetAttribute(k_pf_attention<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
-  k_pf_attention<G><<<dim3((M + kPfQ - 1) / kPfQ, KVH), kPfThreads, smem, s>>>(q, kc, vc, out, p0, M, QH, KVH);
-  return cudaGetLastError();
+// ------------------------------------------------ row-parallel exchange
+constexpr long long kPfWaitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Thread 0: waits until every flag of w reaches w.epoch (bounded); false on
+// a timeout, after recording it in *w.err.
+__device__ bool wait_all(const PfWait &w) {
+  const long long start = clock64();
+  for (uint32_t q = 0; q < w.count; ++q)
+    while (ld_acquire_sys(w.flag[q]) < w.epoch) {
+      if (clock64() - start > kPfWaitCycles) {
+        atomicOr(w.err, 1u);
+        return false;
+      }
+      __nanosleep(64);
+    }
+  return true;
+}
+
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+
+// Bottom-up pairwise tree over t.in[0..n) at element offset off (n a power
+// of two up to 8): for 8, ((0 + 1) + (2 + 3)) + ((4 + 5) + (6 + 7)).
+__device__ __forceinline__ float4 tree4(const PfTree &t, size_t off) {
+  float4 v[kCanonChunks];
+#pragma unroll
+  for (uint32_t i = 0; i < kCanonChunks; ++i)
+    if (i < t.n) v[i] = __ldcg(reinterpret_cast<const float4 *>(t.in[i] + off));
+#pragma unroll
+  for (uint32_t w = 1; w < kCanonChunks; w <<= 1)
+#pragma unroll
+    for (uint32_t i = 0; i < kCanonChunks; i += 2 * w)
+      if (i + w < t.n) v[i] = add4(v[i], v[i + w]);
+  return v[0];
+}
+
+__global__ void k_pf_presum(const __grid_constant__ PfTree t, float *out, uint64_t vecs) {
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < vecs;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+    reinterpret_cast<float4 *>(out)[i] = tree4(t, 4 * i);
+}
+
+// This rank's writes before this kernel (stream order) become visible to the
+// peers that see the flag.
+__global__ void k_pf_signal(unsigned long long *flag, unsigned long long epoch) {
+  __threadfence_system();
+  st_release_sys(flag, epoch);
+}
+
+__global__ void k_pf_wait(const __grid_constant__ PfWait w) { wait_all(w); }
+
+// Row row0 + blockIdx.x: o = bf16(tree sum of the inputs' row), x = bf16(x +
+// o), xn = RMSNorm(x) with norm.
+__global__ void __launch_bounds__(256) k_pf_reduce_rms(const __grid_constant__ PfTree t, const __grid_constant__ PfWait w,
+                                                       uint16_t *x, const uint16_t *norm, uint16_t *xn, uint32_t row0,
+                                                       uint32_t H, float eps) {
+  __shared__ float scratch[32];
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = w.count ? wait_all(w) : 1;
+  __syncthreads();
+  if (!ok) return;
+  const size_t m = row0 + blockIdx.x;
+  uint16_t *xr = x + m * H;
+  for (uint32_t i = 4 * threadIdx.x; i < H; i += 4 * blockDim.x) {
+    const float4 o = tree4(t, m * H + i);
+    const uint2 xv = *reinterpret_cast<const uint2 *>(xr + i);
+    uint2 r;
+    r.x = pack_bf16x2(__fadd_rn(bf16_bits_to_float(xv.x & 0xffffu), round_bf16(o.x)),
+                      __fadd_rn(bf16_bits_to_float(xv.x >> 16), round_bf16(o.y)));
+    r.y = pack_bf16x2(__fadd_rn(bf16_bits_to_float(xv.y & 0xffffu), round_bf16(o.z)),
+                      __fadd_rn(bf16_bits_to_float(xv.y >> 16), round_bf16(o.w)));
+    *reinterpret_cast<uint2 *>(xr + i) = r;
+  }
+  __syncthreads();
+  rms_row(xr, norm, xn + m * H, H, eps, scratch);
+}
+
+// Row blockIdx.x of xn, unless this rank owns it: copied from its owner once
+// the owner has published it.
+__global__ void __launch_bounds__(128) k_pf_gather(const __grid_constant__ PfGather g, uint16_t *xn, uint32_t H) {
+  const uint32_t m = blockIdx.x, q = m / g.rows_per;
+  if (q == g.rank || q >= g.tp) return;
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    const PfWait w{{g.flag[q]}, 1, g.epoch, g.err};
+    ok = wait_all(w);
+  }
+  __syncthreads();
+  if (!ok) return;
+  const uint4 *src = reinterpret_cast<const uint4 *>(g.src[q] + static_cast<size_t>(m) * H);
+  uint4 *dst = reinterpret_cast<uint4 *>(xn + static_cast<size_t>(m) * H);
+  for (uint32_t c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = __ldcg(src + c);
+}
+
+// One CTA: argmax of this rank's logit row, then (tp > 1) every rank's
+// candidate through the lm slots: each rank writes its candidate into slot
+// `rank` of every region, then reads all slots of its own.
+constexpr uint32_t kPickThreads = 1024;
+__global__ void __launch_bounds__(kPickThreads) k_pf_pick(const uint16_t *logits, uint32_t V_l,
+                                                          const __grid_constant__ PfPick p, uint32_t *out) {
+  __shared__ ArgBest wb[kPickThreads / 32];
+  __shared__ uint32_t wbad[kPickThreads / 32];
+  ArgBest best{-INFINITY, 0xffffffffu};
+  uint32_t bad = 0;
+  for (uint32_t i = threadIdx.x; i < V_l; i += kPickThreads) {
+    const float v = bf16_bits_to_float(logits[i]);
+    bad |= not_finite(v) ? 1u : 0u;
+    best = arg_better(best, ArgBest{v, p.v_offset + i});
+  }
+  best = warp_argbest(best);
+  bad = __reduce_or_sync(kFullMask, bad);
+  if ((threadIdx.x & 31) == 0) {
+    wb[threadIdx.x >> 5] = best;
+    wbad[threadIdx.x >> 5] = bad;
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  best = wb[0];
+  for (uint32_t i = 1; i < kPickThreads / 32; ++i) {
+    best = arg_better(best, wb[i]);
+    bad |= wbad[i];
+  }
+  if (p.tp > 1) {
+    for (uint32_t q = 0; q < p.tp; ++q) {
+      LmSlot *slot = p.slots[q] + p.rank;
+      slot->value = best.value;
+      slot->index = best.index;
+      slot->bad = bad;
+    }
+    __threadfence_system();
+    for (uint32_t q = 0; q < p.tp; ++q) st_relaxed_sys64(&(p.slots[q] + p.rank)->epoch, p.epoch);
+    const LmSlot *own = p.slots[p.rank];
+    PfWait w{};
+    for (uint32_t q = 0; q < p.tp; ++q) w.flag[q] = &own[q].epoch;
+    w.count = p.tp;
+    w.epoch = p.epoch;
+    w.err = p.err;
+    if (!wait_all(w)) {
+      *out = 0xffffffffu;
+      return;
+    }
+    best = ArgBest{-INFINITY, 0xffffffffu};
+    bad = 0;
+    for (uint32_t q = 0; q < p.tp; ++q) {
+      best = arg_better(best, ArgBest{__ldcg(&own[q].value), __ldcg(&own[q].index)});
+      bad |= __ldcg(&own[q].bad);
+    }
+  }
+  *out = (bad || best.index == 0xffffffffu) ? 0xffffffffu : best.index;
 }
 
 }  // namespace
@@ -474,12 +489,6 @@ cudaError_t prefill_rms(const uint16_t *x, const uint16_t *w, uint16_t *xn, uint
   return cudaGetLastError();
 }
 
-cudaError_t prefill_add_rms(uint16_t *x, const uint16_t *y, const uint16_t *w, uint16_t *xn, uint32_t M, uint32_t H,
-                            float eps, cudaStream_t s) {
-  k_pf_add_rms<<<M, 256, 0, s>>>(x, y, w, xn, H, eps);
-  return cudaGetLastError();
-}
-
 cudaError_t prefill_heads(const uint16_t *qkv, const uint16_t *q_norm, const uint16_t *k_norm, const uint16_t *cos_t,
                           const uint16_t *sin_t, uint16_t *q, uint16_t *kc, uint16_t *vc, uint32_t p0, uint32_t M,
                           uint32_t QH, uint32_t KVH, float eps, cudaStream_t s) {
@@ -490,19 +499,12 @@ cudaError_t prefill_heads(const uint16_t *qkv, const uint16_t *q_norm, const uin
 }
 
 cudaError_t prefill_attention(const uint16_t *q, const uint16_t *kc, const uint16_t *vc, uint16_t *out, uint32_t p0,
-                              uint32_t M, uint32_t QH, uint32_t KVH, cudaStream_t s, bool tensor_cores) {
-  if (tensor_cores) switch (QH / KVH) {
-      case 1: return launch_attn_tc<1>(q, kc, vc, out, p0, M, QH, KVH, s);
-      case 2: return launch_attn_tc<2>(q, kc, vc, out, p0, M, QH, KVH, s);
-      case 4: return launch_attn_tc<4>(q, kc, vc, out, p0, M, QH, KVH, s);
-      case 8: return launch_attn_tc<8>(q, kc, vc, out, p0, M, QH, KVH, s);
-      default: return cudaErrorInvalidValue;
-    }
+                              uint32_t M, uint32_t QH, uint32_t KVH, cudaStream_t s) {
   switch (QH / KVH) {
-    case 1: return launch_attn<1>(q, kc, vc, out, p0, M, QH, KVH, s);
-    case 2: return launch_attn<2>(q, kc, vc, out, p0, M, QH, KVH, s);
-    case 4: return launch_attn<4>(q, kc, vc, out, p0, M, QH, KVH, s);
-    case 8: return launch_attn<8>(q, kc, vc, out, p0, M, QH, KVH, s);
+    case 1: return launch_attn_tc<1>(q, kc, vc, out, p0, M, QH, KVH, s);
+    case 2: return launch_attn_tc<2>(q, kc, vc, out, p0, M, QH, KVH, s);
+    case 4: return launch_attn_tc<4>(q, kc, vc, out, p0, M, QH, KVH, s);
+    case 8: return launch_attn_tc<8>(q, kc, vc, out, p0, M, QH, KVH, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -510,6 +512,42 @@ cudaError_t prefill_attention(const uint16_t *q, const uint16_t *kc, const uint1
 cudaError_t prefill_swiglu(const uint16_t *gu, uint16_t *h, uint32_t M, uint32_t I, cudaStream_t s) {
   const uint64_t total = static_cast<uint64_t>(M) * I;
   k_pf_swiglu<<<static_cast<uint32_t>(std::min<uint64_t>((total + 255) / 256, 148 * 16)), 256, 0, s>>>(gu, h, I, total);
+  return cudaGetLastError();
+}
+
+cudaError_t prefill_presum(const PfTree &t, float *out, uint64_t elems, cudaStream_t s) {
+  if (elems % 4 || !aligned16(out)) return cudaErrorInvalidValue;
+  const uint64_t vecs = elems / 4;
+  k_pf_presum<<<static_cast<uint32_t>(std::min<uint64_t>((vecs + 255) / 256, 148 * 8)), 256, 0, s>>>(t, out, vecs);
+  return cudaGetLastError();
+}
+
+cudaError_t prefill_signal(unsigned long long *flag, unsigned long long epoch, cudaStream_t s) {
+  k_pf_signal<<<1, 1, 0, s>>>(flag, epoch);
+  return cudaGetLastError();
+}
+
+cudaError_t prefill_wait(const PfWait &w, cudaStream_t s) {
+  k_pf_wait<<<1, 1, 0, s>>>(w);
+  return cudaGetLastError();
+}
+
+cudaError_t prefill_reduce_rms(const PfTree &t, const PfWait &w, uint16_t *x, const uint16_t *norm, uint16_t *xn,
+                               uint32_t row0, uint32_t rows, uint32_t H, float eps, cudaStream_t s) {
+  if (H % 8) return cudaErrorInvalidValue;
+  if (rows == 0) return cudaSuccess;
+  k_pf_reduce_rms<<<rows, 256, 0, s>>>(t, w, x, norm, xn, row0, H, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t prefill_gather(const PfGather &g, uint16_t *xn, uint32_t M, uint32_t H, cudaStream_t s) {
+  if (H % 8 || g.rows_per == 0) return cudaErrorInvalidValue;
+  k_pf_gather<<<M, 128, 0, s>>>(g, xn, H);
+  return cudaGetLastError();
+}
+
+cudaError_t prefill_pick(const uint16_t *logits, uint32_t V_l, const PfPick &p, uint32_t *out, cudaStream_t s) {
+  k_pf_pick<<<1, kPickThreads, 0, s>>>(logits, V_l, p, out);
   return cudaGetLastError();
 }
 

@@ -31,6 +31,10 @@ cudaError_t make_tmap_2d_u16(struct CUtensorMap_st *map, const void *base, uint6
 cudaError_t make_tmap_2d_u16_swizzled(struct CUtensorMap_st *map, const void *base, uint64_t cols, uint64_t rows,
                                       uint64_t pitch_elems, uint32_t box_cols, uint32_t box_rows);
 
+cudaError_t make_tmap_3d_u16_swizzled(struct CUtensorMap_st *map, const void *base, uint64_t d0, uint64_t d1,
+                                      uint64_t d2, uint64_t stride1, uint64_t stride2, uint32_t box_cols,
+                                      uint32_t box_rows);
+
 // ---- GEMM (gemm.cu) ----
 cudaError_t gemm_launch(bool fp16, const void *A, const void *B, void *C, uint32_t m, uint32_t n, uint32_t k,
                         cudaStream_t stream);
@@ -39,6 +43,12 @@ cudaError_t gemm_launch(bool fp16, const void *A, const void *B, void *C, uint32
 // aligned operands).
 cudaError_t gemm_launch_ex(bool fp16, bool b_kmajor, const void *A, const void *B, void *C, uint32_t m, uint32_t n,
                            uint32_t k, cudaStream_t stream);
+// Split GEMM for the row-parallel prefill projections: with A row-major
+// [M, chunks x Kc] and W row-major [N, chunks x Kc], C[c] = A[:, chunk c] .
+// W[:, chunk c]^T as FP32 [chunks][M][N], one accumulation per chunk (bf16
+// in; Kc and N multiples of 8, 16-byte aligned operands).
+cudaError_t gemm_chunks_launch(const void *A, const void *W, float *C, uint32_t M, uint32_t N, uint32_t Kc,
+                               uint32_t chunks, cudaStream_t stream);
 // Reads and clears the sticky device error word (bit 0: a GEMM wait timed out).
 unsigned take_device_error();
 // Same for the calibrator kernels (peak.cu; bit 1: a pipeline wait timed out).
@@ -49,14 +59,11 @@ cudaError_t prefill_embed(const uint16_t *embed, const uint32_t *tokens, uint16_
                           cudaStream_t s);
 cudaError_t prefill_rms(const uint16_t *x, const uint16_t *w, uint16_t *xn, uint32_t M, uint32_t H, float eps,
                         cudaStream_t s);
-cudaError_t prefill_add_rms(uint16_t *x, const uint16_t *y, const uint16_t *w, uint16_t *xn, uint32_t M, uint32_t H,
-                            float eps, cudaStream_t s);
 cudaError_t prefill_heads(const uint16_t *qkv, const uint16_t *q_norm, const uint16_t *k_norm, const uint16_t *cos_t,
                           const uint16_t *sin_t, uint16_t *q, uint16_t *kc, uint16_t *vc, uint32_t p0, uint32_t M,
                           uint32_t QH, uint32_t KVH, float eps, cudaStream_t s);
-// tensor_cores: mma.sync products (else CUDA-core FP32); same rounding points.
 cudaError_t prefill_attention(const uint16_t *q, const uint16_t *kc, const uint16_t *vc, uint16_t *out, uint32_t p0,
-                              uint32_t M, uint32_t QH, uint32_t KVH, cudaStream_t s, bool tensor_cores);
+                              uint32_t M, uint32_t QH, uint32_t KVH, cudaStream_t s);
 cudaError_t prefill_swiglu(const uint16_t *gu, uint16_t *h, uint32_t M, uint32_t I, cudaStream_t s);
 
 // ---- GEMV ----

@@ -29,6 +29,13 @@ step is
     ncu --metrics gpu__time_duration.sum --clock-control none --profile-from-start off \
         --csv python -m xpu_playground_b200.profile_step --batch 16 --context 512
 
+--prefill N profiles the dense prefill of an N-token prompt instead (one
+untimed call, then one between cudaProfilerStart/Stop, whose wall time is
+printed), so that its launch list is
+
+    ncu --metrics gpu__time_duration.sum --clock-control none --profile-from-start off \
+        --csv python -m xpu_playground_b200.profile_step --prefill 2048
+
 With --trace it prints that step's per-kernel timeline (XPU_BATCH_TRACE=1):
 per kernel kind the critical-path time (end minus the previous kernel's end),
 when its wait on the previous kernel returned, when its last CTA saw its first
@@ -55,7 +62,11 @@ def main() -> None:
     ap.add_argument("--mode", choices=["persistent", "graph"], default="persistent")
     ap.add_argument("--trace", action="store_true")
     ap.add_argument("--batch", type=int, default=0, help="profile the batched step of this many sequences")
+    ap.add_argument("--prefill", type=int, default=0, help="profile the dense prefill of this many tokens")
     args = ap.parse_args()
+    if args.prefill:
+        prefill_profile(args)
+        return
     if args.batch:
         batch_profile(args)
         return
@@ -168,6 +179,29 @@ def trace_table(eng, L: int) -> list[str]:
     lm = t[:, -1] - t[:, -3]
     out.append(f"lm_head  total {lm.mean() / 1e3:.1f}/{lm.max() / 1e3:.1f} us (mean/max over CTAs)")
     return out
+
+
+def prefill_profile(args) -> None:
+    import time
+
+    import torch
+
+    from .qwen3 import Qwen3Engine
+    from .qwen3_config import PRESETS
+
+    shape = PRESETS[args.preset]
+    prompt = [int(t) for t in np.random.default_rng(7).integers(0, shape.vocab, args.prefill)]
+    with Qwen3Engine(shape, args.prefill + 8) as eng:
+        eng.init_synthetic(1)
+        eng.prefill_dense(prompt)
+        eng.synchronize()
+        torch.cuda.cudart().cudaProfilerStart()
+        t0 = time.perf_counter()
+        nxt = eng.prefill_dense(prompt)
+        dt = time.perf_counter() - t0
+        torch.cuda.cudart().cudaProfilerStop()
+    print(f"{args.preset}: dense prefill of {args.prefill} tokens {dt * 1e3:.2f} ms "
+          f"({args.prefill / dt:.0f} tok/s), next token {nxt}")
 
 
 def batch_profile(args) -> None:
