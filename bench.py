@@ -388,7 +388,7 @@ def check_tokens(args, first: int, ids: list[int]) -> dict:
     written by `bench.py --record-tokens` on one GPU): the common prefix must
     be identical."""
     info = {"first_position": first, "count": len(ids), "sha256": token_digest(ids), "ids": ids,
-            "prefill": "token by token through the decode step (xpu_qwen3_generate), at every N"}
+            "prefill": PREFILL_PATH + ", at every N"}
     try:
         gold = json.loads(GOLDEN_TOKENS.read_text())
     except (OSError, ValueError):

@@ -124,13 +124,17 @@ __global__ void k_pf_heads(const uint16_t *qkv, uint32_t rows_qkv, const uint16_
 }
 
 // ---------------------------------------------- attention on tensor cores
-// The same causal attention with the two products on the tensor cores
-// (mma.sync m16n8k16, bf16 in, FP32 accumulation): per warp 16 rows (one
-// head, 16 queries), S = Q K^T for 64 keys at a time, the scores rounded as
-// above, exact two-pass softmax (row statistics over the whole context,
-// then bf16 probabilities that feed P V straight from the S accumulators).
+// Causal GQA attention with the two products on the tensor cores (mma.sync
+// m16n8k16, bf16 in, FP32 accumulation): per warp 16 rows (one head, 16
+// queries), S = Q K^T for 64 keys at a time, the scores rounded as above,
+// exact two-pass softmax (row statistics over the whole context, then bf16
+// probabilities that feed P V straight from the S accumulators). K and V
+// tiles stay row-major [key][dim] in shared memory, double buffered with
+// cp.async (rows past the context zero-filled); fragments come from
+// ldmatrix (V's transposed). The heaviest query blocks (most keys) start
+// first.
 constexpr uint32_t kTcKeys = 64;
-constexpr uint32_t kTcPad = 8;  // bf16 padding per smem row: conflict-free fragment loads
+constexpr uint32_t kTcRow = kHD + 8;  // bf16 per smem row: 272 bytes, conflict-free ldmatrix rows
 
 template <int G>
 struct TcAttn {
@@ -142,9 +146,11 @@ struct TcAttn {
 
 template <int G>
 struct TcAttnSmem {
-  uint16_t q[TcAttn<G>::ROWS][kHD + kTcPad];
-  uint16_t k[kTcKeys][kHD + kTcPad];
-  uint16_t vt[kHD][kTcKeys + kTcPad];  // v tile transposed: [dim][key]
+  uint16_t k[2][kTcKeys][kTcRow];
+  union {
+    uint16_t q[TcAttn<G>::ROWS][kTcRow];  // until the fragments are in registers
+    uint16_t v[2][kTcKeys][kTcRow];
+  };
 };
 
 __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -155,19 +161,40 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint32_t lds32(const uint16_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
+__device__ __forceinline__ uint32_t sh_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(sh_addr(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(sh_addr(p)));
+}
+// 16 bytes global -> shared, or 16 zero bytes when !valid.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sh_addr(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 template <int G>
 __global__ void __launch_bounds__(TcAttn<G>::THREADS) k_pf_attention_tc(const uint16_t *q, const uint16_t *kc,
                                                                         const uint16_t *vc, uint16_t *out, uint32_t p0,
                                                                         uint32_t M, uint32_t QH, uint32_t KVH) {
   using C = TcAttn<G>;
-  extern __shared__ __align__(16) uint8_t smem_raw[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
   TcAttnSmem<G> &s = *reinterpret_cast<TcAttnSmem<G> *>(smem_raw);
-  const uint32_t kvh = blockIdx.y, q0 = blockIdx.x * C::QB, tid = threadIdx.x;
+  const uint32_t kvh = blockIdx.y, q0 = (gridDim.x - 1 - blockIdx.x) * C::QB, tid = threadIdx.x;
   const uint32_t warp = tid >> 5, lane = tid & 31, gq = lane >> 2, tq = lane & 3;
   const uint32_t nq = min(C::QB, M - q0);
-  const uint32_t last = p0 + q0 + nq - 1;
+  const uint32_t last = p0 + q0 + nq - 1, tiles = last / kTcKeys + 1;
   // q rows: r = g * QB + i (head kvh G + g, query q0 + i); rows past nq are zero
   for (uint32_t e = tid; e < C::ROWS * (kHD / 8); e += C::THREADS) {
     const uint32_t r = e / (kHD / 8), c8 = e % (kHD / 8), g = r / C::QB, i = r % C::QB;
@@ -175,62 +202,65 @@ __global__ void __launch_bounds__(TcAttn<G>::THREADS) k_pf_attention_tc(const ui
     if (i < nq) v = *reinterpret_cast<const uint4 *>(q + (static_cast<size_t>(q0 + i) * QH + kvh * G + g) * kHD + 8 * c8);
     *reinterpret_cast<uint4 *>(&s.q[r][8 * c8]) = v;
   }
+  // K (and V) tile t into buffer t & 1
+  auto issue = [&](uint32_t t, bool with_v) {
+    const uint32_t key0 = t * kTcKeys, b = t & 1;
+    for (uint32_t e = tid; e < kTcKeys * (kHD / 8); e += C::THREADS) {
+      const uint32_t key = e / (kHD / 8), c8 = e % (kHD / 8), pos = key0 + key;
+      const size_t off = (static_cast<size_t>(pos <= last ? pos : 0) * KVH + kvh) * kHD + 8 * c8;
+      cp_async16(&s.k[b][key][8 * c8], kc + off, pos <= last);
+      if (with_v) cp_async16(&s.v[b][key][8 * c8], vc + off, pos <= last);
+    }
+    cp_async_commit();
+  };
+  issue(0, false);  // pass 1 needs no V: its buffers still hold q
   __syncthreads();
   // this warp's rows: row0 .. row0 + 15; the thread holds rows gq and gq + 8
   const uint32_t row0 = warp * 16;
   uint32_t qa[kHD / 16][4];
 #pragma unroll
-  for (uint32_t kk = 0; kk < kHD / 16; ++kk) {
-    qa[kk][0] = lds32(&s.q[row0 + gq][16 * kk + 2 * tq]);
-    qa[kk][1] = lds32(&s.q[row0 + gq + 8][16 * kk + 2 * tq]);
-    qa[kk][2] = lds32(&s.q[row0 + gq][16 * kk + 8 + 2 * tq]);
-    qa[kk][3] = lds32(&s.q[row0 + gq + 8][16 * kk + 8 + 2 * tq]);
-  }
+  for (uint32_t kk = 0; kk < kHD / 16; ++kk)
+    ldsm_x4(qa[kk], &s.q[row0 + 8 * ((lane >> 3) & 1) + (lane & 7)][16 * kk + 8 * (lane >> 4)]);
   const uint32_t qpos[2] = {p0 + q0 + (row0 + gq) % C::QB, p0 + q0 + (row0 + gq + 8) % C::QB};
+  // ldmatrix row addresses of this lane inside a K / V tile
+  const uint32_t k_row = 8 * (lane >> 4) + (lane & 7), k_col = 8 * ((lane >> 3) & 1);
+  const uint32_t v_row = 8 * ((lane >> 3) & 1) + (lane & 7), v_col = 8 * (lane >> 4);
 
-  auto stage = [&](uint32_t key0, bool with_v) {
-    for (uint32_t e = tid; e < kTcKeys * (kHD / 8); e += C::THREADS) {
-      const uint32_t key = e / (kHD / 8), c8 = e % (kHD / 8), pos = key0 + key;
-      uint4 kv = make_uint4(0, 0, 0, 0);
-      if (pos <= last) kv = *reinterpret_cast<const uint4 *>(kc + (static_cast<size_t>(pos) * KVH + kvh) * kHD + 8 * c8);
-      *reinterpret_cast<uint4 *>(&s.k[key][8 * c8]) = kv;
-    }
-    if (!with_v) return;
-    // v transposed: consecutive threads take consecutive keys of one 8-dim
-    // slice, so their 2-byte stores share rows of vt instead of one bank
-    for (uint32_t e = tid; e < kTcKeys * (kHD / 8); e += C::THREADS) {
-      const uint32_t c8 = e / kTcKeys, key = e % kTcKeys, pos = key0 + key;
-      uint4 vv = make_uint4(0, 0, 0, 0);
-      if (pos <= last) vv = *reinterpret_cast<const uint4 *>(vc + (static_cast<size_t>(pos) * KVH + kvh) * kHD + 8 * c8);
-      const uint16_t *vh = reinterpret_cast<const uint16_t *>(&vv);
-#pragma unroll
-      for (uint32_t j = 0; j < 8; ++j) s.vt[8 * c8 + j][key] = vh[j];
-    }
-  };
   // scores of this warp's 16 rows x 64 keys: sc[n][c] = n-tile n (keys 8n..),
   // c0/c1 row gq keys 2tq, 2tq + 1; c2/c3 row gq + 8
-  auto scores = [&](uint32_t key0, float (&sc)[kTcKeys / 8][4]) {
+  auto scores = [&](uint32_t t, float (&sc)[kTcKeys / 8][4]) {
+    const uint32_t key0 = t * kTcKeys, b = t & 1;
 #pragma unroll
-    for (uint32_t n = 0; n < kTcKeys / 8; ++n) {
-      sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+    for (uint32_t n = 0; n < kTcKeys / 8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
 #pragma unroll
-      for (uint32_t kk = 0; kk < kHD / 16; ++kk)
-        mma_bf16(sc[n], qa[kk], lds32(&s.k[8 * n + gq][16 * kk + 2 * tq]), lds32(&s.k[8 * n + gq][16 * kk + 8 + 2 * tq]));
+    for (uint32_t kk = 0; kk < kHD / 16; ++kk)
+#pragma unroll
+      for (uint32_t n = 0; n < kTcKeys / 8; n += 2) {
+        uint32_t kb[4];  // b0/b1 of n-tiles n and n + 1
+        ldsm_x4(kb, &s.k[b][8 * n + k_row][16 * kk + k_col]);
+        mma_bf16(sc[n], qa[kk], kb[0], kb[1]);
+        mma_bf16(sc[n + 1], qa[kk], kb[2], kb[3]);
+      }
+#pragma unroll
+    for (uint32_t n = 0; n < kTcKeys / 8; ++n)
 #pragma unroll
       for (uint32_t c = 0; c < 4; ++c) {
         const uint32_t key = key0 + 8 * n + 2 * tq + (c & 1);
         sc[n][c] = key <= qpos[c >> 1] ? round_bf16(__fmul_rn(round_bf16(sc[n][c]), kAttnScale)) : -INFINITY;
       }
-    }
   };
   // pass 1: row max and sum of exp over the whole causal context
   float rm[2] = {-INFINITY, -INFINITY}, rl[2] = {0.f, 0.f};
-  for (uint32_t key0 = 0; key0 <= last; key0 += kTcKeys) {
-    __syncthreads();
-    stage(key0, false);
+  for (uint32_t t = 0; t < tiles; ++t) {
+    if (t + 1 < tiles) {
+      issue(t + 1, false);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
     __syncthreads();
     float sc[kTcKeys / 8][4];
-    scores(key0, sc);
+    scores(t, sc);
 #pragma unroll
     for (uint32_t h = 0; h < 2; ++h) {
       float m = -INFINITY;
@@ -251,32 +281,44 @@ __global__ void __launch_bounds__(TcAttn<G>::THREADS) k_pf_attention_tc(const ui
       rl[h] = (rm[h] == -INFINITY ? 0.f : rl[h] * expf(rm[h] - mn)) + l;
       rm[h] = mn;
     }
+    __syncthreads();  // buffer t & 1 is refilled by the next issue
   }
   const float inv[2] = {1.0f / rl[0], 1.0f / rl[1]};
   // pass 2: probabilities and p.v
   float o[kHD / 8][4];
 #pragma unroll
   for (uint32_t n = 0; n < kHD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-  for (uint32_t key0 = 0; key0 <= last; key0 += kTcKeys) {
-    __syncthreads();
-    stage(key0, true);
+  issue(0, true);
+  for (uint32_t t = 0; t < tiles; ++t) {
+    if (t + 1 < tiles) {
+      issue(t + 1, true);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
     __syncthreads();
     float sc[kTcKeys / 8][4];
-    scores(key0, sc);
+    scores(t, sc);
 #pragma unroll
     for (uint32_t n = 0; n < kTcKeys / 8; ++n)
 #pragma unroll
       for (uint32_t c = 0; c < 4; ++c)
         sc[n][c] = sc[n][c] == -INFINITY ? 0.f : round_bf16(__fmul_rn(expf(sc[n][c] - rm[c >> 1]), inv[c >> 1]));
+    const uint32_t b = t & 1;
 #pragma unroll
     for (uint32_t kk = 0; kk < kTcKeys / 16; ++kk) {
       const uint32_t pa[4] = {pack_bf16x2(sc[2 * kk][0], sc[2 * kk][1]), pack_bf16x2(sc[2 * kk][2], sc[2 * kk][3]),
                               pack_bf16x2(sc[2 * kk + 1][0], sc[2 * kk + 1][1]),
                               pack_bf16x2(sc[2 * kk + 1][2], sc[2 * kk + 1][3])};
 #pragma unroll
-      for (uint32_t n = 0; n < kHD / 8; ++n)
-        mma_bf16(o[n], pa, lds32(&s.vt[8 * n + gq][16 * kk + 2 * tq]), lds32(&s.vt[8 * n + gq][16 * kk + 8 + 2 * tq]));
+      for (uint32_t n = 0; n < kHD / 8; n += 2) {
+        uint32_t vb[4];  // b0/b1 of dim tiles n and n + 1
+        ldsm_x4_t(vb, &s.v[b][16 * kk + v_row][8 * n + v_col]);
+        mma_bf16(o[n], pa, vb[0], vb[1]);
+        mma_bf16(o[n + 1], pa, vb[2], vb[3]);
+      }
     }
+    __syncthreads();
   }
 #pragma unroll
   for (uint32_t h = 0; h < 2; ++h) {
@@ -301,14 +343,29 @@ cudaError_t launch_attn_tc(const uint16_t *q, const uint16_t *kc, const uint16_t
   return cudaGetLastError();
 }
 
-__global__ void k_pf_swiglu(const uint16_t *gu, uint16_t *h, uint32_t I, uint64_t total) {
-  for (uint64_t e = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; e < total;
-       e += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-    const uint64_t m = e / I, i = e % I;
-    const float g = bfv(gu, m * 2 * I + 2 * i), u = bfv(gu, m * 2 * I + 2 * i + 1);
-    const float act = round_bf16(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
-    h[e] = bfb(__fmul_rn(act, u));
+// Row blockIdx.y, outputs 8 v .. 8 v + 7 for v = blockIdx.x * blockDim.x +
+// threadIdx.x: two 16-byte loads of interleaved gate/up, one 16-byte store.
+__global__ void k_pf_swiglu(const uint16_t *gu, uint16_t *h, uint32_t I) {
+  const uint32_t v = blockIdx.x * blockDim.x + threadIdx.x;
+  if (8 * v >= I) return;
+  const size_t m = blockIdx.y;
+  const uint4 *src = reinterpret_cast<const uint4 *>(gu + m * 2 * I + 16 * static_cast<size_t>(v));
+  const uint4 w[2] = {src[0], src[1]};
+  const uint32_t *p = reinterpret_cast<const uint32_t *>(w);
+  uint32_t r[4];
+#pragma unroll
+  for (uint32_t j = 0; j < 4; ++j) {
+    float y[2];
+#pragma unroll
+    for (uint32_t e = 0; e < 2; ++e) {
+      const uint32_t pair = p[2 * j + e];  // (gate, up) of output 2 j + e
+      const float g = bf16_bits_to_float(pair & 0xffffu), u = bf16_bits_to_float(pair >> 16);
+      const float act = round_bf16(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+      y[e] = __fmul_rn(act, u);
+    }
+    r[j] = pack_bf16x2(y[0], y[1]);
   }
+  *reinterpret_cast<uint4 *>(h + m * I + 8 * static_cast<size_t>(v)) = make_uint4(r[0], r[1], r[2], r[3]);
 }
 
 // ------------------------------------------------ row-parallel exchange
@@ -510,8 +567,8 @@ cudaError_t prefill_attention(const uint16_t *q, const uint16_t *kc, const uint1
 }
 
 cudaError_t prefill_swiglu(const uint16_t *gu, uint16_t *h, uint32_t M, uint32_t I, cudaStream_t s) {
-  const uint64_t total = static_cast<uint64_t>(M) * I;
-  k_pf_swiglu<<<static_cast<uint32_t>(std::min<uint64_t>((total + 255) / 256, 148 * 16)), 256, 0, s>>>(gu, h, I, total);
+  if (I % 8 || !aligned16(gu) || !aligned16(h)) return cudaErrorInvalidValue;
+  k_pf_swiglu<<<dim3((I / 8 + 255) / 256, M), 256, 0, s>>>(gu, h, I);
   return cudaGetLastError();
 }
 
