@@ -272,16 +272,20 @@ def gemm_extra(torch, device, peak_tflops: float) -> dict:
     return out
 
 
-def batch_extra(torch, device, shape, context: int, batch: int, steps: int, warmup: int) -> dict:
+def batch_extra(torch, device, shape, context: int, batch: int, steps: int, warmup: int,
+                rank: int = 0, world: int = 1, group=None) -> dict:
     """Batched decode (BASELINE configs[4] at batch 16): `batch` sequences,
     each after its own seeded `context`-token prompt (prefilled by batched
     steps), timed over `steps` device-resident batched steps with CUDA
-    events; roofline = weights once + every sequence's K/V per step."""
+    events (max over ranks; tensor parallel over the ranks at N > 1);
+    roofline = this GPU's weights once + every sequence's K/V per step."""
     from xpu_playground_b200.qwen3 import Qwen3Engine
 
     max_seq = context + warmup + steps + 8
-    eng = Qwen3Engine(shape, max_seq, device=device.index or 0, max_batch=batch)
+    eng = Qwen3Engine(shape, max_seq, device=device.index or 0, tp_rank=rank, tp_size=world, max_batch=batch)
     eng.init_synthetic(WEIGHT_SEED)
+    if world > 1:
+        eng.connect_tensor_parallel(group)
     prompts = [seeded_prompt(context, shape.vocab, seed=7 + s) for s in range(batch)]
     eng.batch_generate(prompts, 1)  # prefill: context batched steps
     stream = torch.cuda.ExternalStream(eng.info().stream, device=device)
@@ -297,6 +301,11 @@ def batch_extra(torch, device, shape, context: int, batch: int, steps: int, warm
     _, pos1, err = eng.batch_state(batch)
     if err:
         raise SystemExit(f"batched decode error word {err}")
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     mid = (pos0[0] + pos1[0]) // 2
     nbytes = eng.batch_bytes_per_step(batch, mid)
     peak, kind = measured_peaks()
@@ -304,7 +313,7 @@ def batch_extra(torch, device, shape, context: int, batch: int, steps: int, warm
         "workload": f"{shape.layers}-layer {shape.hidden}-hidden greedy decode, batch {batch}, "
                     f"{context}-token prompt per sequence",
         "value": round(batch * 1000.0 / ms, 1), "unit": "tok/s", "ms_per_step": round(ms, 4),
-        "steps": steps, "context_tokens": [pos0[0], pos1[0]],
+        "steps": steps, "context_tokens": [pos0[0], pos1[0]], "n_gpus": world,
         "kernels_per_step": eng.batch_kernels_per_step(),
         "roofline": {"bound": "hbm", "algorithmic_bytes_per_step": nbytes,
                      "achieved": round(nbytes / (ms * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
@@ -426,8 +435,10 @@ def run_ours(args) -> None:
     mode = args.mode if world == 1 else "persistent"  # tensor parallel runs the persistent step
     eng = Qwen3Engine(shape, max_seq, device=local, tp_rank=rank, tp_size=world, mode=mode)
     eng.init_synthetic(WEIGHT_SEED)
+    tp_group = None
     if world > 1:
-        eng.connect_tensor_parallel(dist.new_group(backend="gloo"))
+        tp_group = dist.new_group(backend="gloo")
+        eng.connect_tensor_parallel(tp_group)
     prompt = seeded_prompt(args.context, shape.vocab)
     chunked = None
     if world == 1:
@@ -525,10 +536,11 @@ def run_ours(args) -> None:
     if not args.no_small and world == 1:
         eng.synchronize()
         extra["qwen3_0p6b_decode"] = small_extra(torch, device, warmup=max(W, 3))
-    if args.batch and world == 1:
+    if args.batch:
         eng.synchronize()
         extra["batch_decode"] = batch_extra(torch, device, shape, args.context, args.batch,
-                                            steps=min(K, 64), warmup=max(W, 3))
+                                            steps=min(K, 64), warmup=max(W, 3), rank=rank, world=world,
+                                            group=tp_group)
     if not args.no_gemv:
         eng.synchronize()
         extra.update(gemv_extra(torch, device, rank, world))

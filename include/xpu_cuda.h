@@ -309,6 +309,16 @@ uint64_t xpu_qwen3_bytes_per_token(xpu_qwen3_engine *engine, uint32_t context);
  * batch-1 arithmetic. xpu_qwen3_create_batched makes a single-GPU engine
  * whose KV cache holds max_batch sequences (sequence 0 is the one the
  * batch-1 calls above use); every engine accepts batch 1.
+ * xpu_qwen3_create_batched_tp makes one rank of a tensor-parallel batched
+ * engine (connect it with xpu_qwen3_tp_connect like the batch-1 engine;
+ * every rank then makes the same batch calls): each rank streams its shard
+ * of the weights, o_proj and down partials are summed across the ranks in
+ * rank order through the exchange regions, the lm_head candidates of every
+ * sequence meet the same way, and every rank returns the same tokens.
+ * Unlike the batch-1 path the row-parallel sums are not in a fixed order
+ * shared with one GPU, so logits match one GPU within rounding, not bit
+ * for bit. xpu_qwen3_batch_logits then returns this rank's vocabulary
+ * shard.
  *
  * xpu_qwen3_batch_decode: one synchronous step of sequences 0..batch-1,
  *   tokens[s] at positions[s] -> next_tokens[s]; XPU_ERR_NONFINITE if any
@@ -348,6 +358,8 @@ int xpu_qwen3_prefill_dense(xpu_qwen3_engine *engine, const uint32_t *prompt, ui
                             uint32_t *next_token);
 int xpu_qwen3_create_batched(const xpu_qwen3_shape *shape, uint32_t maximum_sequence, int device,
                              uint32_t max_batch, xpu_qwen3_engine **out);
+int xpu_qwen3_create_batched_tp(const xpu_qwen3_shape *shape, uint32_t maximum_sequence, int device,
+                                uint32_t tp_rank, uint32_t tp_size, uint32_t max_batch, xpu_qwen3_engine **out);
 int xpu_qwen3_batch_decode(xpu_qwen3_engine *engine, uint32_t batch, const uint32_t *tokens,
                            const uint32_t *positions, uint32_t *next_tokens);
 int xpu_qwen3_batch_generate(xpu_qwen3_engine *engine, uint32_t batch, const uint32_t *prompts,

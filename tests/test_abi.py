@@ -74,11 +74,10 @@ def test_batched_byte_model_without_engine():
     assert L.xpu_qwen3_batch_kernels_per_step(None) == 0
 
 
-def test_python_engine_refuses_batched_tensor_parallel():
-    from xpu_playground_b200.qwen3 import Qwen3Engine
-    from xpu_playground_b200.qwen3_config import PRESETS
-    with pytest.raises(ValueError, match="one GPU"):
-        Qwen3Engine(PRESETS["tiny"], 16, tp_rank=0, tp_size=2, max_batch=4)
+def test_batched_tensor_parallel_create_checks_arguments():
+    L = _lib.load()
+    # null shape / output pointer: refused before any device work
+    assert L.xpu_qwen3_create_batched_tp(None, 16, 0, 0, 2, 4, None) == _lib.XPU_ERR_INVALID
 
 
 def test_attention_group_sizes():

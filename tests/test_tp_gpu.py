@@ -155,6 +155,76 @@ def test_tp_dense_prefill_matches_single_gpu(preset, world, plen):
         assert np.array_equal(last, ref_last[part]), f"rank {rank} decode logits differ"
 
 
+BATCH_SEQS, BATCH_STEPS = 4, 20
+
+
+def _batch_streams(vocab):
+    return [prompt_ids(BATCH_STEPS, vocab, seed=30 + s) for s in range(BATCH_SEQS)]
+
+
+def _batch_run(eng, streams, shard):
+    """Teacher-forced batched steps: at step t sequence s reads streams[s][t]
+    at position t + s (different positions per sequence). Returns every
+    step's greedy tokens and logits (this rank's shard)."""
+    toks, logits = [], []
+    for t in range(BATCH_STEPS):
+        toks.append(eng.batch_decode([streams[s][t] for s in range(BATCH_SEQS)],
+                                     [t + s for s in range(BATCH_SEQS)]))
+        logits.append(np.stack([eng.batch_logits(s)[:shard] for s in range(BATCH_SEQS)]))
+    return toks, logits
+
+
+def _rank_batch(rank, world, port, preset, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        shape = PRESETS[preset]
+        eng = Qwen3Engine(shape, MAX_SEQ, device=rank, tp_rank=rank, tp_size=world, max_batch=BATCH_SEQS)
+        eng.init_synthetic(SEED)
+        eng.connect_tensor_parallel()
+        q.put((rank, _batch_run(eng, _batch_streams(shape.vocab), shape.vocab // world), None))
+        dist.barrier()
+        eng.close()
+    except Exception as e:
+        q.put((rank, repr(e), None))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("preset,world", [("tiny", 2), ("qwen3-8b-l2", 2), ("qwen3-0.6b", 4), ("qwen3-8b-l2", 8)])
+def test_tp_batched_decode_matches_single_gpu(preset, world):
+    """Batched decode (4 sequences, each at its own position) under tensor
+    parallelism against the one-GPU batched engine on the same inputs: the
+    row-parallel partials are summed in rank order rather than in one
+    GPU's order, so every step's logits must agree within the full-logit
+    gates of the fixture tests, and the greedy tokens must be equal except
+    where one GPU's top two logits are within two bf16 steps."""
+    if NGPU < world:
+        pytest.skip(f"needs {world} GPUs")
+    from tests.test_engine_gpu import FULL_MAXABS, FULL_MEANABS, near_tie
+    shape = PRESETS[preset]
+    streams = _batch_streams(shape.vocab)
+    with Qwen3Engine(shape, MAX_SEQ, device=0, max_batch=BATCH_SEQS) as eng:
+        eng.init_synthetic(SEED)
+        ref_toks, ref_logits = _batch_run(eng, streams, shape.vocab)
+    results = _run_ranks(_rank_batch, world, preset)
+    shard = shape.vocab // world
+    f = __import__("oracle.oracle", fromlist=["bf16_to_float"]).bf16_to_float
+    for rank in range(world):
+        got, _ = results[rank]
+        assert not isinstance(got, str), got
+        toks, logits = got
+        for t in range(BATCH_STEPS):
+            e = f(ref_logits[t][:, rank * shard:(rank + 1) * shard]).astype(np.float64)
+            d = np.abs(f(logits[t]).astype(np.float64) - e)
+            assert d.max() <= FULL_MAXABS and d.mean() <= FULL_MEANABS, (rank, t, d.max(), d.mean())
+            for s in range(BATCH_SEQS):
+                if toks[t][s] != ref_toks[t][s]:
+                    assert near_tie(ref_logits[t][s], toks[t][s], ref_toks[t][s]), (rank, t, s)
+
+
 def test_tp_loads_checkpoint_shards(tmp_path):
     """Each rank streams only its shards of a sharded safetensors checkpoint;
     tp=2 then matches one GPU on the same weights."""

@@ -93,6 +93,7 @@ SIGNATURES: dict[str, tuple] = {
     "xpu_qwen3_info": (i32, [vp, vp]),
     "xpu_qwen3_bytes_per_token": (u64, [vp, u32]),
     "xpu_qwen3_create_batched": (i32, [vp, u32, i32, u32, vp]),
+    "xpu_qwen3_create_batched_tp": (i32, [vp, u32, i32, u32, u32, u32, vp]),
     "xpu_qwen3_prefill": (i32, [vp, vp, u32, vp]),
     "xpu_qwen3_prefill_dense": (i32, [vp, vp, u32, vp]),
     "xpu_qwen3_batch_decode": (i32, [vp, u32, vp, vp, vp]),

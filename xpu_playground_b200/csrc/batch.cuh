@@ -61,7 +61,30 @@ struct BatchDims {
   uint32_t trace_slot;     // this launch's slot in BatchBuffers::trace
   uint32_t seq_rows;       // cache rows between two sequences: max_seq, or 0 when
                            // every sequence is a position of one prompt (prefill)
+  uint32_t tp, rank;       // tensor parallel size and this rank (1, 0 on one GPU)
+  uint32_t v_offset;       // first vocabulary row of this rank's lm_head shard
+  uint32_t layers;         // decoder layers (exchanges per step: 2 layers + 1)
 };
+
+// Tensor-parallel batched step (tp > 1): QKV, gate/up and the lm_head rows
+// are split over the ranks like the batch-1 engine's, o_proj and down over
+// their K. Each rank's o_proj / down GEMM writes its FP32 partial Y_r[16][H]
+// into its exchange region; once every rank has published the exchange's
+// epoch, each rank sums the ranks' partials in rank order and applies the
+// residual (x = bf16(x + bf16(sum))) and the per-tile sums of x^2 itself. The
+// lm_head candidates of every sequence meet the same way. Exchange k (1-based)
+// of a step has epoch *xepoch + k; a kernel after the step's argmax adds
+// 2 layers + 1, so epochs only grow. Region layout behind the dense prefill
+// exchange (decode.cuh): flag[2] (o_proj, down), lm[kMaxTp][16] LmSlot at
+// kBatchLmOffset, part[2][16][H] FP32 at kBatchPartOffset.
+constexpr size_t kBatchLmOffset = 256;
+constexpr size_t kBatchPartOffset = 8192;
+inline size_t batch_region_offset(uint32_t H, uint32_t prefill_cap) {
+  return (pf_region_end(H, prefill_cap) + 4095) / 4096 * 4096;
+}
+inline size_t batch_region_end(uint32_t H, uint32_t prefill_cap) {
+  return batch_region_offset(H, prefill_cap) + kBatchPartOffset + 2ull * kMaxBatch * H * sizeof(float);
+}
 
 struct BatchBuffers {
   bf16 *x;              // [16][H] residual stream
@@ -92,6 +115,11 @@ struct BatchBuffers {
   // Step tracing (XPU_BATCH_TRACE=1, else null): per kernel of the step
   // [slot][8] globaltimer ns (see trace_mark in batch_step.cu).
   unsigned long long *trace;
+  // tensor parallel (tp > 1): rank q's exchange region parts
+  float *xpart[kMaxTp];               // [2][16][H] FP32 partials (o_proj, down)
+  unsigned long long *xflag[kMaxTp];  // [2] published epochs
+  LmSlot *xlm[kMaxTp];                // [kMaxTp][16] lm_head candidates (slot [rank][sequence])
+  unsigned long long *xepoch;         // this rank's exchanges before the current step
 };
 
 constexpr uint32_t kBatchTraceSlots = 512;

@@ -87,13 +87,14 @@ constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((kSeqN >> 3) <
 
 static_assert(kStageBytes % 1024 == 0, "swizzled stages stay 1024-byte aligned");
 
-enum Epi : int { kEpiQkv = 0, kEpiResid = 1, kEpiGateUp = 2, kEpiLm = 3 };
+enum Epi : int { kEpiQkv = 0, kEpiResid = 1, kEpiGateUp = 2, kEpiLm = 3, kEpiPart = 4 };
 
 struct BGemm {
   uint32_t rows, nk, tiles, total;  // weight rows, K blocks per tile, tiles, tiles * nk
   BatchDims d;
   BatchBuffers b;
   bf16 *out;                    // residual x (kEpiResid), h (kEpiGateUp) or raw qkv (kEpiQkv)
+  float *part;                  // kEpiPart: this rank's FP32 partial [16][rows] (tensor parallel)
   const bf16 *norm_w;           // normalising GEMMs: the RMSNorm weight of the operand
 };
 
@@ -167,6 +168,14 @@ __device__ inline void epi_qkv(const BGemm &p, uint32_t row, const float (&v)[kS
     if (s < p.d.batch) putv(p.out, static_cast<size_t>(s) * p.rows + row, v[s]);
 }
 
+// Tensor parallel o_proj / down: this rank's unrounded partial sums.
+__device__ inline void epi_part(const BGemm &p, uint32_t row, const float (&v)[kSeqN]) {
+  if (row >= p.rows) return;
+#pragma unroll
+  for (uint32_t s = 0; s < kSeqN; ++s)
+    if (s < p.d.batch) p.part[static_cast<size_t>(s) * p.rows + row] = v[s];
+}
+
 // x[s][row] = bf16(x[s][row] + bf16(sum)) with x[s][row] preloaded in xr;
 // the tile's sum of x^2 per sequence (lanes by a transpose reduction, then
 // quarters in order) goes to ssq[tile][s] for the next normalising GEMM.
@@ -214,7 +223,7 @@ __device__ inline void epi_lm(const BGemm &p, uint32_t t, uint32_t row, const fl
     const float lv = round_bf16(v[s]);
     if (ok && s < p.d.batch) p.b.logits[static_cast<size_t>(s) * p.rows + row] = float_to_bf16_bits(lv);
     const bool bad = ok && not_finite(lv);
-    ArgBest cb = (ok && !bad) ? ArgBest{lv, row} : ArgBest{-INFINITY, 0xffffffffu};
+    ArgBest cb = (ok && !bad) ? ArgBest{lv, p.d.v_offset + row} : ArgBest{-INFINITY, 0xffffffffu};
     cb = warp_argbest(cb);
     const uint32_t anybad = __any_sync(kFullMask, bad) ? 1u : 0u;
     if (lane == 0) { es.best[quarter][s] = cb; es.bad[quarter][s] = anybad; }
@@ -238,6 +247,7 @@ __device__ __forceinline__ void run_epilogue(const BGemm &p, uint32_t t, uint32_
   if (EPI == kEpiResid) epi_resid(p, t, row, v, xr, es, par);
   if (EPI == kEpiGateUp) epi_gateup(p, row, v);
   if (EPI == kEpiLm) epi_lm(p, t, row, v, es);
+  if (EPI == kEpiPart) epi_part(p, row, v);
 }
 
 __device__ __forceinline__ bool failed_now(const int *f) { return *reinterpret_cast<const volatile int *>(f) != 0; }
@@ -1432,6 +1442,108 @@ k_battn_tc(BatchDims bd, BatchBuffers bb, LayerWeights w, const __grid_constant_
 // Per sequence: the lm tiles' candidates in tile order -> greedy token
 // (lowest index on ties; 0xffffffff when any logit was NaN/Inf), then the
 // state advances one position.
+// ---------------------------------------------- tensor-parallel exchange
+constexpr long long kBxWaitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
+
+__device__ __forceinline__ unsigned long long bx_ld_acquire(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void bx_st_release(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void bx_st_relaxed(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// One thread: bounded wait until *flag(q) >= epoch for q < n (flags `stride`
+// 64-bit words apart from base[q]); false on a timeout.
+__device__ bool bx_wait(const unsigned long long *const *base, uint32_t offset, uint32_t n, unsigned long long epoch) {
+  const long long start = clock64();
+  for (uint32_t q = 0; q < n; ++q)
+    while (bx_ld_acquire(base[q] + offset) < epoch) {
+      if (clock64() - start > kBxWaitCycles) return false;
+      __nanosleep(64);
+    }
+  return true;
+}
+
+// Exchange k of the step (which: 0 o_proj, 1 down) is published: this rank's
+// partial (written by the GEMM before this kernel) is visible to the peers.
+__global__ void k_bsignal(BatchDims d, BatchBuffers b, uint32_t which, uint32_t k) {
+  __threadfence_system();
+  bx_st_release(b.xflag[d.rank] + which, *b.xepoch + k);
+}
+
+// Tile blockIdx.x of H (128 rows, one thread each): once every rank's
+// partial of exchange k is published, x = bf16(x + bf16(partials summed in
+// rank order)) and the tile's sums of x^2 per sequence, as the residual
+// epilogue leaves them.
+__global__ void __launch_bounds__(kTileM) k_bxchg(BatchDims d, BatchBuffers b, uint32_t which, uint32_t k) {
+  __shared__ int ok;
+  __shared__ float part_ssq[4][kSeqN];
+  const uint32_t t = blockIdx.x, r = threadIdx.x, row = t * kTileM + r, lane = r & 31, quarter = r >> 5;
+  if (r == 0) {
+    ok = bx_wait(b.xflag, which, d.tp, *b.xepoch + k) ? 1 : 0;
+    if (!ok) atomicOr(b.error, 4u);
+  }
+  __syncthreads();
+  if (!ok) return;
+  const size_t slot = static_cast<size_t>(which) * kMaxBatch * d.H;
+  float sq[kSeqN];
+#pragma unroll
+  for (uint32_t s = 0; s < kSeqN; ++s) {
+    sq[s] = 0.f;
+    if (s < d.batch) {
+      const size_t i = static_cast<size_t>(s) * d.H + row;
+      float v = __ldcg(b.xpart[0] + slot + i);
+      for (uint32_t q = 1; q < d.tp; ++q) v = __fadd_rn(v, __ldcg(b.xpart[q] + slot + i));
+      const float xn = round_bf16(__fadd_rn(bfv(b.x, i), round_bf16(v)));
+      putv(b.x, i, xn);
+      sq[s] = __fmul_rn(xn, xn);
+    }
+  }
+  warp_transpose_sum<kSeqN>(sq, lane);  // lanes 2s, 2s + 1: the warp's sum for sequence s
+  if ((lane & 1) == 0) part_ssq[quarter][lane / 2] = sq[0];
+  __syncthreads();
+  if (r < kSeqN)
+    b.ssq[t * kSeqN + r] = ((part_ssq[0][r] + part_ssq[1][r]) + part_ssq[2][r]) + part_ssq[3][r];
+}
+
+// Sequence s's greedy candidate across the ranks' vocabulary shards: each
+// rank writes its candidate into slot [rank][s] of every rank's region,
+// then combines slot [q][s] of its own for every q (global indices, lowest
+// on ties). One thread; false on a timeout.
+__device__ bool bx_pick(const BatchDims &d, const BatchBuffers &b, uint32_t s, ArgBest &best, uint32_t &bad) {
+  const unsigned long long epoch = *b.xepoch + 2ull * d.layers + 1;
+  for (uint32_t q = 0; q < d.tp; ++q) {
+    LmSlot *slot = b.xlm[q] + d.rank * kMaxBatch + s;
+    slot->value = best.value;
+    slot->index = best.index;
+    slot->bad = bad;
+  }
+  __threadfence_system();
+  for (uint32_t q = 0; q < d.tp; ++q) bx_st_relaxed(&(b.xlm[q] + d.rank * kMaxBatch + s)->epoch, epoch);
+  const LmSlot *own = b.xlm[d.rank];
+  const long long start = clock64();
+  for (uint32_t q = 0; q < d.tp; ++q)
+    while (bx_ld_acquire(&own[q * kMaxBatch + s].epoch) < epoch) {
+      if (clock64() - start > kBxWaitCycles) return false;
+      __nanosleep(64);
+    }
+  best = ArgBest{-INFINITY, 0xffffffffu};
+  bad = 0;
+  for (uint32_t q = 0; q < d.tp; ++q) {
+    best = arg_better(best, ArgBest{__ldcg(&own[q * kMaxBatch + s].value), __ldcg(&own[q * kMaxBatch + s].index)});
+    bad |= __ldcg(&own[q * kMaxBatch + s].bad);
+  }
+  return true;
+}
+
+// After the step's argmax: the step's exchanges are done.
+__global__ void k_bepoch(BatchBuffers b, uint32_t exchanges) { *b.xepoch += exchanges; }
+
 __global__ void __launch_bounds__(256) k_bargmax(BatchDims d, BatchBuffers b, uint32_t tiles) {
   __shared__ ArgBest wb[8];
   __shared__ uint32_t wbad[8];
@@ -1454,6 +1566,7 @@ __global__ void __launch_bounds__(256) k_bargmax(BatchDims d, BatchBuffers b, ui
     ArgBest fb = wb[0];
     uint32_t fbad = wbad[0];
     for (int i = 1; i < 8; ++i) { fb = arg_better(fb, wb[i]); fbad |= wbad[i]; }
+    if (d.tp > 1 && !bx_pick(d, b, s, fb, fbad)) atomicOr(b.error, 4u);
     const uint32_t next = (fbad || fb.index == 0xffffffffu) ? 0xffffffffu : fb.index;
     if (next == 0xffffffffu) atomicOr(b.error, 1u);
     SeqState &st = b.seq[s];
@@ -1635,6 +1748,19 @@ cudaError_t record_batch_step(const BatchDims &d0, const BatchBuffers &b, const 
     return d;
   };
   const uint32_t G = d.QH / d.KVH;
+  if (d.tp > 1 && (prefill || d.H % kTileM)) return cudaErrorInvalidValue;
+  // Tensor parallel o_proj / down: the partial GEMM into this rank's region,
+  // the epoch published, then every rank's partials applied to x.
+  auto exchange = [&](uint32_t which, uint32_t k, const bf16 *W, uint32_t K, const bf16 *X) -> cudaError_t {
+    BGemm pp{};
+    pp.part = b.xpart[d.rank] + static_cast<size_t>(which) * kMaxBatch * d.H;
+    cudaError_t e = launch_bgemm<kEpiPart>(W, d.H, K, X, at(pp), s);
+    if (e != cudaSuccess) return e;
+    k_bsignal<<<1, 1, 0, s>>>(next(), b, which, k);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    k_bxchg<<<d.H / kTileM, kTileM, 0, s>>>(next(), b, which, k);
+    return cudaGetLastError();
+  };
 #define XPU_TRY(expr)                        \
   do {                                       \
     const cudaError_t e_ = (expr);           \
@@ -1660,19 +1786,30 @@ cudaError_t record_batch_step(const BatchDims &d0, const BatchBuffers &b, const 
     }
     BGemm po{};
     po.out = b.x;
-    XPU_TRY(launch_bgemm<kEpiResid>(w.wo, d.H, d.QH * kHD, b.attn, at(po), s));
+    if (d.tp > 1)
+      XPU_TRY(exchange(0, 2 * l + 1, w.wo, d.QH * kHD, b.attn));
+    else
+      XPU_TRY(launch_bgemm<kEpiResid>(w.wo, d.H, d.QH * kHD, b.attn, at(po), s));
     BGemm pg{};
     pg.out = b.h;
     pg.norm_w = w.post_norm;
     XPU_TRY((launch_bgemm<kEpiGateUp, true>(w.wgu, 2 * d.I, d.H, b.x, at(pg), s)));
     BGemm pd{};
     pd.out = b.x;
-    XPU_TRY(launch_bgemm<kEpiResid>(w.wd, d.H, d.I, b.h, at(pd), s));
+    if (d.tp > 1)
+      XPU_TRY(exchange(1, 2 * l + 2, w.wd, d.I, b.h));
+    else
+      XPU_TRY(launch_bgemm<kEpiResid>(w.wd, d.H, d.I, b.h, at(pd), s));
   }
   BGemm pl{};
   pl.norm_w = b.final_norm;
   XPU_TRY((launch_bgemm<kEpiLm, true>(b.lm_head, d.vocab, d.H, b.x, at(pl), s)));
   XPU_TRY(launch_pdl(k_bargmax, dim3(d.batch), dim3(256), 0, s, next(), b, batch_lm_tiles(d.vocab)));
+  if (d.tp > 1) {
+    next();
+    k_bepoch<<<1, 1, 0, s>>>(b, 2 * n_layers + 1);
+    XPU_TRY(cudaGetLastError());
+  }
 #undef XPU_TRY
   return cudaSuccess;
 }

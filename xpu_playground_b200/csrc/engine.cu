@@ -785,25 +785,31 @@ class Qwen3Engine {
   void batch_logits(uint32_t seq, uint16_t *host, uint32_t count) {
     if (seq >= kMaxBatch) throw InvalidArg("sequence index outside the batch (16 rows)");
     if (!bb_.logits) throw InvalidArg("no batched step has run");
-    if (count > shape_.vocab_size) throw InvalidArg("logit count exceeds the vocabulary");
-    CK(cudaMemcpyAsync(host, bb_.logits + static_cast<size_t>(seq) * shape_.vocab_size, count * 2ull,
+    if (count > bd_.vocab) throw InvalidArg("logit count exceeds the vocabulary rows of this rank");
+    CK(cudaMemcpyAsync(host, bb_.logits + static_cast<size_t>(seq) * bd_.vocab, count * 2ull,
                        cudaMemcpyDeviceToHost, stream_));
     CK(cudaStreamSynchronize(stream_));
   }
 
-  // embed + norm, 5 per layer (qkv, attention, o_proj, gate/up, down), lm_head, argmax
-  uint32_t batch_kernels_per_step() const { return 5 * shape_.num_hidden_layers + 3; }
+  // embed + norm, 5 per layer (qkv, attention, o_proj, gate/up, down), lm_head,
+  // argmax; tensor parallel: + 2 per row-parallel GEMM (publish, exchange) and
+  // the epoch update
+  uint32_t batch_kernels_per_step() const {
+    return tp_ > 1 ? 9 * shape_.num_hidden_layers + 4 : 5 * shape_.num_hidden_layers + 3;
+  }
 
   // Bytes one batched step of n sequences must move: the weights once, plus
   // every sequence's K and V over `context` positions.
   uint64_t batch_bytes_per_step(uint32_t n, uint32_t context) const {
-    const uint64_t kv = 2ull * shape_.num_hidden_layers * shape_.num_key_value_heads * 128 * 2;
+    const uint64_t kv = 2ull * shape_.num_hidden_layers * d_.KVH_l * 128 * 2;
     return bytes_per_token(0) + static_cast<uint64_t>(n) * kv * context;
   }
 
  private:
   void check_batch(uint32_t n) const {
-    if (tp_ > 1) throw InvalidArg("batched decode runs on one GPU (tp_size 1)");
+    if (broken_)
+      throw InvalidArg("a tensor-parallel exchange timed out earlier: destroy and recreate the engines on every rank");
+    if (tp_ > 1 && !connected_) throw InvalidArg("tensor-parallel engine not connected: call xpu_qwen3_tp_connect");
     if (n < 1 || n > batch_cap_)
       throw InvalidArg("batch of " + std::to_string(n) + " sequences outside [1, " + std::to_string(batch_cap_) +
                        "] (the engine's batch capacity)");
@@ -825,6 +831,7 @@ class Qwen3Engine {
   // error word) before reporting, so the next call starts clean.
   void after_batch_check() {
     const uint32_t err = *host_berr_;
+    if ((err & 4u) && tp_ > 1) broken_ = true;  // the ranks' exchange epochs may now disagree
     if (err & 4u) {
       CK(cudaMemsetAsync(bb_.cnt_tile, 0, batch_max_tiles(bd_) * sizeof(unsigned), stream_));
       CK(cudaMemsetAsync(bb_.cnt_attn, 0, kMaxBatch * bd_.KVH * sizeof(unsigned), stream_));
@@ -846,10 +853,14 @@ class Qwen3Engine {
     const auto &s = shape_;
     bd_ = BatchDims{};
     bd_.H = s.hidden_size;
-    bd_.I = s.intermediate_size;
-    bd_.QH = s.num_attention_heads;
-    bd_.KVH = s.num_key_value_heads;
-    bd_.vocab = s.vocab_size;
+    bd_.I = d_.I_l;  // this rank's share (everything on one GPU)
+    bd_.QH = d_.QH_l;
+    bd_.KVH = d_.KVH_l;
+    bd_.vocab = d_.V_l;
+    bd_.tp = tp_;
+    bd_.rank = rank_;
+    bd_.v_offset = d_.v_offset;
+    bd_.layers = s.num_hidden_layers;
     bd_.max_seq = max_seq_;
     bd_.nchunks = pos_chunks(max_seq_);
     bd_.batch = 1;
@@ -885,6 +896,16 @@ class Qwen3Engine {
     b.final_norm = reinterpret_cast<const bf16 *>(final_norm_);
     b.lm_head = reinterpret_cast<const bf16 *>(lm_head_);
     b.kv_seq_stride = static_cast<uint64_t>(max_seq_) * bd_.KVH * 128;
+    if (tp_ > 1) {
+      const size_t off = batch_region_offset(static_cast<uint32_t>(H), prefill_cap());
+      for (uint32_t q = 0; q < tp_; ++q) {
+        uint8_t *base = region_base_[q] + off;
+        b.xflag[q] = reinterpret_cast<unsigned long long *>(base);
+        b.xlm[q] = reinterpret_cast<LmSlot *>(base + kBatchLmOffset);
+        b.xpart[q] = reinterpret_cast<float *>(base + kBatchPartOffset);
+      }
+      b.xepoch = dev_zeros<unsigned long long>(1);
+    }
     const char *trace_env = std::getenv("XPU_BATCH_TRACE");
     if (trace_env && trace_env[0] == '1') {
       b.trace = dev_alloc<unsigned long long>(kBatchTraceSlots * kBatchTraceValues);
@@ -993,7 +1014,6 @@ class Qwen3Engine {
     req(s.intermediate_size % (64 * tp_) == 0, "intermediate_size / tp must be a multiple of 64");
     req(s.vocab_size % tp_ == 0 && (s.vocab_size / tp_) % 2 == 0, "vocabulary must split evenly");
     req(batch_cap_ >= 1 && batch_cap_ <= kMaxBatch, "batch capacity must be in [1, 16]");
-    req(tp_ == 1 || batch_cap_ == 1, "batched decode runs on one GPU (tp_size 1)");
   }
 
   void plan() {
@@ -1078,8 +1098,9 @@ class Qwen3Engine {
     b_.x = dev_alloc<bf16>(H);
     b_.x2 = dev_alloc<bf16>(H);
     if (tp_ > 1) {
-      // decode exchange, then the dense prefill exchange of one segment
-      const size_t bytes = pf_region_end(static_cast<uint32_t>(H), prefill_cap());
+      // decode exchange, the dense prefill exchange of one segment, the
+      // batched step's exchange (every engine accepts batch 1)
+      const size_t bytes = batch_region_end(static_cast<uint32_t>(H), prefill_cap());
       xregion_ = dev_alloc<uint8_t>(bytes);
       CK(cudaMemset(xregion_, 0, bytes));
     }
@@ -1336,6 +1357,17 @@ int xpu_qwen3_create_batched(const xpu_qwen3_shape *shape, uint32_t maximum_sequ
     *out = nullptr;
     auto holder = std::make_unique<xpu_qwen3_engine>();
     holder->impl = std::make_unique<Qwen3Engine>(*shape, maximum_sequence, device, 0, 1, max_batch);
+    *out = holder.release();
+  });
+}
+
+int xpu_qwen3_create_batched_tp(const xpu_qwen3_shape *shape, uint32_t maximum_sequence, int device,
+                                uint32_t tp_rank, uint32_t tp_size, uint32_t max_batch, xpu_qwen3_engine **out) {
+  return guarded([&] {
+    if (!shape || !out) throw xpu::InvalidArg("xpu_qwen3_create_batched_tp: null pointer");
+    *out = nullptr;
+    auto holder = std::make_unique<xpu_qwen3_engine>();
+    holder->impl = std::make_unique<Qwen3Engine>(*shape, maximum_sequence, device, tp_rank, tp_size, max_batch);
     *out = holder.release();
   });
 }

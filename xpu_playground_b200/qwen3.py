@@ -66,9 +66,10 @@ class Qwen3Engine:
         self.shape, self.max_seq, self.max_batch = shape, max_seq, max_batch
         self._h = ctypes.c_void_p()
         self._shape_c = shape_struct(shape)
-        if max_batch != 1:
-            if tp_size != 1:
-                raise ValueError("batched decode runs on one GPU (tp_size 1)")
+        if max_batch != 1 and tp_size != 1:
+            _lib.check(self.lib.xpu_qwen3_create_batched_tp(ctypes.byref(self._shape_c), max_seq, device, tp_rank,
+                                                            tp_size, max_batch, ctypes.byref(self._h)))
+        elif max_batch != 1:
             _lib.check(self.lib.xpu_qwen3_create_batched(ctypes.byref(self._shape_c), max_seq, device,
                                                          max_batch, ctypes.byref(self._h)))
         else:
@@ -248,7 +249,9 @@ class Qwen3Engine:
         return [int(x) for x in tok], [int(x) for x in pos], err.value
 
     def batch_logits(self, sequence: int) -> np.ndarray:
-        out = np.empty(self.shape.vocab, np.uint16)
+        """Sequence `sequence`'s logits of the last batched step (this rank's
+        vocabulary shard under tensor parallelism)."""
+        out = np.empty(self.info().vocab_rows, np.uint16)
         _lib.check(self.lib.xpu_qwen3_batch_logits(self._h, sequence, out.ctypes.data, out.size))
         return out
 
