@@ -112,6 +112,14 @@ def test_set_tensor_equals_init_synthetic():
 # over 256 steps): it is held to the floor plus ~10%.
 FULL_MAXABS, FULL_MEANABS, TOP_MAXABS = 0.06, 0.0105, 0.052
 
+# Paths whose projections accumulate on the tensor cores (TMEM: the batched
+# step's GEMMs, the dense prefill) carry more FP32 rounding than the decode
+# GEMVs' FMA chains: against the C restatement on the 8B shapes the dense
+# prefill's distance is 1.33x the decode path's in max-abs, 1.21x in
+# mean-abs and 1.17x in relative L2 (tests/test_prefill_dense_gpu.py). Their
+# gates are the ones above scaled by TC_SCALE.
+TC_SCALE = 1.25
+
 
 @pytest.mark.parametrize("fixture", ["hf_tiny.npz", "hf_tiny-tied.npz", "hf_qwen3-0p6b.npz",
                                      "hf_qwen3-8b-l2.npz"])

@@ -53,7 +53,7 @@ struct SeqState {
 
 struct BatchDims {
   uint32_t H, I, QH, KVH;  // hidden, intermediate, query heads, kv heads
-  uint32_t vocab;
+  uint32_t vocab;           // lm_head rows of this rank (the whole vocabulary on one GPU)
   uint32_t max_seq;
   uint32_t nchunks;        // attention position chunks of max_seq
   uint32_t batch;          // active sequences (1..16)
@@ -63,6 +63,7 @@ struct BatchDims {
                            // every sequence is a position of one prompt (prefill)
   uint32_t tp, rank;       // tensor parallel size and this rank (1, 0 on one GPU)
   uint32_t v_offset;       // first vocabulary row of this rank's lm_head shard
+  uint32_t tokens;         // the whole vocabulary (valid token ids)
   uint32_t layers;         // decoder layers (exchanges per step: 2 layers + 1)
 };
 

@@ -586,7 +586,7 @@ __global__ void __launch_bounds__(256) k_bnorm(BatchDims d, BatchBuffers b, cons
   if (embed) {
     const SeqState st = b.seq[s];
     uint32_t tok = st.position < st.prompt_len ? b.prompt[static_cast<size_t>(s) * d.max_seq + st.position] : st.token;
-    if (tok >= d.vocab) {  // a NaN step's sentinel or a bad id: read row 0, flag the batch
+    if (tok >= d.tokens) {  // a NaN step's sentinel or a bad id: read row 0, flag the batch
       if (t == 0) atomicOr(b.error, 1u);
       tok = 0;
     }

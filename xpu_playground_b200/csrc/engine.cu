@@ -860,6 +860,7 @@ class Qwen3Engine {
     bd_.tp = tp_;
     bd_.rank = rank_;
     bd_.v_offset = d_.v_offset;
+    bd_.tokens = s.vocab_size;
     bd_.layers = s.num_hidden_layers;
     bd_.max_seq = max_seq_;
     bd_.nchunks = pos_chunks(max_seq_);
