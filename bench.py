@@ -300,7 +300,7 @@ def batch_extra(torch, device, shape, context: int, batch: int, steps: int, warm
     ms = e0.elapsed_time(e1) / steps
     _, pos1, err = eng.batch_state(batch)
     if err:
-        raise SystemExit(f"batched decode error word {err}")
+        raise RuntimeError(f"batched decode error word {err}")
     if world > 1:
         import torch.distributed as dist
         t = torch.tensor([ms], device=device)
@@ -538,9 +538,12 @@ def run_ours(args) -> None:
         extra["qwen3_0p6b_decode"] = small_extra(torch, device, warmup=max(W, 3))
     if args.batch:
         eng.synchronize()
-        extra["batch_decode"] = batch_extra(torch, device, shape, args.context, args.batch,
-                                            steps=min(K, 64), warmup=max(W, 3), rank=rank, world=world,
-                                            group=tp_group)
+        try:
+            extra["batch_decode"] = batch_extra(torch, device, shape, args.context, args.batch,
+                                                steps=min(K, 64), warmup=max(W, 3), rank=rank, world=world,
+                                                group=tp_group)
+        except Exception as e:  # recorded in the line; the headline stands on its own
+            extra["batch_decode"] = {"error": f"{type(e).__name__}: {e}"[:300]}
     if not args.no_gemv:
         eng.synchronize()
         extra.update(gemv_extra(torch, device, rank, world))

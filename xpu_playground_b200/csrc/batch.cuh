@@ -72,7 +72,9 @@ struct BatchDims {
 // their K. Each rank's o_proj / down GEMM writes its FP32 partial Y_r[16][H]
 // into its exchange region; once every rank has published the exchange's
 // epoch, each rank sums the ranks' partials in rank order and applies the
-// residual (x = bf16(x + bf16(sum))) and the per-tile sums of x^2 itself. The
+// residual (x = bf16(x + bf16(sum))) and the per-tile sums of x^2 itself
+// (the partial GEMM's last CTA publishes the epoch, the exchange kernel
+// starts early under programmatic dependent launch and waits on it). The
 // lm_head candidates of every sequence meet the same way. Exchange k (1-based)
 // of a step has epoch *xepoch + k; a kernel after the step's argmax adds
 // 2 layers + 1, so epochs only grow. Region layout behind the dense prefill
@@ -121,6 +123,7 @@ struct BatchBuffers {
   unsigned long long *xflag[kMaxTp];  // [2] published epochs
   LmSlot *xlm[kMaxTp];                // [kMaxTp][16] lm_head candidates (slot [rank][sequence])
   unsigned long long *xepoch;         // this rank's exchanges before the current step
+  unsigned *xdone;                    // CTAs of the running partial GEMM that have finished
 };
 
 constexpr uint32_t kBatchTraceSlots = 512;

@@ -95,6 +95,7 @@ struct BGemm {
   BatchBuffers b;
   bf16 *out;                    // residual x (kEpiResid), h (kEpiGateUp) or raw qkv (kEpiQkv)
   float *part;                  // kEpiPart: this rank's FP32 partial [16][rows] (tensor parallel)
+  uint32_t xwhich, xk;          // kEpiPart: exchange slot (0 o_proj, 1 down) and number in the step
   const bf16 *norm_w;           // normalising GEMMs: the RMSNorm weight of the operand
 };
 
@@ -302,6 +303,21 @@ __device__ inline void norm_stage(uint8_t *xs, uint32_t kb, uint32_t e, uint32_t
             make_uint4(norm_word(x.x, wq.x, r), norm_word(x.y, wq.y, r), norm_word(x.z, wq.z, r),
                        norm_word(x.w, wq.w, r));
       }
+}
+
+// Tensor parallel partial GEMM: the last CTA to finish publishes exchange
+// xk's epoch to the peers, once every CTA's partial sums are written (each
+// CTA fences its writes before counting itself done).
+__device__ __forceinline__ void part_published(const BGemm &p) {
+  const unsigned prev = atomicAdd(p.b.xdone, 1u);
+  if (prev == gridDim.x - 1) {
+    __threadfence();
+    *p.b.xdone = 0;  // for the next partial GEMM, which runs after this one
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p.b.xflag[p.d.rank] + p.xwhich),
+                 "l"(*p.b.xepoch + p.xk)
+                 : "memory");
+  }
 }
 
 template <int EPI, bool NORM>
@@ -553,6 +569,7 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
       kb = end;
     }
   }
+  if (EPI == kEpiPart) __threadfence();  // this thread's partial sums, before the CTA counts itself done
   __syncthreads();
   if (threadIdx.x == 0) {
     // Copies still in flight after a failure: wait (bounded) for each issued
@@ -560,6 +577,7 @@ k_bgemm(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUten
     for (uint32_t i = consumed; i < issued_count; ++i)
       if (!mbar_wait(&full[i % kRing], (i / kRing) & 1)) break;
     if (failed) atomicOr(p.b.error, kErrPipelineTimeout);
+    if (EPI == kEpiPart) part_published(p);
   }
   tc_fence_before();
   __syncthreads();
@@ -1469,21 +1487,20 @@ __device__ bool bx_wait(const unsigned long long *const *base, uint32_t offset, 
   return true;
 }
 
-// Exchange k of the step (which: 0 o_proj, 1 down) is published: this rank's
-// partial (written by the GEMM before this kernel) is visible to the peers.
-__global__ void k_bsignal(BatchDims d, BatchBuffers b, uint32_t which, uint32_t k) {
-  __threadfence_system();
-  bx_st_release(b.xflag[d.rank] + which, *b.xepoch + k);
-}
-
 // Tile blockIdx.x of H (128 rows, one thread each): once every rank's
 // partial of exchange k is published, x = bf16(x + bf16(partials summed in
 // rank order)) and the tile's sums of x^2 per sequence, as the residual
 // epilogue leaves them.
+// Launched with programmatic dependent launch: it lets the next GEMM start
+// (and prefetch its weights) at once, and needs no wait on the partial GEMM
+// before it - this rank's own flag is among those it waits for, and that
+// flag is published only when the partial GEMM, and so everything before
+// it, has completed.
 __global__ void __launch_bounds__(kTileM) k_bxchg(BatchDims d, BatchBuffers b, uint32_t which, uint32_t k) {
   __shared__ int ok;
   __shared__ float part_ssq[4][kSeqN];
   const uint32_t t = blockIdx.x, r = threadIdx.x, row = t * kTileM + r, lane = r & 31, quarter = r >> 5;
+  grid_dep_launch();
   if (r == 0) {
     ok = bx_wait(b.xflag, which, d.tp, *b.xepoch + k) ? 1 : 0;
     if (!ok) atomicOr(b.error, 4u);
@@ -1749,17 +1766,16 @@ cudaError_t record_batch_step(const BatchDims &d0, const BatchBuffers &b, const 
   };
   const uint32_t G = d.QH / d.KVH;
   if (d.tp > 1 && (prefill || d.H % kTileM)) return cudaErrorInvalidValue;
-  // Tensor parallel o_proj / down: the partial GEMM into this rank's region,
-  // the epoch published, then every rank's partials applied to x.
+  // Tensor parallel o_proj / down: the partial GEMM into this rank's region
+  // (its last CTA publishes the epoch), then every rank's partials applied to x.
   auto exchange = [&](uint32_t which, uint32_t k, const bf16 *W, uint32_t K, const bf16 *X) -> cudaError_t {
     BGemm pp{};
     pp.part = b.xpart[d.rank] + static_cast<size_t>(which) * kMaxBatch * d.H;
-    cudaError_t e = launch_bgemm<kEpiPart>(W, d.H, K, X, at(pp), s);
+    pp.xwhich = which;
+    pp.xk = k;
+    const cudaError_t e = launch_bgemm<kEpiPart>(W, d.H, K, X, at(pp), s);
     if (e != cudaSuccess) return e;
-    k_bsignal<<<1, 1, 0, s>>>(next(), b, which, k);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    k_bxchg<<<d.H / kTileM, kTileM, 0, s>>>(next(), b, which, k);
-    return cudaGetLastError();
+    return launch_pdl(k_bxchg, dim3(d.H / kTileM), dim3(kTileM), 0, s, next(), b, which, k);
   };
 #define XPU_TRY(expr)                        \
   do {                                       \

@@ -792,10 +792,10 @@ class Qwen3Engine {
   }
 
   // embed + norm, 5 per layer (qkv, attention, o_proj, gate/up, down), lm_head,
-  // argmax; tensor parallel: + 2 per row-parallel GEMM (publish, exchange) and
-  // the epoch update
+  // argmax; tensor parallel: + 1 exchange per row-parallel GEMM and the epoch
+  // update
   uint32_t batch_kernels_per_step() const {
-    return tp_ > 1 ? 9 * shape_.num_hidden_layers + 4 : 5 * shape_.num_hidden_layers + 3;
+    return tp_ > 1 ? 7 * shape_.num_hidden_layers + 4 : 5 * shape_.num_hidden_layers + 3;
   }
 
   // Bytes one batched step of n sequences must move: the weights once, plus
@@ -906,6 +906,7 @@ class Qwen3Engine {
         b.xpart[q] = reinterpret_cast<float *>(base + kBatchPartOffset);
       }
       b.xepoch = dev_zeros<unsigned long long>(1);
+      b.xdone = dev_zeros<unsigned>(1);
     }
     const char *trace_env = std::getenv("XPU_BATCH_TRACE");
     if (trace_env && trace_env[0] == '1') {
