@@ -1507,17 +1507,29 @@ __global__ void __launch_bounds__(kTileM) k_bxchg(BatchDims d, BatchBuffers b, u
   }
   __syncthreads();
   if (!ok) return;
-  const size_t slot = static_cast<size_t>(which) * kMaxBatch * d.H;
-  float sq[kSeqN];
+  const size_t slot = static_cast<size_t>(which) * kMaxBatch * d.H + row;
+  // Every sequence's value of one rank is requested before any is used (one
+  // NVLink round trip per rank, not one per sequence), the ranks summed in
+  // order, and only then is x read and written.
+  float v[kSeqN], sq[kSeqN];
+#pragma unroll
+  for (uint32_t s = 0; s < kSeqN; ++s) v[s] = s < d.batch ? __ldcg(b.xpart[0] + slot + s * d.H) : 0.f;
+  for (uint32_t q = 1; q < d.tp; ++q) {
+    float w[kSeqN];
+#pragma unroll
+    for (uint32_t s = 0; s < kSeqN; ++s) w[s] = s < d.batch ? __ldcg(b.xpart[q] + slot + s * d.H) : 0.f;
+#pragma unroll
+    for (uint32_t s = 0; s < kSeqN; ++s) v[s] = __fadd_rn(v[s], w[s]);
+  }
+  float xr[kSeqN];
+#pragma unroll
+  for (uint32_t s = 0; s < kSeqN; ++s) xr[s] = s < d.batch ? bfv(b.x, static_cast<size_t>(s) * d.H + row) : 0.f;
 #pragma unroll
   for (uint32_t s = 0; s < kSeqN; ++s) {
     sq[s] = 0.f;
     if (s < d.batch) {
-      const size_t i = static_cast<size_t>(s) * d.H + row;
-      float v = __ldcg(b.xpart[0] + slot + i);
-      for (uint32_t q = 1; q < d.tp; ++q) v = __fadd_rn(v, __ldcg(b.xpart[q] + slot + i));
-      const float xn = round_bf16(__fadd_rn(bfv(b.x, i), round_bf16(v)));
-      putv(b.x, i, xn);
+      const float xn = round_bf16(__fadd_rn(xr[s], round_bf16(v[s])));
+      putv(b.x, static_cast<size_t>(s) * d.H + row, xn);
       sq[s] = __fmul_rn(xn, xn);
     }
   }
